@@ -1,0 +1,384 @@
+#!/usr/bin/env python
+"""Decode benchmark for the Talos B200 path.
+
+Workload: Mistral-7B-shaped Llama (d 4096, 32 layers, 32/8 heads, ff 14336,
+vocab 32000, RoPE theta 1e6), random N(0, 0.02) weights from seed 1, Q4_0 with
+output.weight in Q6_K; a 128-token uniform-random prompt (prefill, untimed),
+then batch-1 greedy decode. One step = one decoded token.
+
+  value : K greedy tokens decoded on the GPU with the argmax fed back on the
+          device (talos_generate_greedy: one CUDA graph replay per token), timed
+          with CUDA events on the context's stream. Weights (4.03 GB/token) are
+          far larger than L2, so every step streams them from HBM.
+  e2e   : the same decode through the public per-token call talos_forward with
+          host buffers: token/pos host->device, logits device->host and the argmax
+          on the host every step (the reference's decode loop, src/main.rs:97-113).
+  roofline: the dominant kernel (fused RMSNorm + gate/up Q4_0 matvec + SwiGLU),
+          timed per launch with CUDA events from eagerly launched steps.
+  cpu_baseline: the CPU oracle (a C restatement of the reference's rayon CPU
+          forward) on this host's cores, a bounded sample of tokens.
+
+--impl reference times that CPU path alone, per token, on the same workload.
+Multi-GPU (torchrun, N > 1): replicas, one independent sequence per GPU (weak
+scaling); value = all ranks' tokens / max over ranks of the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+# Algorithmic bytes of one decode token (7B shape): every matvec weight once
+# (6,979,321,856 Q4_0 elements x 18/32 B), the Q6_K output (131,072,000 x 210/256),
+# 65 f32 norm vectors, one Q4_0 embedding row.
+W_BYTES_7B = 6979321856 * 18 // 32 + 131072000 * 210 // 256 + 65 * 4096 * 4 + 4096 // 32 * 18
+KV_BYTES_PER_POS = 2 * 32 * 1024 * 4  # K and V rows read per cached position (f32)
+GATEUP_BYTES = 2 * 14336 * 4096 * 18 // 32 + 4096 * 4 * 2 + 14336 * 4  # weights + x + norm + out
+PROMPT_LEN = 128
+MODEL_SEED = 1
+PROMPT_SEED = 1
+
+
+def env_int(k, d):
+    try:
+        return int(os.environ.get(k, d))
+    except ValueError:
+        return d
+
+
+def argmax_last(v: np.ndarray) -> int:
+    """sample::argmax (src/sample.rs:7-14): last maximal element on ties."""
+    return int(v.size - 1 - np.argmax(v[::-1]))
+
+
+def model_path() -> str:
+    return os.environ.get("TALOS_BENCH_MODEL", f"/dev/shm/talos_bench_m7b_q4_0_s{MODEL_SEED}.gguf")
+
+
+def ensure_model(path: str, threads: int | None = None) -> float:
+    from talos_b200 import gguf, synth
+
+    if os.path.exists(path) and os.path.getsize(path) > 4_000_000_000:
+        return 0.0
+    t = time.time()
+    synth.write_llama(path + ".tmp", synth.MISTRAL_7B, MODEL_SEED, wtype=gguf.Q4_0, out_type=gguf.Q6_K,
+                      threads=threads)
+    os.replace(path + ".tmp", path)
+    return time.time() - t
+
+
+class ClockSampler:
+    """SM clock and throttle reasons from NVML while the timed region runs."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock"}
+
+    def __init__(self, device: int):
+        self.samples, self.reasons, self.ok = [], set(), False
+        self.max_mhz = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = int(vis.split(",")[device]) if vis else device
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            pass
+        self._stop = threading.Event()
+        self._th = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self.ok:
+            self._th = threading.Thread(target=self._run, daemon=True)
+            self._th.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._th:
+            self._th.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """DRAM bytes per launch of the gate/up kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "gateup_q4_0_m7b.md")
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+def cpu_decode_sample(path: str, budget_s: float, max_tokens: int):
+    """Time the oracle's CPU forward (all host threads) on decode tokens of the
+    same model; returns (tok/s, tokens, threads, seconds)."""
+    import oracle
+
+    oracle.build()
+    threads = max(1, len(os.sched_getaffinity(0)))
+    oracle.set_threads(threads)
+    m = oracle.Model(path=path)
+    from talos_b200 import synth
+
+    toks = synth.token_ids(PROMPT_SEED, max_tokens, m.cfg.vocab_size)
+    m.forward(toks[0], 0)  # warm the page cache / thread pool (untimed)
+    m.reset()
+    n, t0 = 0, time.perf_counter()
+    while n < max_tokens:
+        m.forward(toks[n], n)
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    m.close()
+    return n / dt, n, threads, dt
+
+
+def run_reference(args):
+    """--impl reference: the CPU restatement of the reference's forward on this
+    host's cores, each step one decode token of the same workload."""
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return 0
+    from talos_b200 import synth
+
+    ensure_model(model_path())
+    import oracle
+
+    oracle.build()
+    threads = max(1, len(os.sched_getaffinity(0)))
+    oracle.set_threads(threads)
+    m = oracle.Model(path=model_path())
+    toks = synth.token_ids(PROMPT_SEED, PROMPT_LEN, m.cfg.vocab_size)
+    # A bounded workload sample: the prompt is not replayed; decode steps start at
+    # position 0 (the CPU cost of a token is dominated by its 4.03 GB of weights).
+    budget = float(os.environ.get("TALOS_REF_BUDGET_S", "150"))
+    warm = min(args.warmup, 1)
+    pos = 0
+    for i in range(warm):
+        m.forward(toks[i], pos)
+        pos += 1
+    n, t0 = 0, time.perf_counter()
+    tok = toks[warm % len(toks)]
+    while n < args.steps:
+        lg = m.forward(tok, pos)
+        tok = argmax_last(lg)
+        pos += 1
+        n += 1
+        if time.perf_counter() - t0 > budget:
+            break
+    dt = time.perf_counter() - t0
+    v = n / dt
+    sample = (f"{n} greedy decode tokens (positions {warm}..{warm + n - 1}) of the 7B-shape Q4_0/Q6_K model, "
+              f"{threads} threads; steps capped at {budget:.0f} s of CPU time")
+    line = {
+        "metric": "decode tok/s (batch 1, 7B-shape Q4_0)", "value": v, "unit": "tok/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": n, "steps_requested": args.steps, "warmup": warm,
+        "ms_per_step": 1000 * dt / max(n, 1), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q4_0/f32", "data": "synthetic",
+        "config": {"workload": "mistral-7b-shape Q4_0 (+Q6_K output), batch-1 greedy decode",
+                   "global_batch": 1, "prompt": PROMPT_LEN},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="talos_b200", choices=["talos_b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+
+    rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+    import torch
+
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+
+    from talos_b200 import Model, build, synth
+
+    build.build()
+    path = model_path()
+    gen_s = 0.0
+    if local == 0:
+        gen_s = ensure_model(path)
+    if dist:
+        dist.barrier()
+
+    K, W = args.steps, args.warmup
+    t_load = time.time()
+    model = Model.load(path, device=local, max_ctx=PROMPT_LEN + 2 * (K + W) + 16)
+    load_s = time.time() - t_load
+    ctx = model.ctx
+    stream = torch.cuda.ExternalStream(ctx.stream(), device=torch.device("cuda", local))
+    vocab = model.cfg.vocab_size
+    prompt = synth.token_ids(PROMPT_SEED, PROMPT_LEN, vocab)
+
+    # ---------------- device-resident greedy decode (value)
+    last = model.prefill(prompt, 0)
+    tok = argmax_last(last)
+    pos = PROMPT_LEN
+    out = model.generate_greedy(tok, pos, W)
+    tok, pos = int(out[-1]), pos + W
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with clocks:
+        e0.record(stream)
+        out = model.generate_greedy(tok, pos, K)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist:
+        dist.barrier()
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * K / (ms / 1000.0)
+    tok, pos = int(out[-1]), pos + K
+    kv_avg_pos = PROMPT_LEN + W + K / 2
+
+    # ---------------- end to end through talos_forward with host buffers (e2e)
+    logits = np.empty(vocab, np.float32)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(K):
+        ctx.forward(tok, pos, logits)
+        tok = argmax_last(logits)
+        pos += 1
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = world * K / e2e_s
+
+    # ---------------- per-kernel times of eagerly launched steps (roofline)
+    n_prof = 4
+    tot_ms, tot_n = None, None
+    for i in range(n_prof):
+        ms_k, n_k = ctx.profile_step(tok, PROMPT_LEN + W + i)
+        if tot_ms is None:
+            tot_ms, tot_n = ms_k, n_k
+        else:
+            for k in tot_ms:
+                tot_ms[k] += ms_k[k]
+                tot_n[k] += n_k[k]
+    gu_ms = tot_ms["gateup"] / max(tot_n["gateup"], 1)
+    peak, peak_kind = measured_peaks()
+    achieved = GATEUP_BYTES / (gu_ms / 1000.0) / 1e9
+    traffic = profiled_traffic()
+    step_ms = sum(tot_ms.values()) / n_prof
+    breakdown = {k: {"ms_per_step": tot_ms[k] / n_prof, "launches_per_step": tot_n[k] // n_prof}
+                 for k in tot_ms}
+    launches = sum(tot_n.values()) // n_prof + 1  # + the greedy-advance kernel
+
+    # ---------------- CPU baseline (rank 0 at N=1 only)
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        v, n, thr, dt = cpu_decode_sample(path, budget_s=20.0, max_tokens=12)
+        cpu = {"value": v, "unit": "tok/s", "cores": thr, "kind": "port",
+               "sample": f"{n} decode tokens (positions 0..{n - 1}) of the same 7B-shape model through the "
+                         f"oracle's CPU forward, {dt:.1f} s"}
+
+    tok_bytes = W_BYTES_7B + KV_BYTES_PER_POS * kv_avg_pos
+    ms_step = ms / K
+    line = {
+        "metric": "decode tok/s (batch 1, 7B-shape Q4_0)",
+        "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "q4_0 weights, f32 activations/KV", "data": "synthetic",
+        "config": {"workload": "mistral-7b-shape Q4_0 (+Q6_K output), 128-token prompt then batch-1 greedy decode",
+                   "model": "llama d4096 L32 h32/8 ff14336 V32000", "global_batch": world, "seq_len": PROMPT_LEN + W + K,
+                   "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+                   "l2": "inputs larger than L2 (4.03 GB of weights per step)"},
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 24, "d2h_bytes_per_step": vocab * 4 + 24},
+        "roofline": {"bound": "hbm", "kernel": "gateup (RMSNorm + gate/up Q4_0 matvec + SwiGLU)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "traffic": traffic, "bytes_per_launch": GATEUP_BYTES,
+                     "ms_per_launch": gu_ms},
+        "token_roofline": {"bytes_per_token": tok_bytes, "achieved_gbs": tok_bytes / (ms_step / 1000) / 1e9,
+                           "frac": tok_bytes / (ms_step / 1000) / 1e9 / peak, "peak_kind": peak_kind},
+        "kernels": breakdown, "eager_step_ms": step_ms,
+        "gpu_launches": launches * K,
+        "clocks": clocks.summary(),
+        "cpu_baseline": cpu,
+        "setup": {"model_gen_s": gen_s, "load_s": load_s},
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    model.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

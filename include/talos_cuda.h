@@ -1,0 +1,238 @@
+/*
+ * talos_cuda.h -- C ABI of the B200 (sm_100a) decode path for Talos.
+ *
+ * This library replaces the Apple-Metal twin of Talos's CPU forward pass
+ * (Tsuskov/talos, Rust). Each entry point names the reference interface it
+ * stands in for. The Rust side binds these symbols from a `cuda` cargo feature
+ * that mirrors the existing `metal` feature (Cargo.toml:28-31); the binding
+ * a maintainer adds is shown in INTEGRATION.md.
+ *
+ * Conventions
+ *  - Every call returns a talos_status; talos_last_error() gives the message of
+ *    the last failure on the calling thread.
+ *  - Host pointers everywhere unless a name ends in `_dev`; output buffers are
+ *    owned by the caller.
+ *  - One context drives one GPU. A context is not thread-safe: use it from one
+ *    thread at a time (the reference's backend is a thread_local context,
+ *    src/math/metal/mod.rs:25-29).
+ *  - Calls are synchronous unless documented otherwise (the reference commits
+ *    and waits once per token, src/math/metal/mod.rs:511-513).
+ *  - Weights are copied to the GPU once, keyed by tensor name
+ *    (src/math/metal/mod.rs:37-41,63-72), and repacked there into the
+ *    GPU-friendly layouts the kernels read; the GGUF bytes are not kept.
+ *  - ggml type tags: F32 = 0, Q4_0 = 2, Q8_0 = 8, Q6_K = 14
+ *    (src/gguf/dtype.rs:31-41).
+ */
+#ifndef TALOS_CUDA_H
+#define TALOS_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum talos_status {
+    TALOS_OK = 0,
+    TALOS_ERR_INVALID_ARG = 1, /* bad pointer, size, name, type or shape */
+    TALOS_ERR_OOM = 2,         /* device or pinned-host allocation failed */
+    TALOS_ERR_CUDA = 3,        /* a CUDA runtime call failed */
+    TALOS_ERR_NCCL = 4,        /* an NCCL call failed */
+    TALOS_ERR_TIMEOUT = 5,     /* a bounded wait ran out */
+    TALOS_ERR_OOB = 6,         /* a device-side bounds check fired */
+    TALOS_ERR_STATE = 7,       /* call not valid in the current state (e.g. weights missing) */
+    TALOS_ERR_UNSUPPORTED = 8  /* ggml type or shape this build does not handle */
+} talos_status;
+
+enum { TALOS_F32 = 0, TALOS_Q4_0 = 2, TALOS_Q8_0 = 8, TALOS_Q6_K = 14 };
+
+/* Model hyper-parameters; field for field `Config` (src/model/config.rs:14-25). */
+typedef struct talos_cfg {
+    uint32_t n_layer;
+    uint32_t n_head;
+    uint32_t n_head_kv;
+    uint32_t n_embd;
+    uint32_t n_ff;
+    uint32_t context_length;
+    uint32_t vocab_size;
+    uint32_t rope_dim;
+    float rms_eps;
+    float rope_freq_base;
+} talos_cfg;
+
+typedef struct talos_ctx talos_ctx;
+/* A packed weight on the device, for the single-matvec entry points. */
+typedef struct talos_weight talos_weight;
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* talos_last_error(void);
+
+/* Number of CUDA devices visible (0 when there is no GPU). */
+talos_status talos_device_count(int* out);
+
+/* ------------------------------------------------------------ context */
+
+/*
+ * Create a decode context on CUDA device `device`. Replaces the lazily built
+ * Metal context (src/math/metal/mod.rs:43-61) and `GpuKv::new`
+ * (src/math/metal/mod.rs:272-281). Checks n_head_kv > 0 and
+ * n_head % n_head_kv == 0 like Model::from_gguf (src/model/llama.rs:43-51).
+ * The KV cache holds cfg->context_length positions.
+ */
+talos_status talos_ctx_create(const talos_cfg* cfg, int device, talos_ctx** out);
+
+/*
+ * Tensor-parallel context: rank `tp_rank` of `tp_size` ranks, one process per
+ * GPU, joined through the 128-byte NCCL unique id that rank 0 made with
+ * talos_nccl_unique_id() and shared out of band. No reference counterpart (the
+ * reference is single-device); it follows the same rules as talos_ctx_create.
+ */
+talos_status talos_ctx_create_tp(const talos_cfg* cfg, int device, int tp_size, int tp_rank,
+                                 const uint8_t* nccl_unique_id, talos_ctx** out);
+talos_status talos_nccl_unique_id(uint8_t out[128]);
+
+talos_status talos_ctx_destroy(talos_ctx* ctx);
+
+/*
+ * Copy one GGUF tensor to the GPU under its GGUF name and repack it for the
+ * kernels. Replaces `resident_weight` (src/math/metal/mod.rs:63-72) fed from
+ * `QTensor::gpu_parts` (src/model/weights.rs:66-69). `bytes` are the raw
+ * GGUF data (`len` bytes) of a row-major [rows, cols] matrix of `ggml_type`;
+ * 1-D norm weights pass rows = 1. Names and shapes must be those
+ * `Weights::from_gguf` binds (src/model/weights.rs:91-114). Uploading a name
+ * again replaces its data. Under tensor parallelism each rank passes the FULL
+ * tensor and keeps its own shard.
+ */
+talos_status talos_weight_upload(talos_ctx* ctx, const char* name, const void* bytes, size_t len,
+                                 int ggml_type, size_t rows, size_t cols);
+
+/* Bytes of device memory the context holds (weights + KV cache + work areas). */
+talos_status talos_ctx_device_bytes(talos_ctx* ctx, size_t* out);
+
+/*
+ * The CUDA stream (cudaStream_t, as void*) every call on `ctx` runs on, so a
+ * caller can time steps with CUDA events recorded on it. No reference
+ * counterpart (the Metal path exposes its command queue only internally,
+ * src/math/metal/mod.rs:31-34).
+ */
+talos_status talos_ctx_stream(talos_ctx* ctx, void** stream_out);
+
+/*
+ * Shrink the KV cache to `max_ctx` positions (never above the model's own
+ * context_length) and empty it. Model::cap_context (src/model/llama.rs:69-81).
+ */
+talos_status talos_cap_context(talos_ctx* ctx, size_t max_ctx);
+
+/*
+ * Start a fresh sequence. Model::reset (src/model/llama.rs:236-238). The
+ * device KV cache is indexed by position, so this only forgets the cached
+ * length; positions are overwritten as they are decoded.
+ */
+talos_status talos_kv_reset(talos_ctx* ctx);
+
+/* ------------------------------------------------------------ decode */
+
+/*
+ * One decode step for `token` at position `pos`; writes vocab_size logits to
+ * `logits_out` (host). Model::forward_gpu (src/model/llama.rs:188-195) ->
+ * math::metal::forward (src/math/metal/mod.rs:351-359). Unlike the Metal path
+ * the embedding row is looked up on the GPU, so the call takes the token id.
+ * Requires 0 <= pos < context length and token < vocab_size. The whole step is
+ * one CUDA graph replay.
+ */
+talos_status talos_forward(talos_ctx* ctx, uint32_t token, size_t pos, float* logits_out);
+
+/*
+ * Like talos_forward but returns the final-norm hidden state (n_embd floats).
+ * Model::forward_hidden_gpu (src/model/llama.rs:199-206) ->
+ * math::metal::forward_hidden (src/math/metal/mod.rs:363-366).
+ */
+talos_status talos_forward_hidden(talos_ctx* ctx, uint32_t token, size_t pos, float* hidden_out);
+
+/*
+ * Greedy decode entirely on the GPU: feeds `token` at `pos`, then the argmax of
+ * each step's logits at pos+1, pos+2, ... for `n` steps, and writes the n chosen
+ * tokens to `tokens_out` (host). The argmax follows sample::argmax
+ * (src/sample.rs:7-14): total order, last maximal index on ties. This is the
+ * decode loop of src/main.rs:97-113 / benches/tokps.rs:33-41 with the logits
+ * never leaving the GPU.
+ */
+talos_status talos_generate_greedy(talos_ctx* ctx, uint32_t token, size_t pos, size_t n,
+                                   uint32_t* tokens_out);
+
+/*
+ * Feed `n` prompt tokens at positions pos0 .. pos0+n-1 (the prefill loop of
+ * src/main.rs:88-95) and write the logits after the last one to `last_logits`
+ * (host, may be NULL).
+ */
+talos_status talos_prefill(talos_ctx* ctx, const uint32_t* tokens, size_t n, size_t pos0,
+                           float* last_logits);
+
+/*
+ * Run one decode step (as talos_forward, logits stay on the GPU) launching its
+ * kernels one by one with CUDA events between them, and add each kernel's
+ * device time in milliseconds into kernel_ms[kind] and its launch count into
+ * launches[kind] (either may be NULL), kind = talos_kernel_kind. For
+ * benchmarks: the per-kernel durations of the graph the step normally replays.
+ * No reference counterpart.
+ */
+enum talos_kernel_kind {
+    TALOS_K_EMBED = 0,  /* token embedding row dequant */
+    TALOS_K_QKV = 1,    /* RMSNorm + q/k/v matvec + RoPE + KV append */
+    TALOS_K_ATTN = 2,   /* split-position GQA attention */
+    TALOS_K_OPROJ = 3,  /* attn_output matvec + residual */
+    TALOS_K_GATEUP = 4, /* RMSNorm + gate/up matvec + SwiGLU */
+    TALOS_K_DOWN = 5,   /* ffn_down matvec + residual */
+    TALOS_K_OUTPUT = 6, /* final RMSNorm + output matvec (+ argmax) */
+    TALOS_K_COUNT = 7
+};
+talos_status talos_profile_step(talos_ctx* ctx, uint32_t token, size_t pos, double* kernel_ms,
+                                uint32_t* launches);
+
+/* ------------------------------------------------------------ kernels */
+
+/*
+ * Dequantize n_elems values of `ggml_type` from raw GGUF `bytes` (host) into
+ * `out` (host) on the GPU, bit-exact with GgmlType::dequantize
+ * (src/gguf/dtype.rs:64-121). Test hook for the bit-exact contract.
+ */
+talos_status talos_dequant(int ggml_type, const void* bytes, size_t n_elems, float* out);
+
+/*
+ * One fused dequant-matvec y = W x on device `device`, with W uploaded for this
+ * call only. math::metal::matvec_f32 / matvec_quant
+ * (src/math/metal/mod.rs:195-225). x: cols floats, y: rows floats (host).
+ */
+talos_status talos_matvec(int device, int ggml_type, const void* bytes, size_t len, size_t rows,
+                          size_t cols, const float* x, float* y);
+
+/*
+ * Matvec against a weight kept on the GPU under `name` in `ctx`: uploaded on
+ * first use and reused while the byte length stays the same, even if the bytes
+ * differ. math::metal::matvec_f32_resident / matvec_quant_resident
+ * (src/math/metal/mod.rs:227-253), with the cache rule of
+ * src/math/metal/mod.rs:63-72.
+ */
+talos_status talos_matvec_resident(talos_ctx* ctx, const char* name, int ggml_type,
+                                   const void* bytes, size_t len, size_t rows, size_t cols,
+                                   const float* x, float* y);
+
+/*
+ * Device-level matvec for benchmarks: pack a weight onto device `device` once,
+ * then run y_dev = W x_dev on a CUDA stream (cudaStream_t passed as void*,
+ * NULL = legacy default stream) without synchronizing. x_dev/y_dev are device
+ * pointers of cols / rows floats. No reference counterpart; it exposes the
+ * kernel that QTensor::matvec (src/model/weights.rs:47-55) becomes.
+ */
+talos_status talos_weight_create(int device, int ggml_type, const void* bytes, size_t len,
+                                 size_t rows, size_t cols, talos_weight** out);
+talos_status talos_weight_destroy(talos_weight* w);
+talos_status talos_weight_packed_bytes(const talos_weight* w, size_t* out);
+talos_status talos_matvec_dev(const talos_weight* w, const float* x_dev, float* y_dev,
+                              void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

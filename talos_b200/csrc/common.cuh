@@ -1,0 +1,120 @@
+// common.cuh -- device-side types and helpers shared by the Talos sm_100a kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace talos {
+
+enum GType : int { GT_F32 = 0, GT_Q4_0 = 2, GT_Q8_0 = 8, GT_Q6_K = 14 };
+
+// A weight matrix after repacking on the device. Row counts are padded to a
+// multiple of 16 (two 8-row groups); pad rows hold zeros.
+//
+//  F32 : p0 = float [rows_pad][cols]
+//  Q8_0: p0 = int8  [rows_pad][nb*32] (quants of each block, row-contiguous)
+//        p1 = half  [rows_pad][nb]    (block scales)
+//  Q4_0: p0 = uint4 [rows_pad/8][nq][32 lanes]  (one 16-byte word set per lane and
+//        block-quad; see pack_q4_0 in kernels.cu for the nibble order)
+//        p1 = uint2 [rows_pad/8][nq][8 rows]    (4 block scales per row, f16)
+//  Q6_K: p0 = uint32 [rows_pad][nsb][32] (ql bytes l, l+32, 64+l, 96+l per lane)
+//        p1 = uint16 [rows_pad][nsb][32] (qh bytes l, 32+l per lane)
+//        p2 = int8   [rows_pad][nsb][16] (sub-block scales)
+//        p3 = half   [rows_pad][nsb]     (super-block scale d)
+struct PackedW {
+    int type;
+    int rows, cols;   // logical shape [rows, cols]
+    int rows_pad;     // multiple of 16
+    int nk;           // F32: cols; Q8_0: blocks; Q4_0: block quads; Q6_K: super-blocks
+    const void* p0;
+    const void* p1;
+    const void* p2;
+    const void* p3;
+};
+
+// Device-resident step parameters, read by every kernel of a captured graph so
+// one graph serves every token.
+struct StepParams {
+    uint32_t token;
+    uint32_t pos;
+    uint32_t n_gen;      // tokens written to gen_tokens so far (greedy loop)
+    uint32_t error;      // first device-side error code (0 = none)
+    unsigned long long argmax_key;  // packed (total-order key << 32) | index
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Streaming 16-byte load that does not allocate in L1 (weights are read once).
+__device__ __forceinline__ uint4 ldg_stream_u4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint2 ldg_stream_u2(const void* p) {
+    uint2 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint32_t ldg_stream_u1(const void* p) {
+    uint32_t r;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+    return r;
+}
+
+template <int LUT>
+__device__ __forceinline__ uint32_t lop3(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, %4;" : "=r"(d) : "r"(a), "r"(b), "r"(c), "n"(LUT));
+    return d;
+}
+
+// Four 4-bit quants in bit positions {0-3, 16-19} -> f16x2 (q - 8), exact.
+__device__ __forceinline__ uint32_t q4_lo_f16x2(uint32_t w) {
+    uint32_t t = lop3<0xEA>(w, 0x000F000Fu, 0x64006400u);  // 1024 + q
+    uint32_t r;
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(r) : "r"(t), "r"(0x64086408u));  // - 1032
+    return r;
+}
+// Quants in bit positions {4-7, 20-23} -> f16x2 (q - 8), exact.
+__device__ __forceinline__ uint32_t q4_hi_f16x2(uint32_t w) {
+    uint32_t t = lop3<0xEA>(w, 0x00F000F0u, 0x64006400u);  // 1024 + 16 q
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(t), "r"(0x2C002C00u), "r"(0xD480D480u));  // /16 - 72
+    return r;
+}
+
+// D(16x8, f32) += A(16x16, f16, row) * B(16x8, f16, col)
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_half2(half lo, half hi) {
+    return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
+
+// Order-preserving map of f32 onto u32 following Rust's f32::total_cmp.
+__device__ __forceinline__ uint32_t total_order_key(float f) {
+    int32_t b = __float_as_int(f);
+    b ^= (int32_t)(((uint32_t)(b >> 31)) >> 1);
+    return (uint32_t)b ^ 0x80000000u;
+}
+
+}  // namespace talos

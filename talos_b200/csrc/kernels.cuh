@@ -1,0 +1,89 @@
+// kernels.cuh -- launch interface of the Talos sm_100a kernels (kernels.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace talos {
+
+// ---------------------------------------------------------------- packing
+
+// Bytes of device memory a packed weight needs, split per array.
+struct PackSizes {
+    size_t b0, b1, b2, b3;
+    int rows_pad, nk;
+};
+bool pack_sizes(int type, int rows, int cols, PackSizes* out);
+// Repack raw GGUF bytes (device) of a [rows, cols] weight into `w` (arrays
+// already allocated with pack_sizes).
+cudaError_t launch_pack(const uint8_t* raw, const PackedW& w, cudaStream_t s);
+
+// Bit-exact GgmlType::dequantize of n elements (device in, device out).
+cudaError_t launch_dequant(int type, const uint8_t* raw, size_t n, float* out, cudaStream_t s);
+
+// ---------------------------------------------------------------- matvec
+
+enum Epi : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_QKV = 3, EPI_LOGITS = 4 };
+
+// A run of 16-row tiles inside one matvec launch.
+//  pair == 0: tile t covers rows 16t .. 16t+15 of A (B is ignored).
+//  pair == 1: tile t covers rows 8t .. 8t+7 of A and of B (SwiGLU gate/up).
+struct Seg {
+    PackedW A, B;
+    int pair;
+    int ntiles;
+    int role;      // EPI_QKV: 0 = q, 1 = k, 2 = v
+    float* out;    // destination vector
+    int out_rows;  // logical rows written
+};
+
+struct MatvecArgs {
+    Seg seg[3];
+    int nseg;
+    int ntiles;
+    int K;             // logical input length
+    const float* x;    // input vector (device)
+    const float* norm_w;  // if set: x is RMS-normalised with this weight first
+    float eps;
+    int epi;
+    StepParams* step;
+    float* kcache;     // EPI_QKV: this layer's K/V cache, [ctx][kv_dim]
+    float* vcache;
+    int kv_dim;
+    int hd;
+    const float2* rope_cs;  // [ctx][hd/2] (cos, sin)
+};
+
+// Tiles in a segment for a weight of `rows` rows.
+inline int seg_tiles(int rows, int pair) { return pair ? (rows + 7) / 8 : (rows + 15) / 16; }
+cudaError_t launch_matvec(const MatvecArgs& a, int type, int max_ctas, cudaStream_t s);
+size_t matvec_smem_bytes(int type, int K);
+cudaError_t matvec_configure();  // opt-in shared memory limits, once per process
+int matvec_ctas_per_sm(int type, int K);
+
+// ---------------------------------------------------------------- attention
+
+struct AttnArgs {
+    const float* q;     // [n_head * hd], RoPE applied
+    const float* kc;    // [ctx][kv_dim] this layer
+    const float* vc;
+    float* out;         // [n_head * hd]
+    float* part;        // [n_head][nsplit][hd + 2] work area
+    unsigned* counters; // [n_kv], zero between launches
+    StepParams* step;
+    int n_head, n_kv, hd, kv_dim, nsplit;
+    float scale;
+};
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
+
+// ---------------------------------------------------------------- small kernels
+
+// x = dequant(token_embd row step->token); also clears step->argmax_key.
+cudaError_t launch_embed(const uint8_t* embd_raw, int type, int cols, int vocab, StepParams* step,
+                         float* x, cudaStream_t s);
+// out = rmsnorm(x, w)
+cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, float* out,
+                           cudaStream_t s);
+// Greedy feedback: token = argmax, append it to gen[], pos += 1.
+cudaError_t launch_greedy_advance(StepParams* step, uint32_t* gen, int gen_cap, cudaStream_t s);
+
+}  // namespace talos

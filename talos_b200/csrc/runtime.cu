@@ -1,0 +1,979 @@
+// runtime.cu -- the decode context behind include/talos_cuda.h.
+//
+// Host side of the B200 twin of Model::forward_gpu (Tsuskov/talos
+// src/model/llama.rs:188-206 -> src/math/metal/mod.rs:351-520):
+//  * weights are copied once, keyed by GGUF tensor name, and repacked on the
+//    GPU (src/math/metal/mod.rs:63-72 keeps them resident the same way);
+//  * the KV cache is a position-indexed device array per layer
+//    (src/math/metal/mod.rs:391-396,443-454);
+//  * activations live in one arena allocated once, not per token
+//    (src/math/metal/mod.rs:398-412 allocates 14 buffers every token);
+//  * one token = one CUDA graph replay of ~5 kernels per layer; the graph reads
+//    token and position from device memory, so the same graph serves every step.
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <memory>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/talos_cuda.h"
+#include "kernels.cuh"
+
+using namespace talos;
+
+// ------------------------------------------------------------------ errors
+
+static thread_local std::string g_last_error;
+
+static talos_status set_err(talos_status st, const char* fmt, ...) {
+    char buf[768];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return st;
+}
+
+#define CK(call)                                                                                 \
+    do {                                                                                         \
+        cudaError_t e_ = (call);                                                                 \
+        if (e_ != cudaSuccess)                                                                   \
+            return set_err(e_ == cudaErrorMemoryAllocation ? TALOS_ERR_OOM : TALOS_ERR_CUDA,     \
+                           "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__,     \
+                           __LINE__);                                                            \
+    } while (0)
+
+#define TRY(call)                              \
+    do {                                       \
+        talos_status s_ = (call);              \
+        if (s_ != TALOS_OK) return s_;         \
+    } while (0)
+
+extern "C" const char* talos_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" talos_status talos_device_count(int* out) {
+    if (!out) return set_err(TALOS_ERR_INVALID_ARG, "out is NULL");
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    *out = n;
+    return TALOS_OK;
+}
+
+static int block_elems(int t) { return t == GT_F32 ? 1 : t == GT_Q6_K ? 256 : (t == GT_Q4_0 || t == GT_Q8_0) ? 32 : 0; }
+static int block_bytes(int t) {
+    return t == GT_F32 ? 4 : t == GT_Q6_K ? 210 : t == GT_Q4_0 ? 18 : t == GT_Q8_0 ? 34 : 0;
+}
+
+// Raw GGUF byte length of a [rows, cols] tensor, 0 if the shape is invalid for the type.
+static size_t raw_len(int type, size_t rows, size_t cols) {
+    int be = block_elems(type);
+    if (!be || cols % be) return 0;
+    return rows * (cols / be) * block_bytes(type);
+}
+
+// ------------------------------------------------------------------ device tensors
+
+struct DevTensor {
+    int type = -1;
+    size_t rows = 0, cols = 0;
+    void* mem = nullptr;  // one allocation holding every array
+    size_t bytes = 0;
+    PackedW w{};          // packed matrix view (kind == PACKED)
+    enum Kind { PACKED, FLOATS, RAW } kind = PACKED;
+    void release() {
+        if (mem) cudaFree(mem);
+        mem = nullptr;
+        bytes = 0;
+    }
+};
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Allocate and fill a packed matrix from raw GGUF bytes already on the device.
+static talos_status pack_from_device(int type, size_t rows, size_t cols, const uint8_t* raw_dev,
+                                     DevTensor* t, cudaStream_t s) {
+    PackSizes ps;
+    if (rows == 0 || cols == 0 || rows > (1u << 30) || cols > (1u << 30) ||
+        !pack_sizes(type, (int)rows, (int)cols, &ps))
+        return set_err(TALOS_ERR_UNSUPPORTED, "cannot pack a [%zu, %zu] tensor of ggml type %d", rows,
+                       cols, type);
+    size_t o1 = align256(ps.b0), o2 = o1 + align256(ps.b1), o3 = o2 + align256(ps.b2);
+    size_t total = o3 + align256(ps.b3);
+    void* mem = nullptr;
+    CK(cudaMalloc(&mem, total));
+    PackedW w{};
+    w.type = type;
+    w.rows = (int)rows;
+    w.cols = (int)cols;
+    w.rows_pad = ps.rows_pad;
+    w.nk = ps.nk;
+    w.p0 = mem;
+    w.p1 = ps.b1 ? (uint8_t*)mem + o1 : nullptr;
+    w.p2 = ps.b2 ? (uint8_t*)mem + o2 : nullptr;
+    w.p3 = ps.b3 ? (uint8_t*)mem + o3 : nullptr;
+    cudaError_t e = launch_pack(raw_dev, w, s);
+    if (e != cudaSuccess) {
+        cudaFree(mem);
+        return set_err(TALOS_ERR_CUDA, "pack kernel: %s", cudaGetErrorString(e));
+    }
+    t->release();
+    t->type = type;
+    t->rows = rows;
+    t->cols = cols;
+    t->mem = mem;
+    t->bytes = total;
+    t->w = w;
+    t->kind = DevTensor::PACKED;
+    return TALOS_OK;
+}
+
+// Staging buffer for uploads: raw bytes go host -> device here, then get packed.
+struct Staging {
+    uint8_t* dev = nullptr;
+    size_t cap = 0;
+    talos_status reserve(size_t n) {
+        if (n <= cap) return TALOS_OK;
+        if (dev) cudaFree(dev);
+        dev = nullptr;
+        cap = 0;
+        CK(cudaMalloc(&dev, n));
+        cap = n;
+        return TALOS_OK;
+    }
+    void release() {
+        if (dev) cudaFree(dev);
+        dev = nullptr;
+        cap = 0;
+    }
+};
+
+static talos_status upload_packed(int type, const void* bytes, size_t len, size_t rows, size_t cols,
+                                  DevTensor* t, Staging* st, cudaStream_t s) {
+    TRY(st->reserve(len));
+    CK(cudaMemcpyAsync(st->dev, bytes, len, cudaMemcpyHostToDevice, s));
+    TRY(pack_from_device(type, rows, cols, st->dev, t, s));
+    CK(cudaStreamSynchronize(s));
+    return TALOS_OK;
+}
+
+static int g_sms[64];
+static std::once_flag g_cfg_once;
+static cudaError_t g_cfg_err = cudaSuccess;
+
+static talos_status device_setup(int device) {
+    int n = 0;
+    CK(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) return set_err(TALOS_ERR_INVALID_ARG, "device %d of %d", device, n);
+    CK(cudaSetDevice(device));
+    std::call_once(g_cfg_once, [] { g_cfg_err = matvec_configure(); });
+    if (g_cfg_err != cudaSuccess) return set_err(TALOS_ERR_CUDA, "matvec_configure: %s", cudaGetErrorString(g_cfg_err));
+    if (device < 64 && g_sms[device] == 0) {
+        int sms = 0;
+        CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+        g_sms[device] = sms;
+    }
+    return TALOS_OK;
+}
+
+static int max_ctas(int device, int type, int K) {
+    int sms = (device >= 0 && device < 64 && g_sms[device]) ? g_sms[device] : 148;
+    return sms * matvec_ctas_per_sm(type, K);
+}
+
+// ------------------------------------------------------------------ context
+
+struct LayerW {
+    DevTensor* attn_norm;
+    DevTensor *q, *k, *v, *o, *ffn_norm, *gate, *up, *down;
+};
+
+enum GraphMode { GM_LOGITS = 0, GM_HIDDEN = 1, GM_GREEDY = 2, GM_COUNT = 3 };
+
+struct talos_ctx {
+    talos_cfg cfg{};
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int hd = 0, kv_dim = 0, group = 0;
+    size_t kv_ctx = 0;  // positions the KV cache holds
+
+    std::unordered_map<std::string, DevTensor> w;         // model weights by GGUF name
+    std::unordered_map<std::string, DevTensor> resident;  // talos_matvec_resident cache
+    Staging staging;
+
+    // activation arena
+    void* arena = nullptr;
+    size_t arena_bytes = 0;
+    float *x = nullptr, *q = nullptr, *att = nullptr, *ff = nullptr, *logits = nullptr, *hidden = nullptr;
+    float* attn_part = nullptr;
+    unsigned* attn_counters = nullptr;
+    StepParams* step = nullptr;
+    uint32_t* gen = nullptr;
+    int nsplit = 1;
+    // KV + RoPE table
+    float* kcache = nullptr;
+    float* vcache = nullptr;
+    float2* rope_cs = nullptr;
+    size_t kv_bytes = 0;
+
+    // pinned host staging
+    float* h_out = nullptr;
+    StepParams* h_step = nullptr;
+    uint32_t* h_gen = nullptr;
+
+    cudaGraphExec_t graph[GM_COUNT] = {nullptr, nullptr, nullptr};
+    bool weights_dirty = true;
+    // talos_profile_step: events recorded after each launch, tagged by kernel kind
+    std::vector<std::pair<cudaEvent_t, int>>* prof = nullptr;
+    std::vector<LayerW> layers;
+
+    void drop_graphs() {
+        for (auto& g : graph)
+            if (g) {
+                cudaGraphExecDestroy(g);
+                g = nullptr;
+            }
+    }
+};
+
+static std::string lname(uint32_t l, const char* s) { return "blk." + std::to_string(l) + "." + s; }
+
+// Expected (rows, cols) of a model tensor by name; false if the name is not part
+// of the model (src/model/weights.rs:91-114).
+static bool expected_shape(const talos_ctx* c, const std::string& name, size_t* rows, size_t* cols,
+                           bool* is_norm) {
+    const size_t E = c->cfg.n_embd, F = c->cfg.n_ff, V = c->cfg.vocab_size, KV = (size_t)c->kv_dim;
+    *is_norm = false;
+    if (name == "token_embd.weight" || name == "output.weight") {
+        *rows = V;
+        *cols = E;
+        return true;
+    }
+    if (name == "output_norm.weight") {
+        *rows = 1;
+        *cols = E;
+        *is_norm = true;
+        return true;
+    }
+    if (name.compare(0, 4, "blk.") != 0) return false;
+    size_t dot = name.find('.', 4);
+    if (dot == std::string::npos) return false;
+    std::string idx = name.substr(4, dot - 4);
+    if (idx.empty() || idx.size() > 9 || idx.find_first_not_of("0123456789") != std::string::npos) return false;
+    unsigned long l = strtoul(idx.c_str(), nullptr, 10);
+    if (l >= c->cfg.n_layer || std::to_string(l) != idx) return false;
+    std::string rest = name.substr(dot + 1);
+    if (rest == "attn_norm.weight" || rest == "ffn_norm.weight") {
+        *rows = 1;
+        *cols = E;
+        *is_norm = true;
+    } else if (rest == "attn_q.weight" || rest == "attn_output.weight") {
+        *rows = E;
+        *cols = E;
+    } else if (rest == "attn_k.weight" || rest == "attn_v.weight") {
+        *rows = KV;
+        *cols = E;
+    } else if (rest == "ffn_gate.weight" || rest == "ffn_up.weight") {
+        *rows = F;
+        *cols = E;
+    } else if (rest == "ffn_down.weight") {
+        *rows = E;
+        *cols = F;
+    } else {
+        return false;
+    }
+    return true;
+}
+
+static talos_status alloc_kv(talos_ctx* c) {
+    if (c->kcache) cudaFree(c->kcache);
+    if (c->vcache) cudaFree(c->vcache);
+    if (c->rope_cs) cudaFree(c->rope_cs);
+    c->kcache = c->vcache = nullptr;
+    c->rope_cs = nullptr;
+    size_t per = (size_t)c->cfg.n_layer * c->kv_ctx * c->kv_dim * sizeof(float);
+    CK(cudaMalloc(&c->kcache, per ? per : 4));
+    CK(cudaMalloc(&c->vcache, per ? per : 4));
+    CK(cudaMemsetAsync(c->kcache, 0, per ? per : 4, c->stream));
+    CK(cudaMemsetAsync(c->vcache, 0, per ? per : 4, c->stream));
+    // RoPE table: theta = pos * base^(-2i/hd) in f32 with the C library's powf /
+    // sinf / cosf, the functions Rust's f32::powf / sin_cos call
+    // (src/math/ops.rs:53-54).
+    size_t half = (size_t)c->hd / 2;
+    std::vector<float2> cs(c->kv_ctx * (half ? half : 1));
+    for (size_t p = 0; p < c->kv_ctx; ++p)
+        for (size_t i = 0; i < half; ++i) {
+            float theta = (float)p * powf(c->cfg.rope_freq_base, -2.0f * (float)i / (float)c->hd);
+            cs[p * half + i] = make_float2(cosf(theta), sinf(theta));
+        }
+    CK(cudaMalloc(&c->rope_cs, cs.size() * sizeof(float2)));
+    CK(cudaMemcpyAsync(c->rope_cs, cs.data(), cs.size() * sizeof(float2), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    c->kv_bytes = 2 * per + cs.size() * sizeof(float2);
+    if (c->gen) {
+        cudaFree(c->gen);
+        c->gen = nullptr;
+    }
+    CK(cudaMalloc(&c->gen, (c->kv_ctx + 1) * sizeof(uint32_t)));
+    if (c->h_gen) cudaFreeHost(c->h_gen);
+    c->h_gen = nullptr;
+    CK(cudaMallocHost(&c->h_gen, (c->kv_ctx + 1) * sizeof(uint32_t)));
+    c->drop_graphs();
+    return TALOS_OK;
+}
+
+static talos_status alloc_arena(talos_ctx* c) {
+    const size_t E = c->cfg.n_embd, F = c->cfg.n_ff, V = c->cfg.vocab_size;
+    const size_t NH = c->cfg.n_head;
+    int sms = g_sms[c->device] ? g_sms[c->device] : 148;
+    int ns = (2 * sms + (int)c->cfg.n_head_kv - 1) / (int)c->cfg.n_head_kv;
+    if (ns > 64) ns = 64;
+    if (ns < 1) ns = 1;
+    c->nsplit = ns;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off += align256(bytes);
+        return o;
+    };
+    size_t o_x = take(E * 4), o_q = take(E * 4 + 64), o_att = take(E * 4), o_ff = take(F * 4),
+           o_log = take(V * 4), o_hid = take(E * 4),
+           o_part = take(NH * (size_t)ns * (c->hd + 2) * 4), o_cnt = take(c->cfg.n_head_kv * 4),
+           o_step = take(sizeof(StepParams));
+    CK(cudaMalloc(&c->arena, off));
+    CK(cudaMemsetAsync(c->arena, 0, off, c->stream));
+    c->arena_bytes = off;
+    uint8_t* b = (uint8_t*)c->arena;
+    c->x = (float*)(b + o_x);
+    c->q = (float*)(b + o_q);
+    c->att = (float*)(b + o_att);
+    c->ff = (float*)(b + o_ff);
+    c->logits = (float*)(b + o_log);
+    c->hidden = (float*)(b + o_hid);
+    c->attn_part = (float*)(b + o_part);
+    c->attn_counters = (unsigned*)(b + o_cnt);
+    c->step = (StepParams*)(b + o_step);
+    CK(cudaMallocHost(&c->h_out, (V > E ? V : E) * sizeof(float)));
+    CK(cudaMallocHost(&c->h_step, sizeof(StepParams)));
+    CK(cudaStreamSynchronize(c->stream));
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_ctx_create(const talos_cfg* cfg, int device, talos_ctx** out) {
+    if (!cfg || !out) return set_err(TALOS_ERR_INVALID_ARG, "cfg/out is NULL");
+    *out = nullptr;
+    if (cfg->n_head_kv == 0 || cfg->n_head == 0 || cfg->n_head % cfg->n_head_kv)
+        return set_err(TALOS_ERR_INVALID_ARG, "head_count %u must be a positive multiple of head_count_kv %u",
+                       cfg->n_head, cfg->n_head_kv);
+    if (cfg->n_layer == 0 || cfg->n_embd == 0 || cfg->n_ff == 0 || cfg->vocab_size == 0 ||
+        cfg->context_length == 0)
+        return set_err(TALOS_ERR_INVALID_ARG, "zero-sized model dimension");
+    if (cfg->n_embd % cfg->n_head)
+        return set_err(TALOS_ERR_UNSUPPORTED, "n_embd %u not a multiple of n_head %u", cfg->n_embd, cfg->n_head);
+    uint32_t hd = cfg->n_embd / cfg->n_head;
+    if (hd % 2 || hd > 256 || cfg->n_head / cfg->n_head_kv > 8)
+        return set_err(TALOS_ERR_UNSUPPORTED, "head_dim %u / group %u outside this build (even, <= 256; <= 8)",
+                       hd, cfg->n_head / cfg->n_head_kv);
+    TRY(device_setup(device));
+    std::unique_ptr<talos_ctx> c(new talos_ctx());
+    c->cfg = *cfg;
+    c->device = device;
+    c->hd = (int)hd;
+    c->kv_dim = (int)(cfg->n_head_kv * hd);
+    c->group = (int)(cfg->n_head / cfg->n_head_kv);
+    c->kv_ctx = cfg->context_length;
+    CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    TRY(alloc_arena(c.get()));
+    TRY(alloc_kv(c.get()));
+    *out = c.release();
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_ctx_destroy(talos_ctx* c) {
+    if (!c) return TALOS_OK;
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    c->drop_graphs();
+    for (auto& kv : c->w) kv.second.release();
+    for (auto& kv : c->resident) kv.second.release();
+    c->staging.release();
+    if (c->arena) cudaFree(c->arena);
+    if (c->kcache) cudaFree(c->kcache);
+    if (c->vcache) cudaFree(c->vcache);
+    if (c->rope_cs) cudaFree(c->rope_cs);
+    if (c->gen) cudaFree(c->gen);
+    if (c->h_out) cudaFreeHost(c->h_out);
+    if (c->h_step) cudaFreeHost(c->h_step);
+    if (c->h_gen) cudaFreeHost(c->h_gen);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_weight_upload(talos_ctx* c, const char* name, const void* bytes, size_t len,
+                                            int type, size_t rows, size_t cols) {
+    if (!c || !name || (!bytes && len)) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    CK(cudaSetDevice(c->device));
+    size_t er, ec;
+    bool is_norm;
+    std::string nm(name);
+    if (!expected_shape(c, nm, &er, &ec, &is_norm))
+        return set_err(TALOS_ERR_INVALID_ARG, "\"%s\" is not a tensor of this model", name);
+    if (is_norm) {
+        if (type != GT_F32) return set_err(TALOS_ERR_INVALID_ARG, "norm weight \"%s\" must be F32", name);
+        if (rows * cols != ec || len != ec * 4)
+            return set_err(TALOS_ERR_INVALID_ARG, "\"%s\": expected %zu floats, got rows*cols=%zu len=%zu", name,
+                           ec, rows * cols, len);
+    } else {
+        if (rows != er || cols != ec)
+            return set_err(TALOS_ERR_INVALID_ARG, "\"%s\": expected [%zu, %zu], got [%zu, %zu]", name, er, ec, rows,
+                           cols);
+        size_t want = raw_len(type, rows, cols);
+        if (!want) return set_err(TALOS_ERR_UNSUPPORTED, "\"%s\": ggml type %d with %zu cols", name, type, cols);
+        if (len != want)
+            return set_err(TALOS_ERR_INVALID_ARG, "\"%s\": %zu bytes, expected %zu", name, len, want);
+    }
+    DevTensor& t = c->w[nm];
+    if (is_norm || nm == "token_embd.weight") {
+        // Kept as-is: norm weights as f32, the embedding as raw GGUF blocks (one
+        // row is dequantized per token on the GPU).
+        t.release();
+        void* mem = nullptr;
+        CK(cudaMalloc(&mem, len));
+        CK(cudaMemcpy(mem, bytes, len, cudaMemcpyHostToDevice));
+        t.type = type;
+        t.rows = is_norm ? 1 : rows;
+        t.cols = is_norm ? ec : cols;
+        t.mem = mem;
+        t.bytes = len;
+        t.kind = is_norm ? DevTensor::FLOATS : DevTensor::RAW;
+    } else {
+        TRY(upload_packed(type, bytes, len, rows, cols, &t, &c->staging, c->stream));
+    }
+    c->weights_dirty = true;
+    c->drop_graphs();
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_ctx_device_bytes(talos_ctx* c, size_t* out) {
+    if (!c || !out) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    size_t n = c->arena_bytes + c->kv_bytes + c->staging.cap;
+    for (auto& kv : c->w) n += kv.second.bytes;
+    for (auto& kv : c->resident) n += kv.second.bytes;
+    *out = n;
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_ctx_stream(talos_ctx* c, void** out) {
+    if (!c || !out) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    *out = (void*)c->stream;
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_cap_context(talos_ctx* c, size_t max_ctx) {
+    if (!c) return set_err(TALOS_ERR_INVALID_ARG, "NULL ctx");
+    CK(cudaSetDevice(c->device));
+    CK(cudaStreamSynchronize(c->stream));
+    size_t cap = max_ctx > 1 ? max_ctx : 1;
+    if (cap < c->cfg.context_length) c->cfg.context_length = (uint32_t)cap;
+    c->kv_ctx = c->cfg.context_length;
+    return alloc_kv(c);
+}
+
+extern "C" talos_status talos_kv_reset(talos_ctx* c) {
+    if (!c) return set_err(TALOS_ERR_INVALID_ARG, "NULL ctx");
+    return TALOS_OK;
+}
+
+// ------------------------------------------------------------------ the decode step
+
+static talos_status bind_layers(talos_ctx* c) {
+    auto get = [&](const std::string& n, DevTensor** out) -> talos_status {
+        auto it = c->w.find(n);
+        if (it == c->w.end() || !it->second.mem)
+            return set_err(TALOS_ERR_STATE, "weight \"%s\" has not been uploaded", n.c_str());
+        *out = &it->second;
+        return TALOS_OK;
+    };
+    c->layers.assign(c->cfg.n_layer, LayerW{});
+    for (uint32_t l = 0; l < c->cfg.n_layer; ++l) {
+        LayerW& L = c->layers[l];
+        TRY(get(lname(l, "attn_norm.weight"), &L.attn_norm));
+        TRY(get(lname(l, "attn_q.weight"), &L.q));
+        TRY(get(lname(l, "attn_k.weight"), &L.k));
+        TRY(get(lname(l, "attn_v.weight"), &L.v));
+        TRY(get(lname(l, "attn_output.weight"), &L.o));
+        TRY(get(lname(l, "ffn_norm.weight"), &L.ffn_norm));
+        TRY(get(lname(l, "ffn_gate.weight"), &L.gate));
+        TRY(get(lname(l, "ffn_up.weight"), &L.up));
+        TRY(get(lname(l, "ffn_down.weight"), &L.down));
+        if (L.gate->type != L.up->type)
+            return set_err(TALOS_ERR_UNSUPPORTED, "layer %u: ffn_gate and ffn_up must share a ggml type", l);
+    }
+    DevTensor* t;
+    TRY(get("token_embd.weight", &t));
+    TRY(get("output_norm.weight", &t));
+    TRY(get("output.weight", &t));
+    return TALOS_OK;
+}
+
+static Seg make_seg(const DevTensor* A, const DevTensor* B, int pair, float* out, int out_rows, int role) {
+    Seg s{};
+    s.A = A->w;
+    s.B = B ? B->w : A->w;
+    s.pair = pair;
+    s.ntiles = seg_tiles(A->w.rows, pair);
+    s.out = out;
+    s.out_rows = out_rows;
+    s.role = role;
+    return s;
+}
+
+static talos_status run_mv(talos_ctx* c, MatvecArgs& a, int type) {
+    a.ntiles = 0;
+    for (int i = 0; i < a.nseg; ++i) a.ntiles += a.seg[i].ntiles;
+    cudaError_t e = launch_matvec(a, type, max_ctas(c->device, type, a.K), c->stream);
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "matvec launch: %s", cudaGetErrorString(e));
+    return TALOS_OK;
+}
+
+// Record a profiling event after the launch of kernel `kind` (profiling only).
+static talos_status mark(talos_ctx* c, int kind) {
+    if (!c->prof) return TALOS_OK;
+    cudaEvent_t e;
+    CK(cudaEventCreate(&e));
+    c->prof->push_back({e, kind});
+    CK(cudaEventRecord(e, c->stream));
+    return TALOS_OK;
+}
+
+// Enqueue one token step (llama.rs:96-183 + :89) on c->stream.
+static talos_status enqueue_step(talos_ctx* c, GraphMode mode) {
+    const talos_cfg& cfg = c->cfg;
+    const int E = (int)cfg.n_embd, F = (int)cfg.n_ff;
+    cudaStream_t s = c->stream;
+    const DevTensor& embd = c->w["token_embd.weight"];
+    TRY(mark(c, -1));
+    cudaError_t e = launch_embed((const uint8_t*)embd.mem, embd.type, E, (int)cfg.vocab_size, c->step, c->x, s);
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "embed: %s", cudaGetErrorString(e));
+    TRY(mark(c, TALOS_K_EMBED));
+    const size_t kv_layer = c->kv_ctx * (size_t)c->kv_dim;
+    for (uint32_t l = 0; l < cfg.n_layer; ++l) {
+        const LayerW& L = c->layers[l];
+        float* kc = c->kcache + l * kv_layer;
+        float* vc = c->vcache + l * kv_layer;
+        // --- rmsnorm + q/k/v + RoPE + KV append (llama.rs:118-130)
+        {
+            const DevTensor* qkv[3] = {L.q, L.k, L.v};
+            float* outs[3] = {c->q, nullptr, nullptr};
+            int rows[3] = {E, c->kv_dim, c->kv_dim};
+            bool same = L.q->type == L.k->type && L.k->type == L.v->type;
+            for (int i = 0; i < 3;) {
+                MatvecArgs a{};
+                a.K = E;
+                a.x = c->x;
+                a.norm_w = (const float*)L.attn_norm->mem;
+                a.eps = cfg.rms_eps;
+                a.epi = EPI_QKV;
+                a.step = c->step;
+                a.kcache = kc;
+                a.vcache = vc;
+                a.kv_dim = c->kv_dim;
+                a.hd = c->hd;
+                a.rope_cs = c->rope_cs;
+                int type = qkv[i]->type;
+                int n = same ? 3 : 1;
+                for (int j = 0; j < n; ++j)
+                    a.seg[a.nseg++] = make_seg(qkv[i + j], nullptr, 0, outs[i + j], rows[i + j], i + j);
+                TRY(run_mv(c, a, type));
+                TRY(mark(c, TALOS_K_QKV));
+                i += n;
+            }
+        }
+        // --- attention (llama.rs:135-155)
+        {
+            AttnArgs a{};
+            a.q = c->q;
+            a.kc = kc;
+            a.vc = vc;
+            a.out = c->att;
+            a.part = c->attn_part;
+            a.counters = c->attn_counters;
+            a.step = c->step;
+            a.n_head = (int)cfg.n_head;
+            a.n_kv = (int)cfg.n_head_kv;
+            a.hd = c->hd;
+            a.kv_dim = c->kv_dim;
+            a.nsplit = c->nsplit;
+            a.scale = 1.0f / sqrtf((float)c->hd);
+            e = launch_attention(a, s);
+            if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "attention: %s", cudaGetErrorString(e));
+            TRY(mark(c, TALOS_K_ATTN));
+        }
+        // --- o-proj + residual (llama.rs:157-161)
+        {
+            MatvecArgs a{};
+            a.K = E;
+            a.x = c->att;
+            a.epi = EPI_ADD;
+            a.step = c->step;
+            a.seg[a.nseg++] = make_seg(L.o, nullptr, 0, c->x, E, 0);
+            TRY(run_mv(c, a, L.o->type));
+            TRY(mark(c, TALOS_K_OPROJ));
+        }
+        // --- rmsnorm + gate/up + SwiGLU (llama.rs:164-171)
+        {
+            MatvecArgs a{};
+            a.K = E;
+            a.x = c->x;
+            a.norm_w = (const float*)L.ffn_norm->mem;
+            a.eps = cfg.rms_eps;
+            a.epi = EPI_SWIGLU;
+            a.step = c->step;
+            a.seg[a.nseg++] = make_seg(L.gate, L.up, 1, c->ff, F, 0);
+            TRY(run_mv(c, a, L.gate->type));
+            TRY(mark(c, TALOS_K_GATEUP));
+        }
+        // --- down + residual (llama.rs:172-176)
+        {
+            MatvecArgs a{};
+            a.K = F;
+            a.x = c->ff;
+            a.epi = EPI_ADD;
+            a.step = c->step;
+            a.seg[a.nseg++] = make_seg(L.down, nullptr, 0, c->x, E, 0);
+            TRY(run_mv(c, a, L.down->type));
+            TRY(mark(c, TALOS_K_DOWN));
+        }
+    }
+    const DevTensor& onorm = c->w["output_norm.weight"];
+    if (mode == GM_HIDDEN) {
+        e = launch_rmsnorm(c->x, (const float*)onorm.mem, cfg.rms_eps, E, c->hidden, s);
+        if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "rmsnorm: %s", cudaGetErrorString(e));
+        return TALOS_OK;
+    }
+    // --- final rmsnorm + output projection (llama.rs:181, :89)
+    {
+        const DevTensor& ow = c->w["output.weight"];
+        MatvecArgs a{};
+        a.K = E;
+        a.x = c->x;
+        a.norm_w = (const float*)onorm.mem;
+        a.eps = cfg.rms_eps;
+        a.epi = EPI_LOGITS;
+        a.step = c->step;
+        a.seg[a.nseg++] = make_seg(&ow, nullptr, 0, c->logits, (int)cfg.vocab_size, 0);
+        TRY(run_mv(c, a, ow.type));
+        TRY(mark(c, TALOS_K_OUTPUT));
+    }
+    if (mode == GM_GREEDY) {
+        e = launch_greedy_advance(c->step, c->gen, (int)c->kv_ctx + 1, s);
+        if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "greedy advance: %s", cudaGetErrorString(e));
+    }
+    return TALOS_OK;
+}
+
+static talos_status ensure_graph(talos_ctx* c, GraphMode mode) {
+    if (c->weights_dirty) {
+        TRY(bind_layers(c));
+        c->weights_dirty = false;
+    }
+    if (c->graph[mode]) return TALOS_OK;
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    talos_status st = enqueue_step(c, mode);
+    cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+    if (st != TALOS_OK) {
+        if (g) cudaGraphDestroy(g);
+        return st;
+    }
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&c->graph[mode], g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+    return TALOS_OK;
+}
+
+static talos_status check_tok_pos(talos_ctx* c, uint32_t token, size_t pos) {
+    if (token >= c->cfg.vocab_size)
+        return set_err(TALOS_ERR_INVALID_ARG, "token %u out of range (vocab %u)", token, c->cfg.vocab_size);
+    if (pos >= c->kv_ctx)
+        return set_err(TALOS_ERR_INVALID_ARG, "pos %zu outside the KV cache (%zu positions)", pos, c->kv_ctx);
+    return TALOS_OK;
+}
+
+static talos_status set_step(talos_ctx* c, uint32_t token, size_t pos) {
+    StepParams* h = c->h_step;
+    memset(h, 0, sizeof *h);
+    h->token = token;
+    h->pos = (uint32_t)pos;
+    CK(cudaMemcpyAsync(c->step, h, sizeof *h, cudaMemcpyHostToDevice, c->stream));
+    return TALOS_OK;
+}
+
+static talos_status finish_step(talos_ctx* c) {
+    CK(cudaMemcpyAsync(c->h_step, c->step, sizeof(StepParams), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    if (c->h_step->error) return set_err(TALOS_ERR_OOB, "device bounds check fired (code %u)", c->h_step->error);
+    return TALOS_OK;
+}
+
+static talos_status forward_common(talos_ctx* c, uint32_t token, size_t pos, float* out, GraphMode mode) {
+    if (!c || !out) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    CK(cudaSetDevice(c->device));
+    TRY(check_tok_pos(c, token, pos));
+    TRY(ensure_graph(c, mode));
+    TRY(set_step(c, token, pos));
+    CK(cudaGraphLaunch(c->graph[mode], c->stream));
+    size_t n = mode == GM_HIDDEN ? c->cfg.n_embd : c->cfg.vocab_size;
+    CK(cudaMemcpyAsync(c->h_out, mode == GM_HIDDEN ? c->hidden : c->logits, n * 4, cudaMemcpyDeviceToHost,
+                       c->stream));
+    TRY(finish_step(c));
+    memcpy(out, c->h_out, n * 4);
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_forward(talos_ctx* c, uint32_t token, size_t pos, float* logits_out) {
+    return forward_common(c, token, pos, logits_out, GM_LOGITS);
+}
+
+extern "C" talos_status talos_forward_hidden(talos_ctx* c, uint32_t token, size_t pos, float* hidden_out) {
+    return forward_common(c, token, pos, hidden_out, GM_HIDDEN);
+}
+
+extern "C" talos_status talos_generate_greedy(talos_ctx* c, uint32_t token, size_t pos, size_t n,
+                                              uint32_t* tokens_out) {
+    if (!c || (!tokens_out && n)) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    if (n == 0) return TALOS_OK;
+    CK(cudaSetDevice(c->device));
+    TRY(check_tok_pos(c, token, pos));
+    if (pos + n > c->kv_ctx)
+        return set_err(TALOS_ERR_INVALID_ARG, "pos %zu + %zu steps exceeds the KV cache (%zu)", pos, n, c->kv_ctx);
+    TRY(ensure_graph(c, GM_GREEDY));
+    TRY(set_step(c, token, pos));
+    for (size_t i = 0; i < n; ++i) CK(cudaGraphLaunch(c->graph[GM_GREEDY], c->stream));
+    CK(cudaMemcpyAsync(c->h_gen, c->gen, n * 4, cudaMemcpyDeviceToHost, c->stream));
+    TRY(finish_step(c));
+    memcpy(tokens_out, c->h_gen, n * 4);
+    return TALOS_OK;
+}
+
+// Per-token step parameters for a prefill, set by a kernel so the host never
+// rewrites a buffer a pending copy still reads.
+__global__ void k_set_step(StepParams* s, uint32_t token, uint32_t pos) {
+    s->token = token;
+    s->pos = pos;
+}
+
+extern "C" talos_status talos_prefill(talos_ctx* c, const uint32_t* tokens, size_t n, size_t pos0,
+                                      float* last_logits) {
+    if (!c || (!tokens && n)) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    if (n == 0) return TALOS_OK;
+    CK(cudaSetDevice(c->device));
+    for (size_t i = 0; i < n; ++i) TRY(check_tok_pos(c, tokens[i], pos0 + i));
+    TRY(ensure_graph(c, GM_LOGITS));
+    TRY(set_step(c, tokens[0], pos0));
+    for (size_t i = 0; i < n; ++i) {
+        if (i) {
+            k_set_step<<<1, 1, 0, c->stream>>>(c->step, tokens[i], (uint32_t)(pos0 + i));
+            CK(cudaGetLastError());
+        }
+        CK(cudaGraphLaunch(c->graph[GM_LOGITS], c->stream));
+    }
+    if (last_logits)
+        CK(cudaMemcpyAsync(c->h_out, c->logits, c->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, c->stream));
+    TRY(finish_step(c));
+    if (last_logits) memcpy(last_logits, c->h_out, c->cfg.vocab_size * 4);
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_profile_step(talos_ctx* c, uint32_t token, size_t pos, double* kernel_ms,
+                                           uint32_t* launches) {
+    if (!c) return set_err(TALOS_ERR_INVALID_ARG, "NULL ctx");
+    CK(cudaSetDevice(c->device));
+    TRY(check_tok_pos(c, token, pos));
+    if (c->weights_dirty) {
+        TRY(bind_layers(c));
+        c->weights_dirty = false;
+    }
+    TRY(set_step(c, token, pos));
+    std::vector<std::pair<cudaEvent_t, int>> ev;
+    c->prof = &ev;
+    talos_status st = enqueue_step(c, GM_LOGITS);
+    c->prof = nullptr;
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    if (st == TALOS_OK && e != cudaSuccess) st = set_err(TALOS_ERR_CUDA, "profile step: %s", cudaGetErrorString(e));
+    for (size_t i = 1; st == TALOS_OK && i < ev.size(); ++i) {
+        float ms = 0.f;
+        e = cudaEventElapsedTime(&ms, ev[i - 1].first, ev[i].first);
+        if (e != cudaSuccess) {
+            st = set_err(TALOS_ERR_CUDA, "event timing: %s", cudaGetErrorString(e));
+            break;
+        }
+        int k = ev[i].second;
+        if (k >= 0 && k < TALOS_K_COUNT) {
+            if (kernel_ms) kernel_ms[k] += ms;
+            if (launches) launches[k] += 1;
+        }
+    }
+    for (auto& p : ev) cudaEventDestroy(p.first);
+    return st;
+}
+
+// ------------------------------------------------------------------ tensor parallel (not yet)
+
+extern "C" talos_status talos_nccl_unique_id(uint8_t out[128]) {
+    (void)out;
+    return set_err(TALOS_ERR_UNSUPPORTED, "tensor parallelism is not in this build");
+}
+
+extern "C" talos_status talos_ctx_create_tp(const talos_cfg* cfg, int device, int tp_size, int tp_rank,
+                                            const uint8_t* id, talos_ctx** out) {
+    if (tp_size == 1 && tp_rank == 0) return talos_ctx_create(cfg, device, out);
+    (void)id;
+    return set_err(TALOS_ERR_UNSUPPORTED, "tensor parallelism is not in this build");
+}
+
+// ------------------------------------------------------------------ kernels as calls
+
+extern "C" talos_status talos_dequant(int type, const void* bytes, size_t n, float* out) {
+    if ((!bytes || !out) && n) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    int be = block_elems(type);
+    if (!be) return set_err(TALOS_ERR_UNSUPPORTED, "ggml type %d", type);
+    if (n % be) return set_err(TALOS_ERR_INVALID_ARG, "%zu elements is not a multiple of block %d", n, be);
+    if (n == 0) return TALOS_OK;
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    TRY(device_setup(dev));
+    size_t len = n / be * block_bytes(type);
+    uint8_t* d_raw = nullptr;
+    float* d_out = nullptr;
+    CK(cudaMalloc(&d_raw, len));
+    cudaError_t e = cudaMalloc(&d_out, n * 4);
+    if (e == cudaSuccess) e = cudaMemcpy(d_raw, bytes, len, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = launch_dequant(type, d_raw, n, d_out, 0);
+    if (e == cudaSuccess) e = cudaMemcpy(out, d_out, n * 4, cudaMemcpyDeviceToHost);
+    cudaFree(d_raw);
+    if (d_out) cudaFree(d_out);
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "dequant: %s", cudaGetErrorString(e));
+    return TALOS_OK;
+}
+
+struct talos_weight {
+    int device;
+    DevTensor t;
+};
+
+static talos_status matvec_on(const DevTensor& t, int device, const float* x_dev, float* y_dev, cudaStream_t s) {
+    MatvecArgs a{};
+    a.K = (int)t.cols;
+    a.x = x_dev;
+    a.epi = EPI_STORE;
+    Seg sg{};
+    sg.A = sg.B = t.w;
+    sg.ntiles = seg_tiles(t.w.rows, 0);
+    sg.out = y_dev;
+    sg.out_rows = (int)t.rows;
+    a.seg[0] = sg;
+    a.nseg = 1;
+    a.ntiles = sg.ntiles;
+    cudaError_t e = launch_matvec(a, t.type, max_ctas(device, t.type, a.K), s);
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "matvec launch: %s", cudaGetErrorString(e));
+    return TALOS_OK;
+}
+
+static talos_status check_matrix(int type, size_t len, size_t rows, size_t cols) {
+    size_t want = raw_len(type, rows, cols);
+    if (!want) return set_err(TALOS_ERR_UNSUPPORTED, "ggml type %d with %zu cols", type, cols);
+    if (len != want) return set_err(TALOS_ERR_INVALID_ARG, "%zu bytes, expected %zu for [%zu, %zu]", len, want, rows, cols);
+    if (type == GT_Q4_0 || type == GT_Q8_0 || type == GT_Q6_K || type == GT_F32) {
+        size_t KP = type == GT_Q4_0 ? ((cols / 32 + 3) / 4) * 128 : cols;
+        if (KP * 4 + 1024 > 200 * 1024)
+            return set_err(TALOS_ERR_UNSUPPORTED, "cols %zu exceed the staged input limit", cols);
+    }
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_weight_create(int device, int type, const void* bytes, size_t len, size_t rows,
+                                            size_t cols, talos_weight** out) {
+    if (!bytes || !out) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    *out = nullptr;
+    TRY(check_matrix(type, len, rows, cols));
+    TRY(device_setup(device));
+    std::unique_ptr<talos_weight> w(new talos_weight());
+    w->device = device;
+    Staging st;
+    talos_status s = upload_packed(type, bytes, len, rows, cols, &w->t, &st, 0);
+    st.release();
+    TRY(s);
+    *out = w.release();
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_weight_destroy(talos_weight* w) {
+    if (!w) return TALOS_OK;
+    cudaSetDevice(w->device);
+    w->t.release();
+    delete w;
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_weight_packed_bytes(const talos_weight* w, size_t* out) {
+    if (!w || !out) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    *out = w->t.bytes;
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_matvec_dev(const talos_weight* w, const float* x_dev, float* y_dev, void* stream) {
+    if (!w || !x_dev || !y_dev) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    CK(cudaSetDevice(w->device));
+    return matvec_on(w->t, w->device, x_dev, y_dev, (cudaStream_t)stream);
+}
+
+static talos_status matvec_host(const DevTensor& t, int device, const float* x, float* y, cudaStream_t s) {
+    float *dx = nullptr, *dy = nullptr;
+    CK(cudaMalloc(&dx, t.cols * 4));
+    cudaError_t e = cudaMalloc(&dy, t.rows * 4);
+    talos_status st = TALOS_OK;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dx, x, t.cols * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) st = matvec_on(t, device, dx, dy, s);
+    if (e == cudaSuccess && st == TALOS_OK) e = cudaMemcpyAsync(y, dy, t.rows * 4, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess && st == TALOS_OK) e = cudaStreamSynchronize(s);
+    cudaFree(dx);
+    if (dy) cudaFree(dy);
+    if (st != TALOS_OK) return st;
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "matvec: %s", cudaGetErrorString(e));
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_matvec(int device, int type, const void* bytes, size_t len, size_t rows, size_t cols,
+                                     const float* x, float* y) {
+    if (!bytes || !x || !y) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    talos_weight* w = nullptr;
+    TRY(talos_weight_create(device, type, bytes, len, rows, cols, &w));
+    talos_status st = matvec_host(w->t, device, x, y, 0);
+    talos_weight_destroy(w);
+    return st;
+}
+
+extern "C" talos_status talos_matvec_resident(talos_ctx* c, const char* name, int type, const void* bytes,
+                                              size_t len, size_t rows, size_t cols, const float* x, float* y) {
+    if (!c || !name || !bytes || !x || !y) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    CK(cudaSetDevice(c->device));
+    TRY(check_matrix(type, len, rows, cols));
+    DevTensor& t = c->resident[name];
+    // src/math/metal/mod.rs:63-72: reuse the cached buffer while the byte length matches.
+    bool hit = t.mem && t.type == type && t.rows == rows && t.cols == cols &&
+               raw_len(t.type, t.rows, t.cols) == len;
+    if (!hit) TRY(upload_packed(type, bytes, len, rows, cols, &t, &c->staging, c->stream));
+    return matvec_host(t, c->device, x, y, c->stream);
+}

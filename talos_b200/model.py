@@ -1,0 +1,313 @@
+"""Host-side mirror of Talos's ``Model`` for the CUDA decode path.
+
+Same names and argument meaning as the Rust API (Tsuskov/talos
+``src/model/llama.rs:20-238``): ``Model.load`` / ``load_bytes``, ``forward_gpu`` /
+``forward_hidden_gpu`` (the ``cuda`` twins of the Metal functions), ``step`` /
+``step_hidden`` (the dispatch point of ``llama.rs:211-233``; with the CUDA build it
+always takes the GPU path), ``reset`` and ``cap_context``. Weights are read from
+the GGUF with the same names and shapes as ``Weights::from_gguf``
+(``src/model/weights.rs:91-114``) and handed to the C ABI, which copies them to the
+GPU once. There is no CPU forward here: the reference CPU ``forward`` is the
+oracle used by the tests, not part of this package.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+from .gguf import F32, GgufError, GgufFile
+
+
+@dataclass
+class Config:
+    """``Config`` (src/model/config.rs:14-67)."""
+
+    n_layer: int
+    n_head: int
+    n_head_kv: int
+    n_embd: int
+    n_ff: int
+    context_length: int
+    vocab_size: int
+    rms_eps: float
+    rope_dim: int
+    rope_freq_base: float
+
+    def head_dim(self) -> int:
+        return self.n_embd // self.n_head
+
+    def kv_dim(self) -> int:
+        return self.n_head_kv * self.head_dim()
+
+    @classmethod
+    def from_gguf(cls, g: GgufFile) -> "Config":
+        """config.rs:40-67: llama.* keys, vocab = len(tokenizer.ggml.tokens),
+        eps defaults to 1e-5, freq_base to 10000."""
+        arch = g.get_str("general.architecture") or ""
+        if arch != "llama":
+            raise GgufError(f"unsupported architecture {arch!r} (expected \"llama\")")
+
+        def u(k):
+            v = g.get_u32(k)
+            if v is None:
+                raise GgufError(f"missing metadata key {k}")
+            return v
+
+        toks = g.get_arr_str("tokenizer.ggml.tokens")
+        if toks is None:
+            raise GgufError("missing tokenizer.ggml.tokens (needed for vocab size)")
+        eps = g.get_f32("llama.attention.layer_norm_rms_epsilon")
+        base = g.get_f32("llama.rope.freq_base")
+        return cls(
+            n_layer=u("llama.block_count"),
+            n_head=u("llama.attention.head_count"),
+            n_head_kv=u("llama.attention.head_count_kv"),
+            n_embd=u("llama.embedding_length"),
+            n_ff=u("llama.feed_forward_length"),
+            context_length=u("llama.context_length"),
+            vocab_size=len(toks),
+            rms_eps=1e-5 if eps is None else eps,
+            rope_dim=u("llama.rope.dimension_count"),
+            rope_freq_base=10000.0 if base is None else base,
+        )
+
+    def to_c(self) -> _lib.Cfg:
+        return _lib.Cfg(self.n_layer, self.n_head, self.n_head_kv, self.n_embd, self.n_ff,
+                        self.context_length, self.vocab_size, self.rope_dim, self.rms_eps,
+                        self.rope_freq_base)
+
+
+def weight_shapes(cfg: Config) -> dict[str, tuple[int, int]]:
+    """Tensor name -> (rows, cols) exactly as Weights::from_gguf binds them
+    (src/model/weights.rs:91-114); norms are (1, n)."""
+    c, ff, v, kv = cfg.n_embd, cfg.n_ff, cfg.vocab_size, cfg.kv_dim()
+    out = {"token_embd.weight": (v, c), "output_norm.weight": (1, c), "output.weight": (v, c)}
+    for l in range(cfg.n_layer):
+        p = f"blk.{l}."
+        out.update({
+            p + "attn_norm.weight": (1, c),
+            p + "attn_q.weight": (c, c),
+            p + "attn_k.weight": (kv, c),
+            p + "attn_v.weight": (kv, c),
+            p + "attn_output.weight": (c, c),
+            p + "ffn_norm.weight": (1, c),
+            p + "ffn_gate.weight": (ff, c),
+            p + "ffn_up.weight": (ff, c),
+            p + "ffn_down.weight": (c, ff),
+        })
+    return out
+
+
+def _ptr(a) -> int:
+    return a.ctypes.data if isinstance(a, np.ndarray) else C.addressof(a)
+
+
+class Context:
+    """One ``talos_ctx``: a model's weights, KV cache and captured graphs on one GPU."""
+
+    def __init__(self, cfg: Config, device: int = 0, tp_size: int = 1, tp_rank: int = 0,
+                 nccl_id: bytes | None = None):
+        L = _lib.load()
+        self.cfg = cfg
+        h = C.c_void_p()
+        c = cfg.to_c()
+        if tp_size == 1:
+            _lib.check(L.talos_ctx_create(C.byref(c), device, C.byref(h)))
+        else:
+            idbuf = C.create_string_buffer(bytes(nccl_id), 128)
+            _lib.check(L.talos_ctx_create_tp(C.byref(c), device, tp_size, tp_rank, idbuf, C.byref(h)))
+        self.h = h
+        self.device = device
+
+    def close(self):
+        if getattr(self, "h", None):
+            _lib.load().talos_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def upload(self, name: str, raw, gtype: int, rows: int, cols: int):
+        buf = np.frombuffer(raw, np.uint8) if not isinstance(raw, np.ndarray) else raw.view(np.uint8)
+        buf = np.ascontiguousarray(buf)
+        _lib.check(_lib.load().talos_weight_upload(self.h, name.encode(), _ptr(buf), buf.nbytes, gtype,
+                                                   rows, cols))
+
+    def device_bytes(self) -> int:
+        n = C.c_size_t()
+        _lib.check(_lib.load().talos_ctx_device_bytes(self.h, C.byref(n)))
+        return n.value
+
+    def stream(self) -> int:
+        """The cudaStream_t this context runs on (for CUDA-event timing)."""
+        p = C.c_void_p()
+        _lib.check(_lib.load().talos_ctx_stream(self.h, C.byref(p)))
+        return p.value or 0
+
+    def forward(self, token: int, pos: int, out: np.ndarray | None = None) -> np.ndarray:
+        if out is None:
+            out = np.empty(self.cfg.vocab_size, np.float32)
+        _lib.check(_lib.load().talos_forward(self.h, int(token), int(pos), _ptr(out)))
+        return out
+
+    def forward_hidden(self, token: int, pos: int) -> np.ndarray:
+        out = np.empty(self.cfg.n_embd, np.float32)
+        _lib.check(_lib.load().talos_forward_hidden(self.h, int(token), int(pos), _ptr(out)))
+        return out
+
+    def generate_greedy(self, token: int, pos: int, n: int) -> np.ndarray:
+        out = np.empty(max(n, 1), np.uint32)
+        _lib.check(_lib.load().talos_generate_greedy(self.h, int(token), int(pos), int(n), _ptr(out)))
+        return out[:n]
+
+    def prefill(self, tokens, pos0: int = 0, want_logits: bool = True):
+        toks = np.ascontiguousarray(tokens, np.uint32)
+        out = np.empty(self.cfg.vocab_size, np.float32) if want_logits else None
+        _lib.check(_lib.load().talos_prefill(self.h, _ptr(toks), toks.size, int(pos0),
+                                             _ptr(out) if out is not None else None))
+        return out
+
+    def reset(self):
+        _lib.check(_lib.load().talos_kv_reset(self.h))
+
+    KERNEL_KINDS = ("embed", "qkv", "attn", "oproj", "gateup", "down", "output")
+
+    def profile_step(self, token: int, pos: int) -> tuple[dict, dict]:
+        """Per-kernel-kind device ms and launch counts of one eagerly launched step."""
+        ms = (C.c_double * 7)()
+        n = (C.c_uint32 * 7)()
+        _lib.check(_lib.load().talos_profile_step(self.h, int(token), int(pos), ms, n))
+        return ({k: ms[i] for i, k in enumerate(self.KERNEL_KINDS)},
+                {k: int(n[i]) for i, k in enumerate(self.KERNEL_KINDS)})
+
+    def cap_context(self, max_ctx: int):
+        _lib.check(_lib.load().talos_cap_context(self.h, int(max_ctx)))
+        self.cfg.context_length = min(self.cfg.context_length, max(int(max_ctx), 1))
+
+    def matvec_resident(self, name: str, raw, gtype: int, x, rows: int, cols: int) -> np.ndarray:
+        buf = np.ascontiguousarray(np.frombuffer(raw, np.uint8) if not isinstance(raw, np.ndarray) else raw.view(np.uint8))
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.empty(rows, np.float32)
+        _lib.check(_lib.load().talos_matvec_resident(self.h, name.encode(), gtype, _ptr(buf), buf.nbytes,
+                                                     rows, cols, _ptr(x), _ptr(y)))
+        return y
+
+
+class Model:
+    """``Model`` (src/model/llama.rs:20-238) with the CUDA backend."""
+
+    def __init__(self, gguf: GgufFile, device: int = 0, tp_size: int = 1, tp_rank: int = 0,
+                 nccl_id: bytes | None = None, max_ctx: int | None = None):
+        cfg = Config.from_gguf(gguf)
+        if cfg.n_head_kv == 0 or cfg.n_head % cfg.n_head_kv != 0:
+            raise GgufError(f"head_count {cfg.n_head} must be a positive multiple of head_count_kv "
+                            f"{cfg.n_head_kv}")
+        if max_ctx is not None:
+            cfg.context_length = min(cfg.context_length, max(int(max_ctx), 1))
+        self.cfg = cfg
+        self.gguf = gguf
+        self.ctx = Context(cfg, device, tp_size, tp_rank, nccl_id)
+        for name, (rows, cols) in weight_shapes(cfg).items():
+            if rows == 1:
+                data = gguf.tensor_f32(name)
+                self.ctx.upload(name, data, F32, 1, cols)
+            else:
+                raw, gtype = gguf.tensor_raw(name)
+                self.ctx.upload(name, raw, gtype, rows, cols)
+
+    @classmethod
+    def load(cls, path: str, **kw) -> "Model":
+        return cls(GgufFile.open(path), **kw)
+
+    @classmethod
+    def load_bytes(cls, data: bytes, **kw) -> "Model":
+        return cls(GgufFile.from_bytes(data), **kw)
+
+    def close(self):
+        self.ctx.close()
+
+    def cap_context(self, max_ctx: int):
+        """llama.rs:69-81"""
+        self.ctx.cap_context(max_ctx)
+        self.cfg.context_length = self.ctx.cfg.context_length
+
+    def forward_gpu(self, token: int, pos: int) -> np.ndarray:
+        """llama.rs:188-195"""
+        return self.ctx.forward(token, pos)
+
+    def forward_hidden_gpu(self, token: int, pos: int) -> np.ndarray:
+        """llama.rs:199-206"""
+        return self.ctx.forward_hidden(token, pos)
+
+    def step(self, token: int, pos: int) -> np.ndarray:
+        """llama.rs:211-220 (CUDA build: always the GPU forward)."""
+        return self.forward_gpu(token, pos)
+
+    def step_hidden(self, token: int, pos: int) -> np.ndarray:
+        """llama.rs:224-233"""
+        return self.forward_hidden_gpu(token, pos)
+
+    def reset(self):
+        """llama.rs:236-238"""
+        self.ctx.reset()
+
+    def generate_greedy(self, token: int, pos: int, n: int) -> np.ndarray:
+        return self.ctx.generate_greedy(token, pos, n)
+
+    def prefill(self, tokens, pos0: int = 0):
+        return self.ctx.prefill(tokens, pos0)
+
+
+# ----------------------------------------------------------------- kernel entry points
+
+def dequant(gtype: int, raw, n_elems: int) -> np.ndarray:
+    """talos_dequant: GgmlType::dequantize on the GPU (bit-exact)."""
+    buf = np.ascontiguousarray(np.frombuffer(raw, np.uint8) if not isinstance(raw, np.ndarray) else raw.view(np.uint8))
+    out = np.empty(n_elems, np.float32)
+    _lib.check(_lib.load().talos_dequant(gtype, _ptr(buf), n_elems, _ptr(out)))
+    return out
+
+
+def matvec(gtype: int, raw, x, rows: int, cols: int, device: int = 0) -> np.ndarray:
+    """talos_matvec: one fused dequant-matvec (math::metal::matvec_quant twin)."""
+    buf = np.ascontiguousarray(np.frombuffer(raw, np.uint8) if not isinstance(raw, np.ndarray) else raw.view(np.uint8))
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty(rows, np.float32)
+    _lib.check(_lib.load().talos_matvec(device, gtype, _ptr(buf), buf.nbytes, rows, cols, _ptr(x), _ptr(y)))
+    return y
+
+
+class Weight:
+    """A packed weight on one device, for device-pointer matvecs (benchmarks)."""
+
+    def __init__(self, gtype: int, raw, rows: int, cols: int, device: int = 0):
+        buf = np.ascontiguousarray(np.frombuffer(raw, np.uint8) if not isinstance(raw, np.ndarray) else raw.view(np.uint8))
+        h = C.c_void_p()
+        _lib.check(_lib.load().talos_weight_create(device, gtype, _ptr(buf), buf.nbytes, rows, cols, C.byref(h)))
+        self.h = h
+        self.rows, self.cols, self.gtype = rows, cols, gtype
+
+    def packed_bytes(self) -> int:
+        n = C.c_size_t()
+        _lib.check(_lib.load().talos_weight_packed_bytes(self.h, C.byref(n)))
+        return n.value
+
+    def matvec_dev(self, x_ptr: int, y_ptr: int, stream: int = 0):
+        _lib.check(_lib.load().talos_matvec_dev(self.h, C.c_void_p(x_ptr), C.c_void_p(y_ptr), C.c_void_p(stream)))
+
+    def close(self):
+        if getattr(self, "h", None):
+            _lib.load().talos_weight_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
