@@ -379,6 +379,10 @@ extern "C" talos_status talos_ctx_create(const talos_cfg* cfg, int device, talos
         return set_err(TALOS_ERR_INVALID_ARG, "zero-sized model dimension");
     if (cfg->n_embd % cfg->n_head)
         return set_err(TALOS_ERR_UNSUPPORTED, "n_embd %u not a multiple of n_head %u", cfg->n_embd, cfg->n_head);
+    // Every matvec stages its whole input vector in shared memory (4 B/element).
+    if (cfg->n_embd > 49152 || cfg->n_ff > 49152)
+        return set_err(TALOS_ERR_UNSUPPORTED, "n_embd %u / n_ff %u above the staged input limit (49152)",
+                       cfg->n_embd, cfg->n_ff);
     uint32_t hd = cfg->n_embd / cfg->n_head;
     if (hd % 2 || hd > 256 || cfg->n_head / cfg->n_head_kv > 8)
         return set_err(TALOS_ERR_UNSUPPORTED, "head_dim %u / group %u outside this build (even, <= 256; <= 8)",
