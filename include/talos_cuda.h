@@ -232,6 +232,16 @@ talos_status talos_weight_packed_bytes(const talos_weight* w, size_t* out);
 talos_status talos_matvec_dev(const talos_weight* w, const float* x_dev, float* y_dev,
                               void* stream);
 
+/*
+ * Benchmark helper: capture `reps` back-to-back talos_matvec_dev launches that
+ * cycle through the n weights ws[0..n-1] (same shape) into one CUDA graph, replay
+ * it once to warm up and once timed with CUDA events, and write the average
+ * device microseconds per launch to *us_per_launch. Host launch overhead is not
+ * in the number. No reference counterpart.
+ */
+talos_status talos_matvec_bench(const talos_weight* const* ws, int n, const float* x_dev,
+                                float* y_dev, int reps, float* us_per_launch);
+
 #ifdef __cplusplus
 }
 #endif

@@ -17,7 +17,7 @@ OUT = os.path.join(PKG, "_lib")
 CUDA_LIB = os.path.join(OUT, "libtalos_cuda.so")
 SYNTH_LIB = os.path.join(OUT, "libtalos_synth.so")
 
-CU_SOURCES = ["kernels.cu", "runtime.cu"]
+CU_SOURCES = ["kernels.cu", "matvec.cu", "runtime.cu"]
 CU_DEPS = CU_SOURCES + ["common.cuh", "kernels.cuh"]
 
 NVCC_FLAGS = [

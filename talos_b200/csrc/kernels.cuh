@@ -55,10 +55,13 @@ struct MatvecArgs {
 
 // Tiles in a segment for a weight of `rows` rows.
 inline int seg_tiles(int rows, int pair) { return pair ? (rows + 7) / 8 : (rows + 15) / 16; }
-cudaError_t launch_matvec(const MatvecArgs& a, int type, int max_ctas, cudaStream_t s);
+// pdl: launch with programmatic stream serialization (the kernel streams its
+// weights before waiting on the previous kernel of the stream).
+cudaError_t launch_matvec(const MatvecArgs& a, int type, int max_ctas, cudaStream_t s, bool pdl);
 size_t matvec_smem_bytes(int type, int K);
 cudaError_t matvec_configure();  // opt-in shared memory limits, once per process
 int matvec_ctas_per_sm(int type, int K);
+int matvec_max_k(int type);      // largest input length the staged activation fits
 
 // ---------------------------------------------------------------- attention
 
@@ -67,23 +70,23 @@ struct AttnArgs {
     const float* kc;    // [ctx][kv_dim] this layer
     const float* vc;
     float* out;         // [n_head * hd]
-    float* part;        // [n_head][nsplit][hd + 2] work area
-    unsigned* counters; // [n_kv], zero between launches
     StepParams* step;
-    int n_head, n_kv, hd, kv_dim, nsplit;
+    int n_head, n_kv, hd, kv_dim;
     float scale;
 };
-cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
+cudaError_t attention_configure();
+size_t attention_smem_bytes(int hd, int group);
 
 // ---------------------------------------------------------------- small kernels
 
 // x = dequant(token_embd row step->token); also clears step->argmax_key.
 cudaError_t launch_embed(const uint8_t* embd_raw, int type, int cols, int vocab, StepParams* step,
-                         float* x, cudaStream_t s);
+                         float* x, cudaStream_t s, bool pdl);
 // out = rmsnorm(x, w)
 cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, float* out,
-                           cudaStream_t s);
+                           cudaStream_t s, bool pdl);
 // Greedy feedback: token = argmax, append it to gen[], pos += 1.
-cudaError_t launch_greedy_advance(StepParams* step, uint32_t* gen, int gen_cap, cudaStream_t s);
+cudaError_t launch_greedy_advance(StepParams* step, uint32_t* gen, int gen_cap, cudaStream_t s, bool pdl);
 
 }  // namespace talos

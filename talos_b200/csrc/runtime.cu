@@ -175,7 +175,10 @@ static talos_status device_setup(int device) {
     CK(cudaGetDeviceCount(&n));
     if (device < 0 || device >= n) return set_err(TALOS_ERR_INVALID_ARG, "device %d of %d", device, n);
     CK(cudaSetDevice(device));
-    std::call_once(g_cfg_once, [] { g_cfg_err = matvec_configure(); });
+    std::call_once(g_cfg_once, [] {
+        g_cfg_err = matvec_configure();
+        if (g_cfg_err == cudaSuccess) g_cfg_err = attention_configure();
+    });
     if (g_cfg_err != cudaSuccess) return set_err(TALOS_ERR_CUDA, "matvec_configure: %s", cudaGetErrorString(g_cfg_err));
     if (device < 64 && g_sms[device] == 0) {
         int sms = 0;
@@ -214,11 +217,8 @@ struct talos_ctx {
     void* arena = nullptr;
     size_t arena_bytes = 0;
     float *x = nullptr, *q = nullptr, *att = nullptr, *ff = nullptr, *logits = nullptr, *hidden = nullptr;
-    float* attn_part = nullptr;
-    unsigned* attn_counters = nullptr;
     StepParams* step = nullptr;
     uint32_t* gen = nullptr;
-    int nsplit = 1;
     // KV + RoPE table
     float* kcache = nullptr;
     float* vcache = nullptr;
@@ -333,12 +333,6 @@ static talos_status alloc_kv(talos_ctx* c) {
 
 static talos_status alloc_arena(talos_ctx* c) {
     const size_t E = c->cfg.n_embd, F = c->cfg.n_ff, V = c->cfg.vocab_size;
-    const size_t NH = c->cfg.n_head;
-    int sms = g_sms[c->device] ? g_sms[c->device] : 148;
-    int ns = (2 * sms + (int)c->cfg.n_head_kv - 1) / (int)c->cfg.n_head_kv;
-    if (ns > 64) ns = 64;
-    if (ns < 1) ns = 1;
-    c->nsplit = ns;
     size_t off = 0;
     auto take = [&](size_t bytes) {
         size_t o = off;
@@ -346,9 +340,7 @@ static talos_status alloc_arena(talos_ctx* c) {
         return o;
     };
     size_t o_x = take(E * 4), o_q = take(E * 4 + 64), o_att = take(E * 4), o_ff = take(F * 4),
-           o_log = take(V * 4), o_hid = take(E * 4),
-           o_part = take(NH * (size_t)ns * (c->hd + 2) * 4), o_cnt = take(c->cfg.n_head_kv * 4),
-           o_step = take(sizeof(StepParams));
+           o_log = take(V * 4), o_hid = take(E * 4), o_step = take(sizeof(StepParams));
     CK(cudaMalloc(&c->arena, off));
     CK(cudaMemsetAsync(c->arena, 0, off, c->stream));
     c->arena_bytes = off;
@@ -359,8 +351,6 @@ static talos_status alloc_arena(talos_ctx* c) {
     c->ff = (float*)(b + o_ff);
     c->logits = (float*)(b + o_log);
     c->hidden = (float*)(b + o_hid);
-    c->attn_part = (float*)(b + o_part);
-    c->attn_counters = (unsigned*)(b + o_cnt);
     c->step = (StepParams*)(b + o_step);
     CK(cudaMallocHost(&c->h_out, (V > E ? V : E) * sizeof(float)));
     CK(cudaMallocHost(&c->h_step, sizeof(StepParams)));
@@ -380,13 +370,18 @@ extern "C" talos_status talos_ctx_create(const talos_cfg* cfg, int device, talos
     if (cfg->n_embd % cfg->n_head)
         return set_err(TALOS_ERR_UNSUPPORTED, "n_embd %u not a multiple of n_head %u", cfg->n_embd, cfg->n_head);
     // Every matvec stages its whole input vector in shared memory (4 B/element).
-    if (cfg->n_embd > 49152 || cfg->n_ff > 49152)
-        return set_err(TALOS_ERR_UNSUPPORTED, "n_embd %u / n_ff %u above the staged input limit (49152)",
-                       cfg->n_embd, cfg->n_ff);
+    int kmax = matvec_max_k(GT_Q8_0);
+    for (int t : {(int)GT_F32, (int)GT_Q4_0, (int)GT_Q6_K})
+        if (matvec_max_k(t) < kmax) kmax = matvec_max_k(t);
+    if ((int)cfg->n_embd > kmax || (int)cfg->n_ff > kmax)
+        return set_err(TALOS_ERR_UNSUPPORTED, "n_embd %u / n_ff %u above the staged input limit (%d)",
+                       cfg->n_embd, cfg->n_ff, kmax);
     uint32_t hd = cfg->n_embd / cfg->n_head;
-    if (hd % 2 || hd > 256 || cfg->n_head / cfg->n_head_kv > 8)
-        return set_err(TALOS_ERR_UNSUPPORTED, "head_dim %u / group %u outside this build (even, <= 256; <= 8)",
-                       hd, cfg->n_head / cfg->n_head_kv);
+    const uint32_t grp = cfg->n_head / cfg->n_head_kv;
+    if (hd % 4 || hd > 256 || grp > 8 || grp * hd / 4 > 256)
+        return set_err(TALOS_ERR_UNSUPPORTED,
+                       "head_dim %u / group %u outside this build (head_dim a multiple of 4, <= 256; "
+                       "group <= 8; group * head_dim <= 1024)", hd, grp);
     TRY(device_setup(device));
     std::unique_ptr<talos_ctx> c(new talos_ctx());
     c->cfg = *cfg;
@@ -545,7 +540,7 @@ static Seg make_seg(const DevTensor* A, const DevTensor* B, int pair, float* out
 static talos_status run_mv(talos_ctx* c, MatvecArgs& a, int type) {
     a.ntiles = 0;
     for (int i = 0; i < a.nseg; ++i) a.ntiles += a.seg[i].ntiles;
-    cudaError_t e = launch_matvec(a, type, max_ctas(c->device, type, a.K), c->stream);
+    cudaError_t e = launch_matvec(a, type, max_ctas(c->device, type, a.K), c->stream, true);
     if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "matvec launch: %s", cudaGetErrorString(e));
     return TALOS_OK;
 }
@@ -567,7 +562,7 @@ static talos_status enqueue_step(talos_ctx* c, GraphMode mode) {
     cudaStream_t s = c->stream;
     const DevTensor& embd = c->w["token_embd.weight"];
     TRY(mark(c, -1));
-    cudaError_t e = launch_embed((const uint8_t*)embd.mem, embd.type, E, (int)cfg.vocab_size, c->step, c->x, s);
+    cudaError_t e = launch_embed((const uint8_t*)embd.mem, embd.type, E, (int)cfg.vocab_size, c->step, c->x, s, true);
     if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "embed: %s", cudaGetErrorString(e));
     TRY(mark(c, TALOS_K_EMBED));
     const size_t kv_layer = c->kv_ctx * (size_t)c->kv_dim;
@@ -610,16 +605,13 @@ static talos_status enqueue_step(talos_ctx* c, GraphMode mode) {
             a.kc = kc;
             a.vc = vc;
             a.out = c->att;
-            a.part = c->attn_part;
-            a.counters = c->attn_counters;
             a.step = c->step;
             a.n_head = (int)cfg.n_head;
             a.n_kv = (int)cfg.n_head_kv;
             a.hd = c->hd;
             a.kv_dim = c->kv_dim;
-            a.nsplit = c->nsplit;
             a.scale = 1.0f / sqrtf((float)c->hd);
-            e = launch_attention(a, s);
+            e = launch_attention(a, s, true);
             if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "attention: %s", cudaGetErrorString(e));
             TRY(mark(c, TALOS_K_ATTN));
         }
@@ -661,7 +653,7 @@ static talos_status enqueue_step(talos_ctx* c, GraphMode mode) {
     }
     const DevTensor& onorm = c->w["output_norm.weight"];
     if (mode == GM_HIDDEN) {
-        e = launch_rmsnorm(c->x, (const float*)onorm.mem, cfg.rms_eps, E, c->hidden, s);
+        e = launch_rmsnorm(c->x, (const float*)onorm.mem, cfg.rms_eps, E, c->hidden, s, true);
         if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "rmsnorm: %s", cudaGetErrorString(e));
         return TALOS_OK;
     }
@@ -680,7 +672,7 @@ static talos_status enqueue_step(talos_ctx* c, GraphMode mode) {
         TRY(mark(c, TALOS_K_OUTPUT));
     }
     if (mode == GM_GREEDY) {
-        e = launch_greedy_advance(c->step, c->gen, (int)c->kv_ctx + 1, s);
+        e = launch_greedy_advance(c->step, c->gen, (int)c->kv_ctx + 1, s, true);
         if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "greedy advance: %s", cudaGetErrorString(e));
     }
     return TALOS_OK;
@@ -890,7 +882,7 @@ static talos_status matvec_on(const DevTensor& t, int device, const float* x_dev
     a.seg[0] = sg;
     a.nseg = 1;
     a.ntiles = sg.ntiles;
-    cudaError_t e = launch_matvec(a, t.type, max_ctas(device, t.type, a.K), s);
+    cudaError_t e = launch_matvec(a, t.type, max_ctas(device, t.type, a.K), s, false);
     if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "matvec launch: %s", cudaGetErrorString(e));
     return TALOS_OK;
 }
@@ -899,11 +891,9 @@ static talos_status check_matrix(int type, size_t len, size_t rows, size_t cols)
     size_t want = raw_len(type, rows, cols);
     if (!want) return set_err(TALOS_ERR_UNSUPPORTED, "ggml type %d with %zu cols", type, cols);
     if (len != want) return set_err(TALOS_ERR_INVALID_ARG, "%zu bytes, expected %zu for [%zu, %zu]", len, want, rows, cols);
-    if (type == GT_Q4_0 || type == GT_Q8_0 || type == GT_Q6_K || type == GT_F32) {
-        size_t KP = type == GT_Q4_0 ? ((cols / 32 + 3) / 4) * 128 : cols;
-        if (KP * 4 + 1024 > 200 * 1024)
-            return set_err(TALOS_ERR_UNSUPPORTED, "cols %zu exceed the staged input limit", cols);
-    }
+    if (cols > (size_t)matvec_max_k(type))
+        return set_err(TALOS_ERR_UNSUPPORTED, "cols %zu exceed the staged input limit (%d)", cols,
+                       matvec_max_k(type));
     return TALOS_OK;
 }
 
@@ -941,6 +931,47 @@ extern "C" talos_status talos_matvec_dev(const talos_weight* w, const float* x_d
     if (!w || !x_dev || !y_dev) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
     CK(cudaSetDevice(w->device));
     return matvec_on(w->t, w->device, x_dev, y_dev, (cudaStream_t)stream);
+}
+
+extern "C" talos_status talos_matvec_bench(const talos_weight* const* ws, int n, const float* x_dev, float* y_dev,
+                                           int reps, float* us_per_launch) {
+    if (!ws || n <= 0 || !x_dev || !y_dev || reps <= 0 || !us_per_launch)
+        return set_err(TALOS_ERR_INVALID_ARG, "bad argument");
+    for (int i = 0; i < n; ++i)
+        if (!ws[i] || ws[i]->device != ws[0]->device || ws[i]->t.rows != ws[0]->t.rows ||
+            ws[i]->t.cols != ws[0]->t.cols || ws[i]->t.type != ws[0]->t.type)
+            return set_err(TALOS_ERR_INVALID_ARG, "weights differ in device, shape or type");
+    CK(cudaSetDevice(ws[0]->device));
+    cudaStream_t s = nullptr;
+    CK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    talos_status st = TALOS_OK;
+    cudaError_t e = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+    for (int i = 0; e == cudaSuccess && st == TALOS_OK && i < reps; ++i)
+        st = matvec_on(ws[i % n]->t, ws[0]->device, x_dev, y_dev, s);
+    cudaError_t e_end = cudaStreamEndCapture(s, &g);
+    if (e == cudaSuccess) e = e_end;
+    if (st == TALOS_OK && e == cudaSuccess) e = cudaGraphInstantiate(&ge, g, 0);
+    if (st == TALOS_OK && e == cudaSuccess) e = cudaEventCreate(&e0);
+    if (st == TALOS_OK && e == cudaSuccess) e = cudaEventCreate(&e1);
+    if (st == TALOS_OK && e == cudaSuccess) e = cudaGraphLaunch(ge, s);  // warm-up replay
+    if (st == TALOS_OK && e == cudaSuccess) e = cudaEventRecord(e0, s);
+    if (st == TALOS_OK && e == cudaSuccess) e = cudaGraphLaunch(ge, s);
+    if (st == TALOS_OK && e == cudaSuccess) e = cudaEventRecord(e1, s);
+    if (st == TALOS_OK && e == cudaSuccess) e = cudaEventSynchronize(e1);
+    float ms = 0.f;
+    if (st == TALOS_OK && e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (ge) cudaGraphExecDestroy(ge);
+    if (g) cudaGraphDestroy(g);
+    cudaStreamDestroy(s);
+    if (st != TALOS_OK) return st;
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "matvec bench: %s", cudaGetErrorString(e));
+    *us_per_launch = ms * 1000.f / (float)reps;
+    return TALOS_OK;
 }
 
 static talos_status matvec_host(const DevTensor& t, int device, const float* x, float* y, cudaStream_t s) {

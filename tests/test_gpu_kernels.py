@@ -30,7 +30,9 @@ def random_blocks(gtype, n, rng, scale_lo=-0.05, scale_hi=0.05):
     raw = rng.integers(0, 256, n // be * bb, dtype=np.uint8)
     off = 208 if gtype == gguf.Q6_K else 0
     d = rng.uniform(scale_lo, scale_hi, n // be).astype(np.float16)
-    d[:3] = np.array([0.0, 6e-8, -6.1e-5], np.float16)  # zero and subnormal scales
+    special = np.array([0.0, 6e-8, -6.1e-5], np.float16)  # zero and subnormal scales
+    k = min(3, d.size - 1)
+    d[:k] = special[:k]
     for i, v in enumerate(d):
         raw[i * bb + off:i * bb + off + 2] = np.frombuffer(v.tobytes(), np.uint8)
     return raw
