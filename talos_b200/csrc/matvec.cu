@@ -324,19 +324,18 @@ constexpr int MV_CWARPS = MV_CONSUMERS / 32;
 constexpr int MV_THREADS = MV_CONSUMERS + 64;  // + 1 producer warp + 1 epilogue warp
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 
-// D = A(16x16 f16) * B(16x8 f16), f32 accumulate from zero / from d.
+// D = A(16x16 f16) * B(16x8 f16), f32 accumulate from zero / from d. Not
+// volatile: the MMAs of independent blocks may be scheduled around each other.
 __device__ __forceinline__ void mma_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                       uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%10,%10,%10,%10};"
         : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
 }
 __device__ __forceinline__ void mma_acc(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                         uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -712,6 +711,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const __grid_constant_
     float scale = 1.f;
     if (a.norm_w) {  // RMSNorm (src/math/ops.rs:5-12)
         float ss = 0.f;
+#pragma unroll 8
         for (int k = tid; k < K; k += MV_CONSUMERS) {
             const float v = a.x[k];
             ss = fmaf(v, v, ss);
@@ -740,6 +740,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const __grid_constant_
         half* xh = (half*)stage_x;
         const int s16 = lane >> 4, r16 = lane & 15;
         const int m = 2 * s16 + (r16 >> 3), t = (r16 & 7) >> 1, hp = r16 & 1;
+#pragma unroll 4
         for (int j = warp; j < KP / 32; j += MV_CWARPS) {
             const float v = xin(32 * j + lane);
             if (TYPE == GT_F32) {
