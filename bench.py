@@ -142,9 +142,10 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
-def profiled_traffic():
-    """DRAM bytes per launch of the gate/up kernel from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "gateup_q4_0_m7b.md")
+def profiled_traffic(summary: str):
+    """DRAM bytes per launch of the dominant kernel from its committed ncu summary
+    (the `traffic_bytes_per_launch:` line of profiles/<summary>)."""
+    p = os.path.join(ROOT, "profiles", summary)
     try:
         for line in open(p):
             if line.startswith("traffic_bytes_per_launch:"):
@@ -330,14 +331,26 @@ def main():
             for k in tot_ms:
                 tot_ms[k] += ms_k[k]
                 tot_n[k] += n_k[k]
-    gu_ms = tot_ms["gateup"] / max(tot_n["gateup"], 1)
     peak, peak_kind = measured_peaks()
-    achieved = GATEUP_BYTES / (gu_ms / 1000.0) / 1e9
-    traffic = profiled_traffic()
+    step_kernel = ctx.step_kernel()
     step_ms = sum(tot_ms.values()) / n_prof
-    breakdown = {k: {"ms_per_step": tot_ms[k] / n_prof, "launches_per_step": tot_n[k] // n_prof}
+    breakdown = {k: {"ms_per_step": tot_ms[k] / n_prof, "count_per_step": tot_n[k] // n_prof}
                  for k in tot_ms}
-    launches = sum(tot_n.values()) // n_prof + 1  # + the greedy-advance kernel
+    if step_kernel == "fused":
+        # the dominant (only) kernel is k_token: one launch = one whole token
+        prof_pos = PROMPT_LEN + W + (n_prof - 1) / 2
+        dom_bytes = W_BYTES_7B + KV_BYTES_PER_POS * (prof_pos + 1)
+        dom_ms = step_ms
+        dom_name = "k_token (whole decode step: 32 layers + output, one launch)"
+        traffic = profiled_traffic("k_token_m7b.md")
+        launches = 2  # k_token + the greedy-advance kernel
+    else:
+        dom_bytes = GATEUP_BYTES
+        dom_ms = tot_ms["gateup"] / max(tot_n["gateup"], 1)
+        dom_name = "gateup (RMSNorm + gate/up Q4_0 matvec + SwiGLU)"
+        traffic = profiled_traffic("gateup_q4_0_m7b.md")
+        launches = sum(tot_n.values()) // n_prof + 1  # + the greedy-advance kernel
+    achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
 
     # ---------------- CPU baseline (rank 0 at N=1 only)
     cpu = None
@@ -359,13 +372,13 @@ def main():
                    "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
                    "l2": "inputs larger than L2 (4.03 GB of weights per step)"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 24, "d2h_bytes_per_step": vocab * 4 + 24},
-        "roofline": {"bound": "hbm", "kernel": "gateup (RMSNorm + gate/up Q4_0 matvec + SwiGLU)",
+        "roofline": {"bound": "hbm", "kernel": dom_name,
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, "traffic": traffic, "bytes_per_launch": GATEUP_BYTES,
-                     "ms_per_launch": gu_ms},
+                     "peak_kind": peak_kind, "traffic": traffic, "bytes_per_launch": dom_bytes,
+                     "ms_per_launch": dom_ms},
         "token_roofline": {"bytes_per_token": tok_bytes, "achieved_gbs": tok_bytes / (ms_step / 1000) / 1e9,
                            "frac": tok_bytes / (ms_step / 1000) / 1e9 / peak, "peak_kind": peak_kind},
-        "kernels": breakdown, "eager_step_ms": step_ms,
+        "step_kernel": step_kernel, "parts": breakdown, "profiled_step_ms": step_ms,
         "gpu_launches": launches * K,
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,

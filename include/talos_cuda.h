@@ -107,6 +107,23 @@ talos_status talos_ctx_destroy(talos_ctx* ctx);
 talos_status talos_weight_upload(talos_ctx* ctx, const char* name, const void* bytes, size_t len,
                                  int ggml_type, size_t rows, size_t cols);
 
+/*
+ * How a decode step is launched. TALOS_STEP_FUSED: one persistent kernel per
+ * token runs every layer, with grid-wide barriers between the phases and the
+ * weight stream running on across them. TALOS_STEP_LAYERED: a graph of about
+ * five kernels per layer. TALOS_STEP_AUTO (the default): FUSED when the model
+ * fits it (q/k/v of a layer share a ggml type, head_dim <= 128,
+ * n_embd <= 8192), else LAYERED. Both give the same results within the parity
+ * bars, each bit-identical run to run. No reference counterpart (the Metal path
+ * encodes one command buffer per token, src/math/metal/mod.rs:414-513).
+ * talos_ctx_step_kernel reports what the next step will run (FUSED or
+ * LAYERED); with FUSED requested for a model it cannot run, the next step fails
+ * with TALOS_ERR_UNSUPPORTED.
+ */
+enum { TALOS_STEP_AUTO = 0, TALOS_STEP_FUSED = 1, TALOS_STEP_LAYERED = 2 };
+talos_status talos_ctx_set_step_kernel(talos_ctx* ctx, int kind);
+talos_status talos_ctx_step_kernel(talos_ctx* ctx, int* kind_out);
+
 /* Bytes of device memory the context holds (weights + KV cache + work areas). */
 talos_status talos_ctx_device_bytes(talos_ctx* ctx, size_t* out);
 
@@ -170,12 +187,14 @@ talos_status talos_prefill(talos_ctx* ctx, const uint32_t* tokens, size_t n, siz
                            float* last_logits);
 
 /*
- * Run one decode step (as talos_forward, logits stay on the GPU) launching its
- * kernels one by one with CUDA events between them, and add each kernel's
- * device time in milliseconds into kernel_ms[kind] and its launch count into
- * launches[kind] (either may be NULL), kind = talos_kernel_kind. For
- * benchmarks: the per-kernel durations of the graph the step normally replays.
- * No reference counterpart.
+ * Run one decode step (as talos_forward, logits stay on the GPU) and add the
+ * device time in milliseconds of each part of it into kernel_ms[kind] and the
+ * number of such parts into launches[kind] (either may be NULL), kind =
+ * talos_kernel_kind. LAYERED steps launch their kernels one by one with CUDA
+ * events between them. FUSED steps run the per-token kernel once with phase
+ * time stamps (the device's global timer, read by CTA 0 as it passes each
+ * grid barrier); the last phase also carries the launch and drain time. For
+ * benchmarks. No reference counterpart.
  */
 enum talos_kernel_kind {
     TALOS_K_EMBED = 0,  /* token embedding row dequant */
@@ -189,6 +208,20 @@ enum talos_kernel_kind {
 };
 talos_status talos_profile_step(talos_ctx* ctx, uint32_t token, size_t pos, double* kernel_ms,
                                 uint32_t* launches);
+
+/*
+ * Run one decode step of the per-token kernel with profiling stamps and copy
+ * them to `out` (host): for phase p (in step order: per layer q/k/v,
+ * attention, o-proj, gate/up, down; then the output phase) and CTA c, four
+ * device global-timer values in ns at out[(p * n_cta + c) * 4 + k]: k = 0 the
+ * CTA entered the phase, 1 its inputs were staged, 2 its compute finished,
+ * 3 it arrived at the phase's barrier (0 where a stamp does not apply). `cap`
+ * is the length of `out` in elements; *n_phase and *n_cta receive the
+ * dimensions. TALOS_ERR_UNSUPPORTED when steps run the layered graph. For
+ * benchmarks; no reference counterpart.
+ */
+talos_status talos_profile_phases(talos_ctx* ctx, uint32_t token, size_t pos, uint64_t* out, size_t cap,
+                                  int* n_phase, int* n_cta);
 
 /* ------------------------------------------------------------ kernels */
 

@@ -11,6 +11,7 @@ import os
 from .build import CUDA_LIB
 
 OK, INVALID_ARG, OOM, CUDA, NCCL, TIMEOUT, OOB, STATE, UNSUPPORTED = range(9)
+STEP_AUTO, STEP_FUSED, STEP_LAYERED = range(3)
 STATUS_NAMES = ["OK", "INVALID_ARG", "OOM", "CUDA", "NCCL", "TIMEOUT", "OOB", "STATE", "UNSUPPORTED"]
 
 
@@ -38,6 +39,8 @@ SIGNATURES = {
     "talos_nccl_unique_id": (_i, [_vp]),
     "talos_ctx_destroy": (_i, [_vp]),
     "talos_weight_upload": (_i, [_vp, C.c_char_p, _vp, _sz, _i, _sz, _sz]),
+    "talos_ctx_set_step_kernel": (_i, [_vp, _i]),
+    "talos_ctx_step_kernel": (_i, [_vp, C.POINTER(_i)]),
     "talos_ctx_device_bytes": (_i, [_vp, C.POINTER(_sz)]),
     "talos_ctx_stream": (_i, [_vp, C.POINTER(_vp)]),
     "talos_cap_context": (_i, [_vp, _sz]),
@@ -47,6 +50,7 @@ SIGNATURES = {
     "talos_generate_greedy": (_i, [_vp, _u32, _sz, _sz, _vp]),
     "talos_prefill": (_i, [_vp, _vp, _sz, _sz, _vp]),
     "talos_profile_step": (_i, [_vp, _u32, _sz, _vp, _vp]),
+    "talos_profile_phases": (_i, [_vp, _u32, _sz, _vp, _sz, C.POINTER(_i), C.POINTER(_i)]),
     "talos_dequant": (_i, [_i, _vp, _sz, _vp]),
     "talos_matvec": (_i, [_i, _i, _vp, _sz, _sz, _sz, _vp, _vp]),
     "talos_matvec_resident": (_i, [_vp, C.c_char_p, _i, _vp, _sz, _sz, _sz, _vp, _vp]),

@@ -117,4 +117,54 @@ __device__ __forceinline__ uint32_t total_order_key(float f) {
     return (uint32_t)b ^ 0x80000000u;
 }
 
+__device__ __forceinline__ float ld_half_bytes(const uint8_t* p) {
+    return __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
+}
+
+// Element `i` of a tensor stored as raw GGUF blocks, bit-exact with
+// GgmlType::dequantize (src/gguf/dtype.rs:64-121).
+__device__ __forceinline__ float dequant_elem(int type, const uint8_t* raw, size_t i) {
+    switch (type) {
+        case GT_F32: {
+            const uint8_t* p = raw + 4 * i;
+            uint32_t b = p[0] | (p[1] << 8) | (p[2] << 16) | ((uint32_t)p[3] << 24);
+            return __uint_as_float(b);
+        }
+        case GT_Q8_0: {  // dtype.rs:69-78: d * q
+            const uint8_t* b = raw + (i / 32) * 34;
+            return __fmul_rn(ld_half_bytes(b), (float)(int8_t)b[2 + i % 32]);
+        }
+        case GT_Q4_0: {  // dtype.rs:79-91: d * (nibble - 8)
+            const uint8_t* b = raw + (i / 32) * 18;
+            int j = (int)(i % 32);
+            int q = j < 16 ? (b[2 + j] & 0x0F) : (b[2 + j - 16] >> 4);
+            return __fmul_rn(ld_half_bytes(b), (float)(q - 8));
+        }
+        case GT_Q6_K: {  // dtype.rs:93-119: (d * sc) * q
+            const uint8_t* b = raw + (i / 256) * 210;
+            int e = (int)(i % 256);
+            int n = e / 128, r = e % 128;
+            int l = r % 32, j = r / 32;  // element l + 32 j of half n
+            const uint8_t* ql = b + n * 64;
+            const uint8_t* qh = b + 128 + n * 32;
+            const int8_t* sc = (const int8_t*)(b + 192 + n * 8);
+            int lo = (j & 1) ? ql[l + 32] : ql[l];
+            lo = (j & 2) ? (lo >> 4) : (lo & 0xF);
+            int hi = (qh[l] >> (2 * j)) & 3;
+            int q = (lo | (hi << 4)) - 32;
+            float d = ld_half_bytes(b + 208);
+            return __fmul_rn(__fmul_rn(d, (float)sc[l / 16 + 2 * j]), (float)q);
+        }
+    }
+    return 0.f;
+}
+
+// Bytes and elements of one GGUF block of `type`.
+__host__ __device__ inline int gguf_block_bytes(int type) {
+    return type == GT_F32 ? 4 : (type == GT_Q6_K ? 210 : (type == GT_Q8_0 ? 34 : 18));
+}
+__host__ __device__ inline int gguf_block_elems(int type) {
+    return type == GT_F32 ? 1 : (type == GT_Q6_K ? 256 : 32);
+}
+
 }  // namespace talos

@@ -89,4 +89,53 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, flo
 // Greedy feedback: token = argmax, append it to gen[], pos += 1.
 cudaError_t launch_greedy_advance(StepParams* step, uint32_t* gen, int gen_cap, cudaStream_t s, bool pdl);
 
+// ---------------------------------------------------------------- per-token kernel
+//
+// k_token runs a whole decode step in one launch as a list of phases separated
+// by grid barriers (matvec.cu).
+
+enum PhaseKind : int { PH_MATVEC = 0, PH_ATTN = 1, PH_HIDDEN = 2 };
+
+struct TokenPhase {
+    int kind;
+    int type;       // PH_MATVEC: ggml type of every segment
+    int embed_in;   // PH_MATVEC: the input is the token's embedding row (first phase)
+    int prof_kind;  // talos_kernel_kind the phase is reported under
+    MatvecArgs mv;  // PH_MATVEC
+    AttnArgs at;    // PH_ATTN
+};
+
+struct TokenArgs {
+    const TokenPhase* ph;       // device array of nph phases
+    int nph;
+    unsigned long long* bars;   // [nph] arrival counters, never reset
+    unsigned long long* epoch;  // number of completed launches
+    StepParams* step;
+    const uint8_t* embd;        // raw GGUF token_embd rows
+    int embd_type, vocab;
+    float* x;                   // residual stream [E]
+    int E;
+    float* hidden;              // PH_HIDDEN output [E]
+    const float* out_norm;
+    float eps;
+    float* att_part;            // [n_head][nsplit][hd + 2] split-softmax partials
+    unsigned* att_cnt;          // [n_kv] arrivals per kv head (reset by the last one)
+    int nsplit;                 // attention splits per kv head
+    int nst;                    // ring stages
+    int union_bytes;            // staged input / attention scratch bytes
+    unsigned long long* stamps; // optional [nph][grid][4] global-timer stamps (ns): phase
+                                // entered, inputs staged, compute done, barrier arrival
+};
+
+// Staged-input elements the k_token scratch region must hold for input length K.
+int token_stage_elems(int type, int K);
+// Scratch bytes attention needs for `group` heads of `hd` dims and `nsplit` splits.
+int token_attn_bytes(int group, int hd, int nsplit);
+size_t token_smem_bytes(int nst, int union_bytes);
+// Ring stages that fit next to `union_bytes` of scratch (0 if none fit).
+int token_max_stages(int union_bytes);
+cudaError_t token_configure();
+// One CTA per SM; `cooperative` asks the launch to guarantee co-residency.
+cudaError_t launch_token(const TokenArgs& a, int grid, cudaStream_t s, bool cooperative);
+
 }  // namespace talos

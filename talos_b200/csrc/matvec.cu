@@ -555,6 +555,28 @@ __host__ __device__ inline size_t mv_smem_per_k(int KP) { return (size_t)KP * 4 
 // add (src/model/llama.rs:159-161,174-176), SwiGLU of paired gate/up rows
 // (src/math/ops.rs:28-37), q/k RoPE with the KV append (src/math/ops.rs:48-61,
 // src/kv_cache.rs:21-26), or logits with a running argmax (src/sample.rs:7-14).
+// Global inputs of a tile's epilogue, loaded before its partials are ready: the
+// residual row (EPI_ADD, lanes 0-15) and the RoPE (cos, sin) of the lane's pair
+// (EPI_QKV q and k, lanes 0-7).
+struct EpiPre {
+    float xres;
+    float2 cs;
+};
+__device__ __forceinline__ EpiPre epi_prefetch(const MatvecArgs& a, const Seg& sg, int lt, uint32_t pos, int lane) {
+    EpiPre e{0.f, make_float2(1.f, 0.f)};
+    if (a.epi == EPI_ADD) {
+        const int row = 16 * lt + lane;
+        if (lane < 16 && row < sg.out_rows) e.xres = __ldcg(sg.out + row);  // another CTA may have written it
+    } else if (a.epi == EPI_QKV && sg.role != 2 && lane < 8) {
+        const int r0 = 16 * lt + 2 * lane;
+        if (r0 < sg.out_rows) e.cs = a.rope_cs[(size_t)pos * (a.hd >> 1) + ((r0 % a.hd) >> 1)];
+    }
+    return e;
+}
+
+__device__ __forceinline__ void apply_epilogue(const MatvecArgs& a, const Seg& sg, int lt, const float* res,
+                                               uint32_t pos, int lane, const EpiPre& pre);
+
 template <int TYPE>
 __device__ __forceinline__ void epilogue_warp(const MatvecArgs& a, const float* part, float* res, uint64_t* tdone,
                                               uint64_t* tfree, int* s_err) {
@@ -567,6 +589,7 @@ __device__ __forceinline__ void epilogue_warp(const MatvecArgs& a, const float* 
         find_seg(a, t, si, lt);
         const Seg& sg = a.seg[si];
         const int b = n & 1;
+        const EpiPre pre = epi_prefetch(a, sg, lt, pos, lane);
         if (!mbar_wait(&tdone[b], (uint32_t)(n >> 1) & 1)) {
             *s_err = 1;
             if (a.step) atomicOr(&a.step->error, 2u);
@@ -584,7 +607,16 @@ __device__ __forceinline__ void epilogue_warp(const MatvecArgs& a, const float* 
         if (lane == 0) mbar_arrive(&tfree[b]);
         if (lane < 16) res[lane] = v;
         __syncwarp();
+        apply_epilogue(a, sg, lt, res, pos, lane, pre);
+        __syncwarp();
+    }
+}
 
+// The epilogue of one tile: res[0..15] are its 16 row values (8 gate + 8 up rows
+// for SwiGLU); called by all 32 lanes of one warp.
+__device__ __forceinline__ void apply_epilogue(const MatvecArgs& a, const Seg& sg, int lt, const float* res,
+                                               uint32_t pos, int lane, const EpiPre& pre) {
+    {
         if (a.epi == EPI_SWIGLU) {  // src/math/ops.rs:33-37
             if (lane < 8) {
                 const int j = 8 * lt + lane;
@@ -599,8 +631,7 @@ __device__ __forceinline__ void epilogue_warp(const MatvecArgs& a, const float* 
             } else if (lane < 8) {  // RoPE on pairs (2i, 2i+1) (src/math/ops.rs:48-61)
                 const int r0 = 16 * lt + 2 * lane;
                 if (r0 < sg.out_rows) {
-                    const int i = (r0 % a.hd) >> 1;
-                    const float2 cs = a.rope_cs[(size_t)pos * (a.hd >> 1) + i];
+                    const float2 cs = pre.cs;
                     const float x0 = res[2 * lane], x1 = res[2 * lane + 1];
                     const float o0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
                     const float o1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
@@ -614,7 +645,7 @@ __device__ __forceinline__ void epilogue_warp(const MatvecArgs& a, const float* 
             if (lane < 16) {
                 const int row = 16 * lt + lane;
                 if (row < sg.out_rows) {
-                    sg.out[row] = a.epi == EPI_ADD ? __fadd_rn(sg.out[row], res[lane]) : res[lane];
+                    sg.out[row] = a.epi == EPI_ADD ? __fadd_rn(pre.xres, res[lane]) : res[lane];
                     key = ((unsigned long long)total_order_key(res[lane]) << 32) | (unsigned)row;
                 }
             }
@@ -627,7 +658,6 @@ __device__ __forceinline__ void epilogue_warp(const MatvecArgs& a, const float* 
                 if (lane == 0 && key) atomicMax(&a.step->argmax_key, key);
             }
         }
-        __syncwarp();
     }
 }
 
@@ -881,6 +911,715 @@ cudaError_t launch_matvec(const MatvecArgs& a, int type, int max_ctas, cudaStrea
         case GT_Q6_K: return cudaLaunchKernelEx(&cfg, k_matvec<GT_Q6_K>, a);
     }
     return cudaErrorInvalidValue;
+}
+
+// ============================================================================
+// The per-token kernel
+// ============================================================================
+//
+// One launch runs a whole decode step (src/model/llama.rs:96-183, then the
+// logits of :89 or the final norm of :181) as a list of phases: per layer
+// q/k/v -> attention -> o-proj -> gate/up -> down, then the output projection.
+// One CTA per SM with the roles of k_matvec: a producer warp streaming packed
+// weights through a shared-memory ring, 16 consumer warps, an epilogue warp.
+// The producer walks the weights of ALL of the CTA's matvec phases in order, so
+// while the consumers wait for the previous phase to finish grid-wide, the ring
+// is already filling with the next phase's weights; there is no launch, no
+// pipeline fill and no tail between the ~5 L phases of a token.
+//
+// Phase boundaries are grid barriers on 64-bit arrival counters in global
+// memory. When a CTA's outputs of phase p are written (by its epilogue warp, or
+// by its consumers for attention) it fences and adds 1 to bars[p]; the consumers
+// of phase p+1 wait until bars[p] reaches (epoch + 1) * gridDim.x, epoch being
+// the number of earlier launches. Counters are never reset. Every CTA must be
+// resident at once (one CTA per SM); every wait is bounded (2 s) and on expiry
+// the kernel records an error in StepParams::error and leaves.
+//
+// Cross-CTA data (residual stream, q, K/V rows, partials) are read with
+// ld.global.cg (L2), never from a possibly stale L1 line.
+
+constexpr int TK_STAGE = 2 * Fmt<GT_Q4_0>::GCB;  // largest two-group stage of the four formats
+static_assert(2 * Fmt<GT_Q8_0>::GCB <= TK_STAGE && 2 * Fmt<GT_Q6_K>::GCB <= TK_STAGE &&
+                  2 * Fmt<GT_F32>::GCB <= TK_STAGE,
+              "ring stage too small");
+constexpr int TK_NORM_REGS = 16;               // normed-input registers per thread: K <= 16 * 512
+constexpr int TK_MAXG = 8;                     // query heads per kv head in attention
+constexpr int TK_BAR_BYTES = 64 * 8;           // room for the ring's mbarriers (nst <= 30)
+constexpr int TK_TAIL_BYTES = (2 * MV_CWARPS * 16 + 16 + 32) * 4;
+constexpr uint64_t TK_WAIT_NS = 2000000000ull;
+
+__host__ __device__ constexpr int ck_of(int type) {
+    return type == GT_Q4_0 ? Fmt<GT_Q4_0>::CK
+                           : (type == GT_Q8_0 ? Fmt<GT_Q8_0>::CK
+                                              : (type == GT_Q6_K ? Fmt<GT_Q6_K>::CK : Fmt<GT_F32>::CK));
+}
+__host__ __device__ constexpr int gcb_of(int type) {
+    return type == GT_Q4_0 ? Fmt<GT_Q4_0>::GCB
+                           : (type == GT_Q8_0 ? Fmt<GT_Q8_0>::GCB
+                                              : (type == GT_Q6_K ? Fmt<GT_Q6_K>::GCB : Fmt<GT_F32>::GCB));
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_add_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Bounded spin of one thread until *bar >= target.
+__device__ __noinline__ bool grid_wait_one(const unsigned long long* bar, unsigned long long target) {
+    if (ld_acquire_u64(bar) >= target) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        for (int i = 0; i < 16; ++i)
+            if (ld_acquire_u64(bar) >= target) return true;
+        if (globaltimer_ns() - t0 > TK_WAIT_NS) return false;
+    }
+}
+// Bounded spin until the shared counter reaches v.
+__device__ __forceinline__ bool smem_wait_geq(const volatile int* p, int v) {
+    if (*p >= v) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        for (int i = 0; i < 64; ++i)
+            if (*p >= v) return true;
+        if (globaltimer_ns() - t0 > TK_WAIT_NS) return false;
+    }
+}
+__device__ __forceinline__ void bulk_g2s_evict_first(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                                     uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+        "%4;" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+struct TkShared {
+    int err;      // any role gave up on a wait (set at any time)
+    int stop;     // consumer thread 0's snapshot of err at a phase start, read after the sync
+    int started;  // last phase the consumers entered (epilogue warp follows it)
+    int last;     // attention: this CTA merges the splits of its kv head
+};
+
+// Profiling stamps (TokenArgs::stamps): [phase][cta][4] = phase entered,
+// inputs staged, compute done, arrival at the phase's barrier.
+__device__ __forceinline__ void tk_stamp(const TokenArgs& a, int p, int k) {
+    if (a.stamps) a.stamps[((size_t)p * gridDim.x + blockIdx.x) * 4 + k] = globaltimer_ns();
+}
+
+__device__ __forceinline__ void tk_fail(const TokenArgs& a, TkShared* sh, uint32_t code) {
+    *(volatile int*)&sh->err = 1;
+    atomicOr(&a.step->error, code);
+}
+
+// Four consecutive inputs e0 .. e0+3 (e0 % 4 == 0) into the staged layout
+// consume_* reads: f16 hi / lo B fragments per 32-element block (Q4_0's
+// high-nibble slots pre-divided by 16) or plain floats (F32).
+template <int TYPE>
+__device__ __forceinline__ void tk_put4(float* U, int e0, float4 v) {
+    if (TYPE == GT_F32) {
+        *(float4*)(U + e0) = v;
+        return;
+    }
+    const int j = e0 >> 5, k0 = e0 & 31;
+    const int r0 = k0 & 15, mq = 2 * (k0 >> 4) + (r0 >> 3), t0 = (r0 & 7) >> 1;
+    float a0 = v.x, a1 = v.y, a2 = v.z, a3 = v.w;
+    if (TYPE == GT_Q4_0 && (r0 >> 3)) {
+        a0 *= 0.0625f;
+        a1 *= 0.0625f;
+        a2 *= 0.0625f;
+        a3 *= 0.0625f;
+    }
+    uint32_t h01, l01, h23, l23;
+    split_pair(a0, a1, h01, l01);
+    split_pair(a2, a3, h23, l23);
+    uint32_t* xw = (uint32_t*)U;  // one 32-bit word = the (hp 0, hp 1) half pair
+    xw[(j * 8 + t0) * 4 + mq] = h01;
+    xw[(j * 8 + t0 + 1) * 4 + mq] = h23;
+    xw[(j * 8 + 4 + t0) * 4 + mq] = l01;
+    xw[(j * 8 + 4 + t0 + 1) * 4 + mq] = l23;
+}
+
+// Block sums S of the zero-point term: lane l of a warp holds elements 4l..4l+3
+// of a 128-element run, so 8 lanes make a 32-element block (4 a 16-element half).
+template <int TYPE>
+__device__ __forceinline__ void tk_sums(float* xs16, int e0, float4 v, int lane) {
+    if (TYPE == GT_F32) return;
+    float s = (v.x + v.y) + (v.z + v.w);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if (TYPE == GT_Q6_K) {
+        if ((lane & 3) == 0) xs16[e0 >> 4] = s;
+        return;
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    if ((lane & 7) == 0) xs16[e0 >> 5] = s;
+}
+
+// Stage phase P's input for the format TYPE: RMSNorm with P.mv.norm_w when set
+// (src/math/ops.rs:5-12, (x * s) * w), the token's embedding row for the first
+// phase (src/model/weights.rs:57-62). All global loads of a round are issued
+// before any is used (one L2 round trip per round, not one per element).
+constexpr int TK_ROUND = 8;  // 128-element runs per warp and round
+template <int TYPE>
+__device__ __forceinline__ void tk_stage(const TokenArgs& a, const TokenPhase& P, uint32_t tok, float* U, float* red) {
+    const MatvecArgs& m = P.mv;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = m.K, KP = ((K + Fmt<TYPE>::CK - 1) / Fmt<TYPE>::CK) * Fmt<TYPE>::CK, nrun = KP / 128;
+    float* xs16 = U + KP;
+    const uint8_t* erow = nullptr;
+    if (P.embed_in)
+        erow = a.embd + (size_t)tok * (K / gguf_block_elems(a.embd_type)) * gguf_block_bytes(a.embd_type);
+    auto load4 = [&](int e0) -> float4 {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (erow) {
+            float t[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) t[i] = e0 + i < K ? dequant_elem(a.embd_type, erow, e0 + i) : 0.f;
+            v = make_float4(t[0], t[1], t[2], t[3]);
+            if (blockIdx.x == 0 && e0 < K) {  // the residual stream starts as the embedding
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    if (e0 + i < K) a.x[e0 + i] = t[i];
+            }
+        } else if (e0 + 4 <= K && !(K & 3)) {
+            v = __ldcg((const float4*)(m.x + e0));
+        } else {
+            float t[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) t[i] = e0 + i < K ? __ldcg(m.x + e0 + i) : 0.f;
+            v = make_float4(t[0], t[1], t[2], t[3]);
+        }
+        return v;
+    };
+    auto loadw4 = [&](int e0) -> float4 {
+        if (e0 + 4 <= K && !(K & 3)) return __ldg((const float4*)(m.norm_w + e0));
+        float t[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) t[i] = e0 + i < K ? __ldg(m.norm_w + e0 + i) : 0.f;
+        return make_float4(t[0], t[1], t[2], t[3]);
+    };
+    if (m.norm_w) {
+        // the whole input in registers (K <= 16 * 128 * 4 = 8192), one reduction
+        float4 xv[TK_NORM_REGS / 4], wv[TK_NORM_REGS / 4];
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < TK_NORM_REGS / 4; ++i) {
+            const int r = warp + MV_CWARPS * i, e0 = 128 * r + 4 * lane;
+            xv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            wv[i] = xv[i];
+            if (r < nrun) {
+                xv[i] = load4(e0);
+                wv[i] = loadw4(e0);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < TK_NORM_REGS / 4; ++i)
+            ss = fmaf(xv[i].w, xv[i].w, fmaf(xv[i].z, xv[i].z, fmaf(xv[i].y, xv[i].y, fmaf(xv[i].x, xv[i].x, ss))));
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        consumer_sync();
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < MV_CWARPS; ++w) tot += red[w];
+        const float sc = 1.0f / sqrtf(tot / (float)K + m.eps);
+#pragma unroll
+        for (int i = 0; i < TK_NORM_REGS / 4; ++i) {
+            const int r = warp + MV_CWARPS * i, e0 = 128 * r + 4 * lane;
+            if (r < nrun) {
+                const float4 v = make_float4(__fmul_rn(__fmul_rn(xv[i].x, sc), wv[i].x),
+                                             __fmul_rn(__fmul_rn(xv[i].y, sc), wv[i].y),
+                                             __fmul_rn(__fmul_rn(xv[i].z, sc), wv[i].z),
+                                             __fmul_rn(__fmul_rn(xv[i].w, sc), wv[i].w));
+                tk_put4<TYPE>(U, e0, v);
+                tk_sums<TYPE>(xs16, e0, v, lane);
+            }
+        }
+    } else {
+        for (int r0 = 0; r0 < nrun; r0 += MV_CWARPS * TK_ROUND) {
+            float4 xv[TK_ROUND];
+#pragma unroll
+            for (int i = 0; i < TK_ROUND; ++i) {
+                const int r = r0 + warp + MV_CWARPS * i;
+                xv[i] = r < nrun ? load4(128 * r + 4 * lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int i = 0; i < TK_ROUND; ++i) {
+                const int r = r0 + warp + MV_CWARPS * i;
+                if (r < nrun) {
+                    tk_put4<TYPE>(U, 128 * r + 4 * lane, xv[i]);
+                    tk_sums<TYPE>(xs16, 128 * r + 4 * lane, xv[i], lane);
+                }
+            }
+        }
+    }
+    consumer_sync();
+}
+
+// Consumers of one matvec phase: stage the input, then every tile of this CTA.
+template <int TYPE>
+__device__ __noinline__ bool tk_matvec(const TokenArgs& a, const TokenPhase& P, int p, uint32_t tok, uint8_t* ring,
+                                       uint64_t* full, uint64_t* empty, uint64_t* tdone, uint64_t* tfree, float* U,
+                                       float* part, float* red, uint32_t& slot, uint32_t& par, int& ntile) {
+    const MatvecArgs& m = P.mv;
+    if ((int)blockIdx.x >= m.ntiles) return true;  // no tiles here: read nothing
+    tk_stage<TYPE>(a, P, tok, U, red);
+    if (threadIdx.x == 0) tk_stamp(a, p, 1);
+    constexpr int GCB = Fmt<TYPE>::GCB, CK = Fmt<TYPE>::CK;
+    const int nchunk = (m.K + CK - 1) / CK, KP = nchunk * CK;
+    const float* stage_x = U;
+    const float* xs16 = U + KP;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t nst = (uint32_t)a.nst;
+    for (int t = blockIdx.x; t < m.ntiles; t += gridDim.x) {
+        Acc acc = {0.f, 0.f, 0.f, 0.f};
+        for (int c = 0; c < nchunk; ++c) {
+            if (!mbar_wait(&full[slot], par)) return false;
+            const uint8_t* sA = ring + slot * TK_STAGE;
+            const uint8_t* sB = sA + GCB;
+            if (TYPE == GT_Q4_0)
+                consume_q4_0(sA, sB, (const uint4*)stage_x, xs16, c, acc);
+            else if (TYPE == GT_Q8_0)
+                consume_q8_0(sA, sB, (const uint4*)stage_x, xs16, c, acc);
+            else if (TYPE == GT_Q6_K)
+                consume_q6_k(sA, sB, (const uint4*)stage_x, xs16, c, acc);
+            else
+                consume_f32(sA, sB, stage_x, c, acc);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (++slot == nst) {
+                slot = 0;
+                par ^= 1u;
+            }
+        }
+        // hand the tile's partials to the epilogue warp (double-buffered)
+        const int b = ntile & 1;
+        if (!mbar_wait(&tfree[b], ((uint32_t)(ntile >> 1) & 1u) ^ 1u)) return false;
+        float* pb = part + b * MV_CWARPS * 16;
+        if (TYPE == GT_F32) {
+            const float v = warp_sum(acc.pA);
+            if (lane < 16) pb[warp * 16 + lane] = (lane == warp) ? v : 0.f;
+        } else if ((lane & 3) == 0) {
+            pb[warp * 16 + (lane >> 2)] = fmaf(acc.pA, kTwo24, -Zero<TYPE>::z * acc.qA);
+            pb[warp * 16 + 8 + (lane >> 2)] = fmaf(acc.pB, kTwo24, -Zero<TYPE>::z * acc.qB);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tdone[b]);
+        ++ntile;
+    }
+    if (threadIdx.x == 0) tk_stamp(a, p, 2);
+    return true;
+}
+
+// Attention for one (kv head, position split) item per CTA (src/model/llama.rs:
+// 135-155): scores q.k * scale, softmax, sum of p V, as split softmax partials
+// (max m, sum l, unnormalised o) merged across warps, then across the splits of
+// the kv head by the CTA that finishes last.
+__device__ __noinline__ void tk_attention(const TokenArgs& a, const AttnArgs& A, int p, uint32_t pos, float* U,
+                                          TkShared* sh) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nsplit = a.nsplit;
+    if ((int)blockIdx.x >= A.n_kv * nsplit) return;
+    const int kh = blockIdx.x / nsplit, s = blockIdx.x % nsplit;
+    // partial records: {m, l, o[hd]} in global memory, {m, l, pad, pad, o[hd]} in
+    // shared memory (16-byte aligned o for the float4 stores)
+    const int group = A.n_head / A.n_kv, hd = A.hd, hw = hd + 2, hs = hd + 4;
+    const int seq = (int)pos + 1;
+    const int per = (seq + nsplit - 1) / nsplit;
+    const int p0 = s * per, p1 = min(seq, p0 + per);
+    float* qs = U;               // [group][hd]
+    float* ws = U + group * hd;  // [16 warps][group][hd + 4]
+    const float* qsrc = A.q + (size_t)kh * group * hd;
+    for (int i = tid; i < group * hd; i += MV_CONSUMERS) qs[i] = __ldcg(qsrc + i);
+    consumer_sync();
+    if (tid == 0) tk_stamp(a, p, 1);
+
+    const bool act = 4 * lane < hd;
+    float m[TK_MAXG], l[TK_MAXG], o[TK_MAXG][4];
+#pragma unroll
+    for (int g = 0; g < TK_MAXG; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+        o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+    }
+    const size_t hoff = (size_t)kh * hd + 4 * lane;
+    for (int t = p0 + warp; t < p1; t += MV_CWARPS) {
+        float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+        if (act) {
+            kv = __ldcg((const float4*)(A.kc + (size_t)t * A.kv_dim + hoff));
+            vv = __ldcg((const float4*)(A.vc + (size_t)t * A.kv_dim + hoff));
+        }
+#pragma unroll
+        for (int g = 0; g < TK_MAXG; ++g) {
+            if (g < group) {
+                float d = 0.f;
+                if (act) {
+                    const float4 q4 = *(const float4*)(qs + g * hd + 4 * lane);
+                    d = fmaf(q4.x, kv.x, fmaf(q4.y, kv.y, fmaf(q4.z, kv.z, q4.w * kv.w)));
+                }
+                const float sc = warp_sum(d) * A.scale;
+                const float mn = fmaxf(m[g], sc);
+                const float cr = expf(m[g] - mn), pe = expf(sc - mn);
+                l[g] = fmaf(l[g], cr, pe);
+                o[g][0] = fmaf(o[g][0], cr, pe * vv.x);
+                o[g][1] = fmaf(o[g][1], cr, pe * vv.y);
+                o[g][2] = fmaf(o[g][2], cr, pe * vv.z);
+                o[g][3] = fmaf(o[g][3], cr, pe * vv.w);
+                m[g] = mn;
+            }
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < TK_MAXG; ++g) {
+        if (g < group) {
+            float* w = ws + (warp * group + g) * hs;
+            if (lane == 0) {
+                w[0] = m[g];
+                w[1] = l[g];
+            }
+            if (act) *(float4*)(w + 4 + 4 * lane) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
+        }
+    }
+    consumer_sync();
+    // merge the 16 warps: one thread per (head, dim)
+    for (int idx = tid; idx < group * hd; idx += MV_CONSUMERS) {
+        const int g = idx / hd, d = idx % hd;
+        float M = -INFINITY;
+        for (int w = 0; w < MV_CWARPS; ++w) M = fmaxf(M, ws[(w * group + g) * hs]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+            for (int w = 0; w < MV_CWARPS; ++w) {
+                const float* ww = ws + (w * group + g) * hs;
+                const float e = expf(ww[0] - M);
+                L = fmaf(ww[1], e, L);
+                O = fmaf(ww[4 + d], e, O);
+            }
+        }
+        float* dst = a.att_part + ((size_t)(kh * group + g) * nsplit + s) * hw;
+        if (d == 0) {
+            dst[0] = M;
+            dst[1] = L;
+        }
+        dst[2 + d] = O;
+    }
+    __threadfence();
+    consumer_sync();
+    if (tid == 0) {
+        tk_stamp(a, p, 2);
+        const unsigned old = atomicAdd(&a.att_cnt[kh], 1u);
+        const int last = old == (unsigned)(nsplit - 1);
+        if (last) a.att_cnt[kh] = 0u;  // every split of this kv head has arrived
+        sh->last = last;
+    }
+    consumer_sync();
+    if (!sh->last) return;
+    __threadfence();
+    // (m, l) of every split of the group's heads into shared memory, in parallel
+    float* ml = ws;                       // [group][nsplit][2]
+    float* wq = ml + 2 * group * nsplit;  // [group][nsplit] exp(m_q - M), 0 for empty splits
+    float* lsum = wq + group * nsplit;    // [group]
+    for (int i = tid; i < group * nsplit; i += MV_CONSUMERS) {
+        const float* src = a.att_part + ((size_t)kh * group * nsplit + i) * hw;
+        ml[2 * i] = __ldcg(src);
+        ml[2 * i + 1] = __ldcg(src + 1);
+    }
+    consumer_sync();
+    if (tid < group) {
+        float M = -INFINITY;
+        for (int q = 0; q < nsplit; ++q) M = fmaxf(M, ml[2 * (tid * nsplit + q)]);
+        float L = 0.f;
+        for (int q = 0; q < nsplit; ++q) {
+            const float mq = ml[2 * (tid * nsplit + q)];
+            const float e = mq != -INFINITY ? expf(mq - M) : 0.f;
+            wq[tid * nsplit + q] = e;
+            L = fmaf(ml[2 * (tid * nsplit + q) + 1], e, L);
+        }
+        lsum[tid] = L;
+    }
+    consumer_sync();
+    // o = sum_q e_q o_q / L: one thread per (head, dim), the splits' loads in flight together
+    for (int idx = tid; idx < group * hd; idx += MV_CONSUMERS) {
+        const int g = idx / hd, d = idx % hd;
+        const float* base = a.att_part + (size_t)(kh * group + g) * nsplit * hw + 2 + d;
+        const float* w = wq + g * nsplit;
+        float O = 0.f;
+#pragma unroll 8
+        for (int q = 0; q < nsplit; ++q) O = fmaf(__ldcg(base + q * hw), w[q], O);
+        A.out[(size_t)(kh * group + g) * hd + d] = O / lsum[g];
+    }
+    __threadfence();
+}
+
+// Final norm to the hidden state (src/model/llama.rs:181), CTA 0 only.
+__device__ __noinline__ void tk_hidden(const TokenArgs& a, float* red) {
+    if (blockIdx.x != 0) return;
+    const int tid = threadIdx.x;
+    float ss = 0.f;
+    for (int k = tid; k < a.E; k += MV_CONSUMERS) {
+        const float v = __ldcg(a.x + k);
+        ss = fmaf(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    consumer_sync();
+    float tot = 0.f;
+    for (int w = 0; w < MV_CWARPS; ++w) tot += red[w];
+    const float scale = 1.0f / sqrtf(tot / (float)a.E + a.eps);
+    for (int k = tid; k < a.E; k += MV_CONSUMERS)
+        a.hidden[k] = __fmul_rn(__fmul_rn(__ldcg(a.x + k), scale), a.out_norm[k]);
+}
+
+__device__ __forceinline__ void tk_tile_src(const Seg& sg, int lt, int c, int gcb, const uint8_t*& pa,
+                                            const uint8_t*& pb) {
+    const PackedW& WA = sg.A;
+    const PackedW& WB = sg.pair ? sg.B : sg.A;
+    const int gA = sg.pair ? lt : 2 * lt;
+    const int gB = sg.pair ? lt : 2 * lt + 1;
+    pa = (const uint8_t*)WA.p0 + ((size_t)gA * WA.nk + c) * gcb;
+    pb = (const uint8_t*)WB.p0 + ((size_t)gB * WB.nk + c) * gcb;
+}
+
+__global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__ TokenArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ TkShared sh;
+    const int tid = threadIdx.x;
+    const uint32_t nst = (uint32_t)a.nst;
+    uint8_t* ring = smem;
+    uint64_t* full = (uint64_t*)(smem + (size_t)nst * TK_STAGE);
+    uint64_t* empty = full + nst;
+    uint64_t* tdone = empty + nst;  // [2]
+    uint64_t* tfree = tdone + 2;    // [2]
+    float* U = (float*)(smem + (size_t)nst * TK_STAGE + TK_BAR_BYTES);
+    float* part = U + a.union_bytes / 4;     // [2][16][16]
+    float* res = part + 2 * MV_CWARPS * 16;  // 16
+    float* red = res + 16;                   // 32
+
+    const unsigned long long epoch = *a.epoch;
+    const uint32_t pos = a.step->pos;
+    uint32_t tok = a.step->token;
+    if (tok >= (uint32_t)a.vocab) {
+        if (tid == 0 && blockIdx.x == 0) atomicOr(&a.step->error, 1u);
+        tok = 0;
+    }
+    if (tid == 0) {
+        for (uint32_t i = 0; i < nst; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], MV_CWARPS);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tdone[i], MV_CWARPS);
+            mbar_init(&tfree[i], 1);
+        }
+        sh.err = 0;
+        sh.stop = 0;
+        sh.started = 0;
+        sh.last = 0;
+        if (blockIdx.x == 0) a.step->argmax_key = 0ull;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    const unsigned long long target = (epoch + 1ull) * gridDim.x;
+
+    if (tid >= MV_CONSUMERS + 32) {
+        // ---------------- epilogue warp
+        const int lane = tid & 31;
+        int n = 0;
+        for (int p = 0; p < a.nph; ++p) {
+            const TokenPhase& P = a.ph[p];
+            if (P.kind != PH_MATVEC) continue;
+            if (!smem_wait_geq(&sh.started, p)) {
+                if (lane == 0) tk_fail(a, &sh, 4u);
+                return;
+            }
+            if (*(volatile int*)&sh.err) return;
+            const MatvecArgs& m = P.mv;
+            for (int t = blockIdx.x; t < m.ntiles; t += gridDim.x, ++n) {
+                int si, lt;
+                find_seg(m, t, si, lt);
+                const Seg& sg = m.seg[si];
+                const int b = n & 1;
+                const EpiPre pre = epi_prefetch(m, sg, lt, pos, lane);
+                if (!mbar_wait(&tdone[b], (uint32_t)(n >> 1) & 1u)) {
+                    if (lane == 0) tk_fail(a, &sh, 4u);
+                    return;
+                }
+                const float* pb = part + b * MV_CWARPS * 16;
+                const int r = lane & 15, h = lane >> 4;
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < MV_CWARPS / 2; ++w) v += pb[(8 * h + w) * 16 + r];
+                const float other = __shfl_xor_sync(0xffffffffu, v, 16);
+                v = h == 0 ? v + other : other + v;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tfree[b]);
+                if (lane < 16) res[lane] = v;
+                __syncwarp();
+                apply_epilogue(m, sg, lt, res, pos, lane, pre);
+                __syncwarp();
+            }
+            if (p + 1 < a.nph) {
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) {
+                    red_release_add_u64(&a.bars[p], 1ull);
+                    tk_stamp(a, p, 3);
+                }
+            }
+        }
+        return;
+    }
+    if (tid >= MV_CONSUMERS) {
+        // ---------------- producer warp: the weights of every matvec phase, in order
+        if (tid == MV_CONSUMERS) {
+            uint64_t policy;
+            asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+            uint32_t slot = 0, par = 0, issued = 0;
+            bool ok = true;
+            for (int p = 0; p < a.nph && ok; ++p) {
+                const TokenPhase& P = a.ph[p];
+                if (P.kind != PH_MATVEC) continue;
+                const MatvecArgs& m = P.mv;
+                const int gcb = gcb_of(P.type), ck = ck_of(P.type);
+                const int nchunk = (m.K + ck - 1) / ck;
+                for (int t = blockIdx.x; t < m.ntiles && ok; t += gridDim.x) {
+                    int si, lt;
+                    find_seg(m, t, si, lt);
+                    for (int c = 0; c < nchunk; ++c) {
+                        if (!mbar_wait(&empty[slot], par ^ 1u) || *(volatile int*)&sh.err) {
+                            ok = false;
+                            break;
+                        }
+                        const uint8_t *ga, *gb;
+                        tk_tile_src(m.seg[si], lt, c, gcb, ga, gb);
+                        uint8_t* dst = ring + slot * TK_STAGE;
+                        mbar_expect_tx(&full[slot], 2 * gcb);
+                        bulk_g2s_evict_first(dst, ga, gcb, &full[slot], policy);
+                        bulk_g2s_evict_first(dst + gcb, gb, gcb, &full[slot], policy);
+                        ++issued;
+                        if (++slot == nst) {
+                            slot = 0;
+                            par ^= 1u;
+                        }
+                    }
+                }
+            }
+            // drain: every issued copy has landed before this thread exits
+            const uint32_t first = issued > nst ? issued - nst : 0;
+            for (uint32_t j = first; j < issued; ++j) mbar_wait(&full[j % nst], (j / nst) & 1u);
+            if (!ok) tk_fail(a, &sh, 2u);
+        }
+        return;
+    }
+
+    // ---------------- consumers
+    uint32_t slot = 0, par = 0;
+    int ntile = 0;
+    for (int p = 0; p < a.nph; ++p) {
+        const TokenPhase& P = a.ph[p];
+        if (p > 0) {
+            if (tid == 0) {
+                if (!grid_wait_one(&a.bars[p - 1], target)) tk_fail(a, &sh, 4u);
+                __threadfence();
+                *(volatile int*)&sh.started = p;
+                sh.stop = *(volatile int*)&sh.err;
+                tk_stamp(a, p, 0);
+            }
+            consumer_sync();
+            if (sh.stop) break;  // every consumer warp reads the same snapshot
+        } else if (tid == 0) {
+            tk_stamp(a, 0, 0);
+        }
+        if (P.kind == PH_MATVEC) {
+            bool ok = true;
+            switch (P.type) {
+                case GT_Q4_0:
+                    ok = tk_matvec<GT_Q4_0>(a, P, p, tok, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
+                    break;
+                case GT_Q8_0:
+                    ok = tk_matvec<GT_Q8_0>(a, P, p, tok, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
+                    break;
+                case GT_Q6_K:
+                    ok = tk_matvec<GT_Q6_K>(a, P, p, tok, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
+                    break;
+                default:
+                    ok = tk_matvec<GT_F32>(a, P, p, tok, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
+                    break;
+            }
+            if (!ok) {
+                // no early exit: the other consumer warps meet this one at the next
+                // phase's consumer_sync, see the error there and leave together
+                if ((tid & 31) == 0) tk_fail(a, &sh, 4u);
+                continue;
+            }
+        } else if (P.kind == PH_ATTN) {
+            tk_attention(a, P.at, p, pos, U, &sh);
+            consumer_sync();
+            if (tid == 0 && p + 1 < a.nph) {
+                __threadfence();
+                red_release_add_u64(&a.bars[p], 1ull);
+                tk_stamp(a, p, 3);
+            }
+        } else {
+            tk_hidden(a, red);
+        }
+    }
+    // every CTA has read the epoch once it arrived at the last barrier
+    if (tid == 0 && blockIdx.x == 0 && !*(volatile int*)&sh.err) atomicAdd(a.epoch, 1ull);
+}
+
+int token_stage_elems(int type, int K) {
+    const int ck = fmt_ck(type);
+    if (!ck) return 0;
+    return ceil_div_h(K, ck) * ck;
+}
+
+int token_attn_bytes(int group, int hd, int nsplit) {
+    const int warps = MV_CWARPS * group * (hd + 4), merge = 3 * group * nsplit + group;
+    return (group * hd + (warps > merge ? warps : merge)) * 4;
+}
+
+size_t token_smem_bytes(int nst, int union_bytes) {
+    return (size_t)nst * TK_STAGE + TK_BAR_BYTES + (size_t)union_bytes + TK_TAIL_BYTES;
+}
+
+// Dynamic shared memory k_token may use: the opt-in maximum less its static part.
+static int token_smem_limit() {
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return 0;
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, k_token) != cudaSuccess) return 0;
+    return v - (int)fa.sharedSizeBytes;
+}
+
+int token_max_stages(int union_bytes) {
+    const long room = (long)token_smem_limit() - TK_BAR_BYTES - union_bytes - TK_TAIL_BYTES;
+    long n = room / TK_STAGE;
+    if (n > 24) n = 24;
+    return n < 2 ? 0 : (int)n;
+}
+
+cudaError_t token_configure() {
+    const int lim = token_smem_limit();
+    if (lim <= 0) return cudaErrorInvalidValue;
+    return cudaFuncSetAttribute(k_token, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+}
+
+cudaError_t launch_token(const TokenArgs& a, int grid, cudaStream_t s, bool cooperative) {
+    if (a.nst < 2 || a.nst > 24 || a.union_bytes % 16) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(MV_THREADS);
+    cfg.dynamicSmemBytes = token_smem_bytes(a.nst, a.union_bytes);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = cooperative ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_token, a);
 }
 
 }  // namespace talos

@@ -8,8 +8,10 @@
 //    (src/math/metal/mod.rs:391-396,443-454);
 //  * activations live in one arena allocated once, not per token
 //    (src/math/metal/mod.rs:398-412 allocates 14 buffers every token);
-//  * one token = one CUDA graph replay of ~5 kernels per layer; the graph reads
-//    token and position from device memory, so the same graph serves every step.
+//  * one token = one CUDA graph replay; the graph reads token and position from
+//    device memory, so the same graph serves every step. The graph holds either
+//    the per-token kernel k_token (one launch for the whole step, the default)
+//    or the layered sequence of ~5 kernels per layer.
 #include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -178,6 +180,7 @@ static talos_status device_setup(int device) {
     std::call_once(g_cfg_once, [] {
         g_cfg_err = matvec_configure();
         if (g_cfg_err == cudaSuccess) g_cfg_err = attention_configure();
+        if (g_cfg_err == cudaSuccess) g_cfg_err = token_configure();
     });
     if (g_cfg_err != cudaSuccess) return set_err(TALOS_ERR_CUDA, "matvec_configure: %s", cudaGetErrorString(g_cfg_err));
     if (device < 64 && g_sms[device] == 0) {
@@ -232,6 +235,24 @@ struct talos_ctx {
 
     cudaGraphExec_t graph[GM_COUNT] = {nullptr, nullptr, nullptr};
     bool weights_dirty = true;
+
+    // per-token kernel (k_token)
+    int step_pref = TALOS_STEP_AUTO;  // talos_ctx_set_step_kernel
+    bool fused = false;               // the current graphs run k_token
+    std::string fused_why;            // why k_token cannot run this model ("" = it can)
+    bool coop = true;                 // capture k_token as a cooperative launch
+    void* sync_mem = nullptr;         // barrier counters, epoch, attention partials
+    size_t sync_bytes = 0;
+    unsigned long long* bars = nullptr;
+    unsigned long long* epoch = nullptr;
+    unsigned long long* stamps = nullptr;
+    unsigned* att_cnt = nullptr;
+    float* att_part = nullptr;
+    int nsplit = 0, nph_max = 0;
+    TokenPhase* d_phases[GM_COUNT] = {nullptr, nullptr, nullptr};
+    int nph[GM_COUNT] = {0, 0, 0};
+    int tk_nst = 0, tk_union = 0;
+    std::vector<unsigned long long>* last_stamps = nullptr;  // talos_profile_phases
     // talos_profile_step: events recorded after each launch, tagged by kernel kind
     std::vector<std::pair<cudaEvent_t, int>>* prof = nullptr;
     std::vector<LayerW> layers;
@@ -241,6 +262,11 @@ struct talos_ctx {
             if (g) {
                 cudaGraphExecDestroy(g);
                 g = nullptr;
+            }
+        for (auto& p : d_phases)
+            if (p) {
+                cudaFree(p);
+                p = nullptr;
             }
     }
 };
@@ -358,6 +384,45 @@ static talos_status alloc_arena(talos_ctx* c) {
     return TALOS_OK;
 }
 
+// Grid-barrier counters, launch epoch, phase stamps and attention partials of
+// k_token, zeroed.
+static talos_status alloc_sync(talos_ctx* c) {
+    const int sms = (c->device < 64 && g_sms[c->device]) ? g_sms[c->device] : 148;
+    c->nsplit = sms / (int)c->cfg.n_head_kv;
+    if (c->nsplit < 1) c->nsplit = 1;
+    c->nph_max = (int)c->cfg.n_layer * 5 + 1;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off += align256(bytes);
+        return o;
+    };
+    const size_t o_bars = take((size_t)c->nph_max * 8), o_epoch = take(8),
+                 o_stamps = take((size_t)c->nph_max * sms * 4 * 8),
+                 o_cnt = take((size_t)c->cfg.n_head_kv * 4),
+                 o_part = take((size_t)c->cfg.n_head * c->nsplit * (c->hd + 2) * 4);
+    CK(cudaMalloc(&c->sync_mem, off));
+    c->sync_bytes = off;
+    uint8_t* b = (uint8_t*)c->sync_mem;
+    c->bars = (unsigned long long*)(b + o_bars);
+    c->epoch = (unsigned long long*)(b + o_epoch);
+    c->stamps = (unsigned long long*)(b + o_stamps);
+    c->att_cnt = (unsigned*)(b + o_cnt);
+    c->att_part = (float*)(b + o_part);
+    CK(cudaMemsetAsync(c->sync_mem, 0, off, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return TALOS_OK;
+}
+
+// After a failed step the barrier counters may be part-way through a launch:
+// start them again from zero (no kernel of this context is running).
+static void reset_sync(talos_ctx* c) {
+    if (c->sync_mem) {
+        cudaMemsetAsync(c->sync_mem, 0, c->sync_bytes, c->stream);
+        cudaStreamSynchronize(c->stream);
+    }
+}
+
 extern "C" talos_status talos_ctx_create(const talos_cfg* cfg, int device, talos_ctx** out) {
     if (!cfg || !out) return set_err(TALOS_ERR_INVALID_ARG, "cfg/out is NULL");
     *out = nullptr;
@@ -393,6 +458,7 @@ extern "C" talos_status talos_ctx_create(const talos_cfg* cfg, int device, talos
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     TRY(alloc_arena(c.get()));
     TRY(alloc_kv(c.get()));
+    TRY(alloc_sync(c.get()));
     *out = c.release();
     return TALOS_OK;
 }
@@ -406,6 +472,7 @@ extern "C" talos_status talos_ctx_destroy(talos_ctx* c) {
     for (auto& kv : c->resident) kv.second.release();
     c->staging.release();
     if (c->arena) cudaFree(c->arena);
+    if (c->sync_mem) cudaFree(c->sync_mem);
     if (c->kcache) cudaFree(c->kcache);
     if (c->vcache) cudaFree(c->vcache);
     if (c->rope_cs) cudaFree(c->rope_cs);
@@ -465,7 +532,7 @@ extern "C" talos_status talos_weight_upload(talos_ctx* c, const char* name, cons
 
 extern "C" talos_status talos_ctx_device_bytes(talos_ctx* c, size_t* out) {
     if (!c || !out) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
-    size_t n = c->arena_bytes + c->kv_bytes + c->staging.cap;
+    size_t n = c->arena_bytes + c->kv_bytes + c->staging.cap + c->sync_bytes;
     for (auto& kv : c->w) n += kv.second.bytes;
     for (auto& kv : c->resident) n += kv.second.bytes;
     *out = n;
@@ -678,24 +745,284 @@ static talos_status enqueue_step(talos_ctx* c, GraphMode mode) {
     return TALOS_OK;
 }
 
-static talos_status ensure_graph(talos_ctx* c, GraphMode mode) {
+// ------------------------------------------------------------------ per-token kernel
+
+// The phases of one step for k_token (llama.rs:96-183, then :89 or :181).
+static void build_phases(talos_ctx* c, GraphMode mode, std::vector<TokenPhase>& ph) {
+    const talos_cfg& cfg = c->cfg;
+    const int E = (int)cfg.n_embd, F = (int)cfg.n_ff;
+    const size_t kv_layer = c->kv_ctx * (size_t)c->kv_dim;
+    ph.clear();
+    for (uint32_t l = 0; l < cfg.n_layer; ++l) {
+        const LayerW& L = c->layers[l];
+        float* kc = c->kcache + l * kv_layer;
+        float* vc = c->vcache + l * kv_layer;
+        TokenPhase p{};
+        // rmsnorm + q/k/v + RoPE + KV append (llama.rs:118-130); layer 0 reads the embedding row
+        p.kind = PH_MATVEC;
+        p.type = L.q->type;
+        p.embed_in = l == 0;
+        p.prof_kind = TALOS_K_QKV;
+        p.mv.K = E;
+        p.mv.x = c->x;
+        p.mv.norm_w = (const float*)L.attn_norm->mem;
+        p.mv.eps = cfg.rms_eps;
+        p.mv.epi = EPI_QKV;
+        p.mv.step = c->step;
+        p.mv.kcache = kc;
+        p.mv.vcache = vc;
+        p.mv.kv_dim = c->kv_dim;
+        p.mv.hd = c->hd;
+        p.mv.rope_cs = c->rope_cs;
+        p.mv.seg[p.mv.nseg++] = make_seg(L.q, nullptr, 0, c->q, E, 0);
+        p.mv.seg[p.mv.nseg++] = make_seg(L.k, nullptr, 0, nullptr, c->kv_dim, 1);
+        p.mv.seg[p.mv.nseg++] = make_seg(L.v, nullptr, 0, nullptr, c->kv_dim, 2);
+        ph.push_back(p);
+        // attention (llama.rs:135-155)
+        p = TokenPhase{};
+        p.kind = PH_ATTN;
+        p.prof_kind = TALOS_K_ATTN;
+        p.at.q = c->q;
+        p.at.kc = kc;
+        p.at.vc = vc;
+        p.at.out = c->att;
+        p.at.step = c->step;
+        p.at.n_head = (int)cfg.n_head;
+        p.at.n_kv = (int)cfg.n_head_kv;
+        p.at.hd = c->hd;
+        p.at.kv_dim = c->kv_dim;
+        p.at.scale = 1.0f / sqrtf((float)c->hd);
+        ph.push_back(p);
+        // o-proj + residual (llama.rs:157-161)
+        p = TokenPhase{};
+        p.kind = PH_MATVEC;
+        p.type = L.o->type;
+        p.prof_kind = TALOS_K_OPROJ;
+        p.mv.K = E;
+        p.mv.x = c->att;
+        p.mv.epi = EPI_ADD;
+        p.mv.step = c->step;
+        p.mv.seg[p.mv.nseg++] = make_seg(L.o, nullptr, 0, c->x, E, 0);
+        ph.push_back(p);
+        // rmsnorm + gate/up + SwiGLU (llama.rs:164-171)
+        p = TokenPhase{};
+        p.kind = PH_MATVEC;
+        p.type = L.gate->type;
+        p.prof_kind = TALOS_K_GATEUP;
+        p.mv.K = E;
+        p.mv.x = c->x;
+        p.mv.norm_w = (const float*)L.ffn_norm->mem;
+        p.mv.eps = cfg.rms_eps;
+        p.mv.epi = EPI_SWIGLU;
+        p.mv.step = c->step;
+        p.mv.seg[p.mv.nseg++] = make_seg(L.gate, L.up, 1, c->ff, F, 0);
+        ph.push_back(p);
+        // down + residual (llama.rs:172-176)
+        p = TokenPhase{};
+        p.kind = PH_MATVEC;
+        p.type = L.down->type;
+        p.prof_kind = TALOS_K_DOWN;
+        p.mv.K = F;
+        p.mv.x = c->ff;
+        p.mv.epi = EPI_ADD;
+        p.mv.step = c->step;
+        p.mv.seg[p.mv.nseg++] = make_seg(L.down, nullptr, 0, c->x, E, 0);
+        ph.push_back(p);
+    }
+    TokenPhase p{};
+    p.prof_kind = TALOS_K_OUTPUT;
+    if (mode == GM_HIDDEN) {
+        p.kind = PH_HIDDEN;  // final rmsnorm (llama.rs:181)
+    } else {                 // final rmsnorm + output projection (llama.rs:181, :89)
+        const DevTensor& ow = c->w["output.weight"];
+        const DevTensor& onorm = c->w["output_norm.weight"];
+        p.kind = PH_MATVEC;
+        p.type = ow.type;
+        p.mv.K = E;
+        p.mv.x = c->x;
+        p.mv.norm_w = (const float*)onorm.mem;
+        p.mv.eps = cfg.rms_eps;
+        p.mv.epi = EPI_LOGITS;
+        p.mv.step = c->step;
+        p.mv.seg[p.mv.nseg++] = make_seg(&ow, nullptr, 0, c->logits, (int)cfg.vocab_size, 0);
+    }
+    ph.push_back(p);
+    for (auto& q : ph) {
+        q.mv.ntiles = 0;
+        for (int i = 0; i < q.mv.nseg; ++i) q.mv.ntiles += q.mv.seg[i].ntiles;
+    }
+}
+
+// Whether k_token can run this model; sets c->fused_why, tk_union and tk_nst.
+static void fused_check(talos_ctx* c) {
+    c->fused_why.clear();
+    char buf[256];
+    if (c->hd > 128) {
+        snprintf(buf, sizeof buf, "head_dim %d above 128", c->hd);
+        c->fused_why = buf;
+        return;
+    }
+    if (c->cfg.n_embd > 8192) {
+        snprintf(buf, sizeof buf, "n_embd %u above 8192", c->cfg.n_embd);
+        c->fused_why = buf;
+        return;
+    }
+    const DevTensor& embd = c->w["token_embd.weight"];
+    if (c->cfg.n_embd % gguf_block_elems(embd.type)) {
+        c->fused_why = "n_embd is not a whole number of token_embd blocks";
+        return;
+    }
+    std::vector<TokenPhase> ph;
+    build_phases(c, GM_LOGITS, ph);
+    int ub = token_attn_bytes(c->group, c->hd, c->nsplit);
+    for (uint32_t l = 0; l < c->cfg.n_layer; ++l) {
+        const LayerW& L = c->layers[l];
+        if (L.k->type != L.q->type || L.v->type != L.q->type) {
+            snprintf(buf, sizeof buf, "layer %u: attn_q/k/v do not share a ggml type", l);
+            c->fused_why = buf;
+            return;
+        }
+    }
+    for (const auto& p : ph)
+        if (p.kind == PH_MATVEC) {
+            const int kp = token_stage_elems(p.type, p.mv.K);
+            const int b = kp * 4 + kp / 16 * 4;
+            if (b > ub) ub = b;
+        }
+    ub = (ub + 15) / 16 * 16;
+    c->tk_union = ub;
+    c->tk_nst = token_max_stages(ub);
+    if (c->tk_nst < 2) {
+        snprintf(buf, sizeof buf, "staged input (%d bytes) leaves no room for the weight ring", ub);
+        c->fused_why = buf;
+    }
+}
+
+static talos_status use_fused(talos_ctx* c, bool* out) {
+    *out = false;
+    if (c->step_pref == TALOS_STEP_LAYERED) return TALOS_OK;
+    if (c->fused_why.empty()) {
+        *out = true;
+        return TALOS_OK;
+    }
+    if (c->step_pref == TALOS_STEP_FUSED)
+        return set_err(TALOS_ERR_UNSUPPORTED, "the per-token kernel cannot run this model: %s", c->fused_why.c_str());
+    return TALOS_OK;
+}
+
+static TokenArgs token_args(talos_ctx* c, GraphMode mode, unsigned long long* stamps) {
+    TokenArgs a{};
+    const DevTensor& embd = c->w["token_embd.weight"];
+    a.ph = c->d_phases[mode];
+    a.nph = c->nph[mode];
+    a.bars = c->bars;
+    a.epoch = c->epoch;
+    a.step = c->step;
+    a.embd = (const uint8_t*)embd.mem;
+    a.embd_type = embd.type;
+    a.vocab = (int)c->cfg.vocab_size;
+    a.x = c->x;
+    a.E = (int)c->cfg.n_embd;
+    a.hidden = c->hidden;
+    a.out_norm = (const float*)c->w["output_norm.weight"].mem;
+    a.eps = c->cfg.rms_eps;
+    a.att_part = c->att_part;
+    a.att_cnt = c->att_cnt;
+    a.nsplit = c->nsplit;
+    a.nst = c->tk_nst;
+    a.union_bytes = c->tk_union;
+    a.stamps = stamps;
+    return a;
+}
+
+static int sm_count(const talos_ctx* c) { return (c->device < 64 && g_sms[c->device]) ? g_sms[c->device] : 148; }
+
+// Upload the phase list of `mode` (outside any capture).
+static talos_status prepare_phases(talos_ctx* c, GraphMode mode) {
+    if (c->d_phases[mode]) return TALOS_OK;
+    std::vector<TokenPhase> ph;
+    build_phases(c, mode, ph);
+    if ((int)ph.size() > c->nph_max) return set_err(TALOS_ERR_STATE, "phase list longer than the barrier area");
+    CK(cudaMalloc(&c->d_phases[mode], ph.size() * sizeof(TokenPhase)));
+    CK(cudaMemcpy(c->d_phases[mode], ph.data(), ph.size() * sizeof(TokenPhase), cudaMemcpyHostToDevice));
+    c->nph[mode] = (int)ph.size();
+    return TALOS_OK;
+}
+
+static talos_status enqueue_fused(talos_ctx* c, GraphMode mode, unsigned long long* stamps) {
+    TokenArgs a = token_args(c, mode, stamps);
+    cudaError_t e = launch_token(a, sm_count(c), c->stream, c->coop);
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "per-token kernel launch: %s", cudaGetErrorString(e));
+    if (mode == GM_GREEDY) {
+        e = launch_greedy_advance(c->step, c->gen, (int)c->kv_ctx + 1, c->stream, false);
+        if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "greedy advance: %s", cudaGetErrorString(e));
+    }
+    return TALOS_OK;
+}
+
+static talos_status bind_if_dirty(talos_ctx* c) {
     if (c->weights_dirty) {
         TRY(bind_layers(c));
+        fused_check(c);
+        c->drop_graphs();
         c->weights_dirty = false;
     }
-    if (c->graph[mode]) return TALOS_OK;
+    return TALOS_OK;
+}
+
+static talos_status capture(talos_ctx* c, GraphMode mode, bool fused, cudaGraphExec_t* out) {
     cudaGraph_t g = nullptr;
     CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-    talos_status st = enqueue_step(c, mode);
+    talos_status st = fused ? enqueue_fused(c, mode, nullptr) : enqueue_step(c, mode);
     cudaError_t e = cudaStreamEndCapture(c->stream, &g);
     if (st != TALOS_OK) {
         if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
         return st;
     }
     if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
-    e = cudaGraphInstantiate(&c->graph[mode], g, 0);
+    e = cudaGraphInstantiate(out, g, 0);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+    return TALOS_OK;
+}
+
+static talos_status ensure_graph(talos_ctx* c, GraphMode mode) {
+    TRY(bind_if_dirty(c));
+    if (c->graph[mode]) return TALOS_OK;
+    bool fused = false;
+    TRY(use_fused(c, &fused));
+    c->fused = fused;
+    if (!fused) return capture(c, mode, false, &c->graph[mode]);
+    TRY(prepare_phases(c, mode));
+    talos_status st = capture(c, mode, true, &c->graph[mode]);
+    if (st != TALOS_OK && c->coop) {
+        // a graph that cannot hold a cooperative launch: every CTA is still
+        // resident (one per SM, the kernel's shared memory allows no second)
+        c->coop = false;
+        st = capture(c, mode, true, &c->graph[mode]);
+    }
+    return st;
+}
+
+extern "C" talos_status talos_ctx_set_step_kernel(talos_ctx* c, int kind) {
+    if (!c) return set_err(TALOS_ERR_INVALID_ARG, "NULL ctx");
+    if (kind != TALOS_STEP_AUTO && kind != TALOS_STEP_FUSED && kind != TALOS_STEP_LAYERED)
+        return set_err(TALOS_ERR_INVALID_ARG, "step kernel kind %d", kind);
+    CK(cudaSetDevice(c->device));
+    CK(cudaStreamSynchronize(c->stream));
+    c->step_pref = kind;
+    c->drop_graphs();
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_ctx_step_kernel(talos_ctx* c, int* out) {
+    if (!c || !out) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    CK(cudaSetDevice(c->device));
+    TRY(bind_if_dirty(c));
+    bool fused = false;
+    TRY(use_fused(c, &fused));
+    *out = fused ? TALOS_STEP_FUSED : TALOS_STEP_LAYERED;
     return TALOS_OK;
 }
 
@@ -716,11 +1043,16 @@ static talos_status set_step(talos_ctx* c, uint32_t token, size_t pos) {
     return TALOS_OK;
 }
 
+// Error bits of StepParams::error: 1 = token id out of range, 2 = the weight
+// stream gave up waiting, 4 = a barrier or hand-off wait ran out.
 static talos_status finish_step(talos_ctx* c) {
     CK(cudaMemcpyAsync(c->h_step, c->step, sizeof(StepParams), cudaMemcpyDeviceToHost, c->stream));
     CK(cudaStreamSynchronize(c->stream));
-    if (c->h_step->error) return set_err(TALOS_ERR_OOB, "device bounds check fired (code %u)", c->h_step->error);
-    return TALOS_OK;
+    const uint32_t err = c->h_step->error;
+    if (!err) return TALOS_OK;
+    reset_sync(c);
+    if (err & ~1u) return set_err(TALOS_ERR_TIMEOUT, "a bounded device wait ran out (code %u)", err);
+    return set_err(TALOS_ERR_OOB, "device bounds check fired (code %u)", err);
 }
 
 static talos_status forward_common(talos_ctx* c, uint32_t token, size_t pos, float* out, GraphMode mode) {
@@ -792,16 +1124,79 @@ extern "C" talos_status talos_prefill(talos_ctx* c, const uint32_t* tokens, size
     return TALOS_OK;
 }
 
+static talos_status profile_fused(talos_ctx* c, double* kernel_ms, uint32_t* launches) {
+    TRY(prepare_phases(c, GM_LOGITS));
+    const int nph = c->nph[GM_LOGITS];
+    std::vector<TokenPhase> ph;
+    build_phases(c, GM_LOGITS, ph);
+    cudaEvent_t e0, e1;
+    CK(cudaEventCreate(&e0));
+    CK(cudaEventCreate(&e1));
+    CK(cudaEventRecord(e0, c->stream));
+    talos_status st = enqueue_fused(c, GM_LOGITS, c->stamps);
+    CK(cudaEventRecord(e1, c->stream));
+    const int G = sm_count(c);
+    std::vector<unsigned long long> raw((size_t)nph * G * 4), stamps(nph);
+    CK(cudaMemcpyAsync(raw.data(), c->stamps, raw.size() * 8, cudaMemcpyDeviceToHost, c->stream));
+    if (st == TALOS_OK) st = finish_step(c);
+    float total = 0.f;
+    if (st == TALOS_OK) CK(cudaEventElapsedTime(&total, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    TRY(st);
+    for (int p = 0; p < nph; ++p) stamps[p] = raw[(size_t)p * G * 4];  // CTA 0 entering phase p
+    if (c->last_stamps) *c->last_stamps = raw;
+    double inner = 0.0;
+    for (int p = 0; p < nph; ++p) {
+        double ms;
+        if (p + 1 < nph) {
+            ms = (double)(stamps[p + 1] - stamps[p]) * 1e-6;
+            inner += ms;
+        } else {
+            ms = (double)total - inner;  // last phase + launch and drain
+        }
+        const int k = ph[p].prof_kind;
+        if (kernel_ms) kernel_ms[k] += ms;
+        if (launches) launches[k] += 1;
+    }
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_profile_phases(talos_ctx* c, uint32_t token, size_t pos, uint64_t* out, size_t cap,
+                                             int* n_phase, int* n_cta) {
+    if (!c || !out || !n_phase || !n_cta) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    CK(cudaSetDevice(c->device));
+    TRY(check_tok_pos(c, token, pos));
+    TRY(bind_if_dirty(c));
+    bool fused = false;
+    TRY(use_fused(c, &fused));
+    if (!fused) return set_err(TALOS_ERR_UNSUPPORTED, "steps run the layered graph: no phase stamps");
+    TRY(prepare_phases(c, GM_LOGITS));
+    const size_t n = (size_t)c->nph[GM_LOGITS] * sm_count(c) * 4;
+    if (cap < n) return set_err(TALOS_ERR_INVALID_ARG, "out holds %zu values, %zu needed", cap, n);
+    CK(cudaMemsetAsync(c->stamps, 0, n * 8, c->stream));
+    TRY(set_step(c, token, pos));
+    std::vector<unsigned long long> raw;
+    c->last_stamps = &raw;
+    talos_status st = profile_fused(c, nullptr, nullptr);
+    c->last_stamps = nullptr;
+    TRY(st);
+    memcpy(out, raw.data(), n * 8);
+    *n_phase = c->nph[GM_LOGITS];
+    *n_cta = sm_count(c);
+    return TALOS_OK;
+}
+
 extern "C" talos_status talos_profile_step(talos_ctx* c, uint32_t token, size_t pos, double* kernel_ms,
                                            uint32_t* launches) {
     if (!c) return set_err(TALOS_ERR_INVALID_ARG, "NULL ctx");
     CK(cudaSetDevice(c->device));
     TRY(check_tok_pos(c, token, pos));
-    if (c->weights_dirty) {
-        TRY(bind_layers(c));
-        c->weights_dirty = false;
-    }
+    TRY(bind_if_dirty(c));
+    bool fused = false;
+    TRY(use_fused(c, &fused));
     TRY(set_step(c, token, pos));
+    if (fused) return profile_fused(c, kernel_ms, launches);
     std::vector<std::pair<cudaEvent_t, int>> ev;
     c->prof = &ev;
     talos_status st = enqueue_step(c, GM_LOGITS);

@@ -139,6 +139,17 @@ class Context:
         _lib.check(_lib.load().talos_weight_upload(self.h, name.encode(), _ptr(buf), buf.nbytes, gtype,
                                                    rows, cols))
 
+    def set_step_kernel(self, kind: str):
+        """"auto", "fused" (one per-token kernel) or "layered" (~5 kernels per layer)."""
+        k = {"auto": _lib.STEP_AUTO, "fused": _lib.STEP_FUSED, "layered": _lib.STEP_LAYERED}[kind]
+        _lib.check(_lib.load().talos_ctx_set_step_kernel(self.h, k))
+
+    def step_kernel(self) -> str:
+        """What the next step runs: "fused" or "layered"."""
+        k = C.c_int()
+        _lib.check(_lib.load().talos_ctx_step_kernel(self.h, C.byref(k)))
+        return "fused" if k.value == _lib.STEP_FUSED else "layered"
+
     def device_bytes(self) -> int:
         n = C.c_size_t()
         _lib.check(_lib.load().talos_ctx_device_bytes(self.h, C.byref(n)))
@@ -179,12 +190,24 @@ class Context:
     KERNEL_KINDS = ("embed", "qkv", "attn", "oproj", "gateup", "down", "output")
 
     def profile_step(self, token: int, pos: int) -> tuple[dict, dict]:
-        """Per-kernel-kind device ms and launch counts of one eagerly launched step."""
+        """Per-kernel-kind device ms and counts of one step: kernels launched one by
+        one (layered), or the per-token kernel's phases timed on the device clock
+        (fused)."""
         ms = (C.c_double * 7)()
         n = (C.c_uint32 * 7)()
         _lib.check(_lib.load().talos_profile_step(self.h, int(token), int(pos), ms, n))
         return ({k: ms[i] for i, k in enumerate(self.KERNEL_KINDS)},
                 {k: int(n[i]) for i, k in enumerate(self.KERNEL_KINDS)})
+
+    def profile_phases(self, token: int, pos: int) -> np.ndarray:
+        """Per-token kernel stamps of one step: uint64 ns [phase][cta][4] = entered,
+        staged, computed, arrived (0 where a stamp does not apply)."""
+        cap = (self.cfg.n_layer * 5 + 1) * 256 * 4
+        out = np.zeros(cap, np.uint64)
+        nph, ncta = C.c_int(), C.c_int()
+        _lib.check(_lib.load().talos_profile_phases(self.h, int(token), int(pos), _ptr(out), cap, C.byref(nph),
+                                                    C.byref(ncta)))
+        return out[: nph.value * ncta.value * 4].reshape(nph.value, ncta.value, 4)
 
     def cap_context(self, max_ctx: int):
         _lib.check(_lib.load().talos_cap_context(self.h, int(max_ctx)))
@@ -203,7 +226,7 @@ class Model:
     """``Model`` (src/model/llama.rs:20-238) with the CUDA backend."""
 
     def __init__(self, gguf: GgufFile, device: int = 0, tp_size: int = 1, tp_rank: int = 0,
-                 nccl_id: bytes | None = None, max_ctx: int | None = None):
+                 nccl_id: bytes | None = None, max_ctx: int | None = None, step_kernel: str = "auto"):
         cfg = Config.from_gguf(gguf)
         if cfg.n_head_kv == 0 or cfg.n_head % cfg.n_head_kv != 0:
             raise GgufError(f"head_count {cfg.n_head} must be a positive multiple of head_count_kv "
@@ -213,6 +236,8 @@ class Model:
         self.cfg = cfg
         self.gguf = gguf
         self.ctx = Context(cfg, device, tp_size, tp_rank, nccl_id)
+        if step_kernel != "auto":
+            self.ctx.set_step_kernel(step_kernel)
         for name, (rows, cols) in weight_shapes(cfg).items():
             if rows == 1:
                 data = gguf.tensor_f32(name)

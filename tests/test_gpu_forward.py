@@ -2,7 +2,8 @@
 
 Bars: greedy tokens identical; logits within 1e-4 max-abs
 for F32 weights and 1e-3 max-abs for quantized weights; a re-run is bit-identical
-(tests/forward_gpu.rs:183-190).
+(tests/forward_gpu.rs:183-190). The step tests run both ways a step can be
+launched: the per-token kernel ("fused") and the layered kernel graph.
 """
 import numpy as np
 import pytest
@@ -16,10 +17,16 @@ from .helpers import forward_gpu_model, gqa_pair, prompt, tiny_model
 pytestmark = pytest.mark.gpu
 
 
-def test_forward_gpu_matches_cpu():  # tests/forward_gpu.rs:146-193
+@pytest.fixture(params=["fused", "layered"])
+def sk(request):
+    return request.param
+
+
+def test_forward_gpu_matches_cpu(sk):  # tests/forward_gpu.rs:146-193
     data = forward_gpu_model(0)
     cpu = oracle.Model(data=data)
-    gpu = Model.load_bytes(data)
+    gpu = Model.load_bytes(data, step_kernel=sk)
+    assert gpu.ctx.step_kernel() == sk
     toks = [1, 3, 5, 7, 2, 4]
     max_rel, run1 = 0.0, None
     for pos, t in enumerate(toks):
@@ -34,10 +41,10 @@ def test_forward_gpu_matches_cpu():  # tests/forward_gpu.rs:146-193
     assert np.array_equal(run1, run2), "GPU forward is nondeterministic"
 
 
-def test_forward_hidden_gpu_matches_cpu():  # tests/forward_gpu.rs:197-228
+def test_forward_hidden_gpu_matches_cpu(sk):  # tests/forward_gpu.rs:197-228
     data = forward_gpu_model(1)
     cpu = oracle.Model(data=data)
-    gpu = Model.load_bytes(data)
+    gpu = Model.load_bytes(data, step_kernel=sk)
     for pos, t in enumerate([1, 3, 5, 7, 2, 4]):
         c = cpu.forward_hidden(t, pos)
         g = gpu.forward_hidden_gpu(t, pos)
@@ -45,11 +52,11 @@ def test_forward_hidden_gpu_matches_cpu():  # tests/forward_gpu.rs:197-228
         assert np.max(np.abs(g - c) / np.maximum(np.abs(c), 1.0)) <= 1e-3
 
 
-def test_gqa_matches_replicated_mha_gpu():  # tests/gqa.rs:194-227 on the GPU path
+def test_gqa_matches_replicated_mha_gpu(sk):  # tests/gqa.rs:194-227 on the GPU path
     g_bytes, m_bytes = gqa_pair(7)
     outs = []
     for data in (g_bytes, m_bytes):
-        m = Model.load_bytes(data)
+        m = Model.load_bytes(data, step_kernel=sk)
         for pos, t in enumerate([1, 2, 3, 4, 5]):
             lg = m.forward_gpu(t, pos)
         outs.append(lg)
@@ -57,11 +64,11 @@ def test_gqa_matches_replicated_mha_gpu():  # tests/gqa.rs:194-227 on the GPU pa
     assert np.max(np.abs(outs[0] - outs[1])) <= 1e-5
 
 
-def greedy_parity(data, n_prompt, n_gen, tol, seed=42):
+def greedy_parity(data, n_prompt, n_gen, tol, seed=42, sk="auto"):
     """Prompt token by token, then greedy decode; compare every step's logits and
     the chosen tokens with the oracle. Returns (max abs err, min top-2 gap)."""
     cpu = oracle.Model(data=data)
-    gpu = Model.load_bytes(data)
+    gpu = Model.load_bytes(data, step_kernel=sk)
     vocab = cpu.cfg.vocab_size
     toks = prompt(n_prompt, vocab, seed)
     max_err, min_gap = 0.0, np.inf
@@ -94,19 +101,19 @@ def greedy_parity(data, n_prompt, n_gen, tol, seed=42):
     return max_err, min_gap
 
 
-def test_tiny_f32_greedy_parity():
-    err, gap = greedy_parity(tiny_model(gguf.F32), 16, 64, 1e-4)
+def test_tiny_f32_greedy_parity(sk):
+    err, gap = greedy_parity(tiny_model(gguf.F32), 16, 64, 1e-4, sk=sk)
     print(f"tiny F32: max abs err {err:.2e}, min top-2 gap {gap:.2e}")
 
 
 @pytest.mark.parametrize("wtype", [gguf.Q4_0, gguf.Q8_0])
-def test_tiny_quant_greedy_parity(wtype):
-    err, gap = greedy_parity(tiny_model(wtype), 16, 64, 1e-3)
+def test_tiny_quant_greedy_parity(wtype, sk):
+    err, gap = greedy_parity(tiny_model(wtype), 16, 64, 1e-3, sk=sk)
     print(f"tiny {gguf.TYPE_NAMES[wtype]}: max abs err {err:.2e}, min top-2 gap {gap:.2e}")
 
 
-def test_argument_errors():
-    m = Model.load_bytes(forward_gpu_model(2))
+def test_argument_errors(sk):
+    m = Model.load_bytes(forward_gpu_model(2), step_kernel=sk)
     with pytest.raises(TalosError, match="INVALID_ARG"):
         m.forward_gpu(16, 0)  # token == vocab
     with pytest.raises(TalosError, match="INVALID_ARG"):
@@ -127,8 +134,8 @@ def test_missing_weight_is_state_error():
     ctx.close()
 
 
-def test_cap_context():
-    m = Model.load_bytes(forward_gpu_model(3))
+def test_cap_context(sk):
+    m = Model.load_bytes(forward_gpu_model(3), step_kernel=sk)
     m.cap_context(4)
     assert m.cfg.context_length == 4
     m.forward_gpu(1, 3)
@@ -137,14 +144,47 @@ def test_cap_context():
     m.close()
 
 
+def test_step_kernel_choice():
+    """AUTO takes the per-token kernel where the model fits it; head_dim 256 does
+    not (attention keeps head_dim <= 128 in registers), so AUTO falls back to the
+    layered graph and an explicit FUSED request fails as UNSUPPORTED."""
+    wide = synth.Shape(n_embd=256, n_layer=1, n_head=1, n_head_kv=1, n_ff=64, vocab=32, ctx=8)
+    data = synth.llama_bytes(wide, 5, wtype=gguf.F32)
+    m = Model.load_bytes(data)
+    assert m.ctx.step_kernel() == "layered"
+    cpu = oracle.Model(data=data)
+    assert np.max(np.abs(m.forward_gpu(3, 0) - cpu.forward(3, 0))) <= 1e-4
+    m.ctx.set_step_kernel("fused")
+    with pytest.raises(TalosError, match="UNSUPPORTED"):
+        m.forward_gpu(3, 1)
+    m.close()
+    t = Model.load_bytes(tiny_model(gguf.Q4_0))
+    assert t.ctx.step_kernel() == "fused"
+    t.close()
+
+
+def test_fused_and_layered_agree():
+    """The two launch paths compute the same step: logits within 1e-5 of each
+    other on the tiny Q4_0 model over a prompt."""
+    data = tiny_model(gguf.Q4_0)
+    a = Model.load_bytes(data, step_kernel="fused")
+    b = Model.load_bytes(data, step_kernel="layered")
+    for pos, t in enumerate(prompt(12, 4096, 9)):
+        la, lb = a.forward_gpu(t, pos), b.forward_gpu(t, pos)
+    assert np.max(np.abs(la - lb)) <= 1e-5
+    a.close()
+    b.close()
+
+
 @pytest.mark.slow
-def test_mistral_7b_shape_parity(tmp_path):
+@pytest.mark.parametrize("step_kernel", ["fused", "layered"])
+def test_mistral_7b_shape_parity(tmp_path, step_kernel):
     """BASELINE config 4 at full size: Q4_0 + Q6_K output; a short prompt and
     greedy steps against the oracle (the CPU forward reads 4 GB per token)."""
     path = str(tmp_path / "m7b.gguf")
     synth.write_llama(path, synth.with_ctx(synth.MISTRAL_7B, 64), 1, wtype=gguf.Q4_0, out_type=gguf.Q6_K)
     cpu = oracle.Model(path=path)
-    gpu = Model.load(path)
+    gpu = Model.load(path, step_kernel=step_kernel)
     toks = prompt(4, 32000, 1)
     pos, max_err = 0, 0.0
     for t in toks:
