@@ -47,7 +47,8 @@ typedef enum talos_status {
 
 enum { TALOS_F32 = 0, TALOS_Q4_0 = 2, TALOS_Q8_0 = 8, TALOS_Q6_K = 14 };
 
-/* Model hyper-parameters; field for field `Config` (src/model/config.rs:14-25). */
+/* Model hyper-parameters: the fields of `Config` (src/model/config.rs:14-25) as
+ * fixed-width C types (usize -> uint32_t); a binding copies them by name. */
 typedef struct talos_cfg {
     uint32_t n_layer;
     uint32_t n_head;

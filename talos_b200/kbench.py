@@ -1,13 +1,23 @@
-"""Single-kernel microbenchmark of the fused dequant-matvec.
+"""Kernel microbenchmarks.
+
+Matvec:
 
     python -m talos_b200.kbench [--type q4_0|q8_0|q6_k|f32] [--rows R] [--cols C]
                                 [--copies N] [--reps K] [--warmup W]
 
 Packs N distinct copies of a seeded N(0, 0.02) weight [R, C] (N chosen so that
-together they exceed twice the L2), then times K launches of talos_matvec_dev
-cycling through the copies, with CUDA events on one stream. Reports microseconds
-per matvec and algorithmic GB/s (packed weight bytes + x + y per launch).
-Default: the 4096 x 4096 Q4_0 microbench, seed 7, x ~ N(0, 1).
+together they exceed twice the L2), then times K graph-captured launches of
+talos_matvec_dev cycling through the copies. Reports microseconds per matvec
+and algorithmic GB/s (packed weight bytes + x + y per launch). Default: the
+4096 x 4096 Q4_0 microbench, seed 7, x ~ N(0, 1).
+
+Decode step on a reduced-depth model (a small case of the same kernels, for
+profiling; its weights still exceed the L2):
+
+    python -m talos_b200.kbench --step [--layers L] [--steps K] [--step-kernel fused|layered]
+
+builds the Mistral-7B shape (seed 1, Q4_0, Q6_K output) with L layers, feeds a
+16-token prompt and times K device-side greedy steps.
 """
 from __future__ import annotations
 
@@ -32,7 +42,13 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--seed", type=int, default=7)
     ap.add_argument("--device", type=int, default=0)
+    ap.add_argument("--step", action="store_true")
+    ap.add_argument("--layers", type=int, default=2)
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--step-kernel", default="auto", choices=["auto", "fused", "layered"])
     a = ap.parse_args(argv)
+    if a.step:
+        return step_bench(a)
 
     import torch
 
@@ -67,6 +83,43 @@ def main(argv=None):
     print(json.dumps(out), flush=True)
     for w in ws:
         w.close()
+    return 0
+
+
+def step_bench(a) -> int:
+    import dataclasses
+    import time
+
+    import torch
+
+    from talos_b200 import Model, build, gguf, synth
+
+    build.build()
+    torch.cuda.set_device(a.device)
+    shape = dataclasses.replace(synth.MISTRAL_7B, n_layer=a.layers, ctx=64)
+    t0 = time.time()
+    data = synth.llama_bytes(shape, 1, wtype=gguf.Q4_0, out_type=gguf.Q6_K)
+    gen_s = time.time() - t0
+    m = Model.load_bytes(data, device=a.device, step_kernel=a.step_kernel)
+    del data
+    prompt = synth.token_ids(1, 16, shape.vocab)
+    last = m.prefill(prompt, 0)
+    tok = int(np.argmax(last))
+    m.generate_greedy(tok, 16, 2)
+    stream = torch.cuda.ExternalStream(m.ctx.stream(), device=torch.device("cuda", a.device))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    m.generate_greedy(tok, 18, a.steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.steps
+    E, F, V = shape.n_embd, shape.n_ff, shape.vocab
+    wbytes = a.layers * (2 * E * E + 2 * shape.kv_dim * E + 3 * E * F) * 18 // 32 + V * E * 210 // 256
+    out = {"kernel": "decode_step", "step_kernel": m.ctx.step_kernel(), "layers": a.layers,
+           "ms_per_step": ms, "weight_bytes": wbytes, "gbs": wbytes / (ms * 1e-3) / 1e9, "model_gen_s": gen_s}
+    print(json.dumps(out), flush=True)
+    m.close()
     return 0
 
 
