@@ -7,20 +7,26 @@ output.weight in Q6_K; a 128-token uniform-random prompt (prefill, untimed),
 then batch-1 greedy decode. One step = one decoded token.
 
   value : K greedy tokens decoded on the GPU with the argmax fed back on the
-          device (talos_generate_greedy: one CUDA graph replay per token), timed
-          with CUDA events on the context's stream. Weights (4.03 GB/token) are
-          far larger than L2, so every step streams them from HBM.
+          device (talos_generate_greedy: one CUDA graph replay per token, i.e. one
+          per-token kernel launch), timed with CUDA events on the context's
+          stream. Weights (4.03 GB/token) are far larger than L2, so every step
+          streams them from HBM.
   e2e   : the same decode through the public per-token call talos_forward with
           host buffers: token/pos host->device, logits device->host and the argmax
           on the host every step (the reference's decode loop, src/main.rs:97-113).
-  roofline: the dominant kernel (fused RMSNorm + gate/up Q4_0 matvec + SwiGLU),
-          timed per launch with CUDA events from eagerly launched steps.
+  roofline: the dominant kernel: the per-token kernel k_token (one launch = one
+          token; algorithmic bytes = the token's weights + KV rows read), timed per
+          launch with CUDA events (the layered graph's gate/up kernel when steps
+          run the layered graph).
   cpu_baseline: the CPU oracle (a C restatement of the reference's rayon CPU
           forward) on this host's cores, a bounded sample of tokens.
 
 --impl reference times that CPU path alone, per token, on the same workload.
-Multi-GPU (torchrun, N > 1): replicas, one independent sequence per GPU (weak
-scaling); value = all ranks' tokens / max over ranks of the timed region.
+Multi-GPU (torchrun, N > 1): tensor parallel over the N GPUs (one process per
+GPU; heads, ff rows and vocab split, the all-reduce after o-proj and down runs
+inside the per-token kernel over peer memory). All ranks decode the same single
+sequence, so the work is fixed as N grows (strong scaling); value = tokens /
+max over ranks of the timed region.
 """
 from __future__ import annotations
 
@@ -58,6 +64,13 @@ def env_int(k, d):
 def argmax_last(v: np.ndarray) -> int:
     """sample::argmax (src/sample.rs:7-14): last maximal element on ties."""
     return int(v.size - 1 - np.argmax(v[::-1]))
+
+
+def bench_config(world: int, seq_len: int) -> dict:
+    return {"workload": "mistral-7b-shape Q4_0 (+Q6_K output), 128-token prompt then batch-1 greedy decode",
+            "model": "llama d4096 L32 h32/8 ff14336 V32000", "global_batch": 1, "seq_len": seq_len,
+            "parallelism": f"tp{world}" if world > 1 else "1 GPU",
+            "l2": "inputs larger than L2 (4.03 GB of weights per step)"}
 
 
 def model_path() -> str:
@@ -220,10 +233,9 @@ def run_reference(args):
     line = {
         "metric": "decode tok/s (batch 1, 7B-shape Q4_0)", "value": v, "unit": "tok/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": n, "steps_requested": args.steps, "warmup": warm,
-        "ms_per_step": 1000 * dt / max(n, 1), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "q4_0/f32", "data": "synthetic",
-        "config": {"workload": "mistral-7b-shape Q4_0 (+Q6_K output), batch-1 greedy decode",
-                   "global_batch": 1, "prompt": PROMPT_LEN},
+        "ms_per_step": 1000 * dt / max(n, 1), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "q4_0 weights, f32 activations/KV", "data": "synthetic",
+        "config": bench_config(args.gpus, PROMPT_LEN + warm + n),
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -269,8 +281,18 @@ def main():
         dist.barrier()
 
     K, W = args.steps, args.warmup
+    uid = None
+    if world > 1:  # rank 0's NCCL id bootstraps the tensor-parallel contexts
+        from talos_b200 import nccl_unique_id
+
+        t = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            t.copy_(torch.frombuffer(bytearray(nccl_unique_id()), dtype=torch.uint8))
+        dist.broadcast(t, src=0)
+        uid = bytes(t.cpu().numpy().tobytes())
     t_load = time.time()
-    model = Model.load(path, device=local, max_ctx=PROMPT_LEN + 2 * (K + W) + 16)
+    model = Model.load(path, device=local, max_ctx=PROMPT_LEN + 2 * (K + W) + 16, tp_size=world, tp_rank=rank,
+                       nccl_id=uid)
     load_s = time.time() - t_load
     ctx = model.ctx
     stream = torch.cuda.ExternalStream(ctx.stream(), device=torch.device("cuda", local))
@@ -299,7 +321,7 @@ def main():
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    value = world * K / (ms / 1000.0)
+    value = K / (ms / 1000.0)
     tok, pos = int(out[-1]), pos + K
     kv_avg_pos = PROMPT_LEN + W + K / 2
 
@@ -318,7 +340,7 @@ def main():
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = world * K / e2e_s
+    e2e = K / e2e_s
 
     # ---------------- per-kernel times of eagerly launched steps (roofline)
     n_prof = 4
@@ -365,12 +387,9 @@ def main():
     line = {
         "metric": "decode tok/s (batch 1, 7B-shape Q4_0)",
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "q4_0 weights, f32 activations/KV", "data": "synthetic",
-        "config": {"workload": "mistral-7b-shape Q4_0 (+Q6_K output), 128-token prompt then batch-1 greedy decode",
-                   "model": "llama d4096 L32 h32/8 ff14336 V32000", "global_batch": world, "seq_len": PROMPT_LEN + W + K,
-                   "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
-                   "l2": "inputs larger than L2 (4.03 GB of weights per step)"},
+        "config": bench_config(world, PROMPT_LEN + W + K),
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 24, "d2h_bytes_per_step": vocab * 4 + 24},
         "roofline": {"bound": "hbm", "kernel": dom_name,
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,

@@ -8,7 +8,7 @@ Public API (mirrors Tsuskov/talos ``src/model`` for the CUDA backend):
 The compute runs in libtalos_cuda.so through the C ABI of include/talos_cuda.h.
 """
 from .gguf import F32, Q4_0, Q6_K, Q8_0, GgufError, GgufFile, GgufWriter, TensorInfo
-from .model import Config, Context, Model, Weight, dequant, matvec, weight_shapes
+from .model import Config, Context, Model, Weight, dequant, matvec, nccl_unique_id, weight_shapes
 
 __all__ = ["F32", "Q4_0", "Q6_K", "Q8_0", "GgufError", "GgufFile", "GgufWriter", "TensorInfo", "Config",
-           "Context", "Model", "Weight", "dequant", "matvec", "weight_shapes"]
+           "Context", "Model", "Weight", "dequant", "matvec", "nccl_unique_id", "weight_shapes"]

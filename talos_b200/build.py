@@ -29,6 +29,11 @@ NVCC_FLAGS = [
 ]
 
 
+# NCCL (opened with dlopen at run time) bootstraps tensor-parallel contexts;
+# only its header is needed here. The all-reduce runs inside the per-token kernel.
+LINK = ["-ldl"]
+
+
 def _nvcc() -> str:
     for c in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", "nvcc"):
         if c and (os.path.isabs(c) and os.path.exists(c) or not os.path.isabs(c)):
@@ -49,7 +54,7 @@ def build_cuda(force: bool = False, verbose: bool = False) -> str:
         return CUDA_LIB
     os.makedirs(OUT, exist_ok=True)
     cmd = [_nvcc(), *NVCC_FLAGS, "-o", CUDA_LIB + ".tmp",
-           *[os.path.join(CSRC, f) for f in CU_SOURCES]]
+           *[os.path.join(CSRC, f) for f in CU_SOURCES], *LINK]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)

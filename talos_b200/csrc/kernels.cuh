@@ -22,7 +22,9 @@ cudaError_t launch_dequant(int type, const uint8_t* raw, size_t n, float* out, c
 
 // ---------------------------------------------------------------- matvec
 
-enum Epi : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_QKV = 3, EPI_LOGITS = 4 };
+// EPI_PEER (per-token kernel, tensor parallel): the tile's rows are this rank's
+// partial sums of a row-parallel matvec; they go to every rank's receive slot.
+enum Epi : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_QKV = 3, EPI_LOGITS = 4, EPI_PEER = 5 };
 
 // A run of 16-row tiles inside one matvec launch.
 //  pair == 0: tile t covers rows 16t .. 16t+15 of A (B is ignored).
@@ -101,9 +103,16 @@ struct TokenPhase {
     int type;       // PH_MATVEC: ggml type of every segment
     int embed_in;   // PH_MATVEC: the input is the token's embedding row (first phase)
     int prof_kind;  // talos_kernel_kind the phase is reported under
+    // tensor parallel (TokenArgs::tp > 1)
+    int xsum;       // input = xbuf[xsrc] + sum over ranks of rx slot xslot; CTA 0 stores it to xbuf[xdst]
+    int xsrc, xdst, xslot;
+    int rx_slot;    // EPI_PEER: receive slot written
+    int xrank;      // arrivals at this phase's barrier come from every rank
     MatvecArgs mv;  // PH_MATVEC
     AttnArgs at;    // PH_ATTN
 };
+
+constexpr int TALOS_MAX_TP = 8;
 
 struct TokenArgs {
     const TokenPhase* ph;       // device array of nph phases
@@ -125,6 +134,14 @@ struct TokenArgs {
     int union_bytes;            // staged input / attention scratch bytes
     unsigned long long* stamps; // optional [nph][grid][4] global-timer stamps (ns): phase
                                 // entered, inputs staged, compute done, barrier arrival
+    // tensor parallel: tp ranks, one per GPU; peer pointers are CUDA IPC mappings
+    int tp, rank;
+    unsigned long long* pbars[TALOS_MAX_TP];  // each rank's barrier counters (own: bars)
+    float* prx[TALOS_MAX_TP];                 // each rank's receive slots [2][tp][E]
+    float* plogits[TALOS_MAX_TP];             // each rank's full logits [vocab]
+    unsigned long long* pkey[TALOS_MAX_TP];   // each rank's StepParams::argmax_key
+    int vocab_off;                            // first vocab row of this rank's output shard
+    float* xbuf[2];                           // residual stream, double-buffered (tp > 1)
 };
 
 // Staged-input elements the k_token scratch region must hold for input length K.

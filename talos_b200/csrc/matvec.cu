@@ -967,14 +967,32 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
 __device__ __forceinline__ void red_release_add_u64(unsigned long long* p, unsigned long long v) {
     asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+// System scope: counters that CTAs on other GPUs (tensor-parallel ranks) add to.
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_sys_add_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 // Bounded spin of one thread until *bar >= target.
-__device__ __noinline__ bool grid_wait_one(const unsigned long long* bar, unsigned long long target) {
-    if (ld_acquire_u64(bar) >= target) return true;
+__device__ __noinline__ bool grid_wait_one(const unsigned long long* bar, unsigned long long target, bool sys) {
+    auto ld = [&]() { return sys ? ld_acquire_sys_u64(bar) : ld_acquire_u64(bar); };
+    if (ld() >= target) return true;
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
         for (int i = 0; i < 16; ++i)
-            if (ld_acquire_u64(bar) >= target) return true;
+            if (ld() >= target) return true;
         if (globaltimer_ns() - t0 > TK_WAIT_NS) return false;
+    }
+}
+// One CTA's arrival at phase p's barrier: on this GPU, or (xrank) on every rank.
+__device__ __forceinline__ void tk_arrive(const TokenArgs& a, int p, bool xrank) {
+    if (xrank) {
+        for (int r = 0; r < a.tp; ++r) red_release_sys_add_u64(a.pbars[r] + p, 1ull);
+    } else {
+        red_release_add_u64(&a.bars[p], 1ull);
     }
 }
 // Bounded spin until the shared counter reaches v.
@@ -1072,17 +1090,32 @@ __device__ __forceinline__ void tk_stage(const TokenArgs& a, const TokenPhase& P
     const uint8_t* erow = nullptr;
     if (P.embed_in)
         erow = a.embd + (size_t)tok * (K / gguf_block_elems(a.embd_type)) * gguf_block_bytes(a.embd_type);
+    // tensor parallel: x = xbuf[xsrc] + the ranks' partial sums, in rank order
+    // (every rank computes the same bits); CTA 0 keeps it in xbuf[xdst]
+    const bool xs = a.tp > 1 && P.xsum && !erow;
+    const float* xsrc = xs ? a.xbuf[P.xsrc] : nullptr;
+    const float* rxs = xs ? a.prx[a.rank] + (size_t)P.xslot * a.tp * a.E : nullptr;
     auto load4 = [&](int e0) -> float4 {
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (erow) {
+        if (xs) {
+            if (e0 < K) {  // K = E, a multiple of 4
+                v = __ldcg((const float4*)(xsrc + e0));
+                for (int r = 0; r < a.tp; ++r) {
+                    const float4 d = __ldcg((const float4*)(rxs + (size_t)r * a.E + e0));
+                    v = make_float4(v.x + d.x, v.y + d.y, v.z + d.z, v.w + d.w);
+                }
+                if (blockIdx.x == 0) *(float4*)(a.xbuf[P.xdst] + e0) = v;
+            }
+        } else if (erow) {
             float t[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) t[i] = e0 + i < K ? dequant_elem(a.embd_type, erow, e0 + i) : 0.f;
             v = make_float4(t[0], t[1], t[2], t[3]);
             if (blockIdx.x == 0 && e0 < K) {  // the residual stream starts as the embedding
+                float* x0 = a.tp > 1 ? a.xbuf[P.xdst] : a.x;
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
-                    if (e0 + i < K) a.x[e0 + i] = t[i];
+                    if (e0 + i < K) x0[e0 + i] = t[i];
             }
         } else if (e0 + 4 <= K && !(K & 3)) {
             v = __ldcg((const float4*)(m.x + e0));
@@ -1353,12 +1386,23 @@ __device__ __noinline__ void tk_attention(const TokenArgs& a, const AttnArgs& A,
 }
 
 // Final norm to the hidden state (src/model/llama.rs:181), CTA 0 only.
-__device__ __noinline__ void tk_hidden(const TokenArgs& a, float* red) {
+__device__ __noinline__ void tk_hidden(const TokenArgs& a, const TokenPhase& P, float* red) {
     if (blockIdx.x != 0) return;
     const int tid = threadIdx.x;
+    float* x = a.x;
+    if (a.tp > 1 && P.xsum) {  // the last down-proj's partial sums, as in tk_stage
+        x = a.xbuf[P.xdst];
+        const float* rxs = a.prx[a.rank] + (size_t)P.xslot * a.tp * a.E;
+        for (int k = tid; k < a.E; k += MV_CONSUMERS) {
+            float v = __ldcg(a.xbuf[P.xsrc] + k);
+            for (int r = 0; r < a.tp; ++r) v += __ldcg(rxs + (size_t)r * a.E + k);
+            x[k] = v;
+        }
+        consumer_sync();
+    }
     float ss = 0.f;
     for (int k = tid; k < a.E; k += MV_CONSUMERS) {
-        const float v = __ldcg(a.x + k);
+        const float v = __ldcg(x + k);
         ss = fmaf(v, v, ss);
     }
     ss = warp_sum(ss);
@@ -1368,7 +1412,7 @@ __device__ __noinline__ void tk_hidden(const TokenArgs& a, float* red) {
     for (int w = 0; w < MV_CWARPS; ++w) tot += red[w];
     const float scale = 1.0f / sqrtf(tot / (float)a.E + a.eps);
     for (int k = tid; k < a.E; k += MV_CONSUMERS)
-        a.hidden[k] = __fmul_rn(__fmul_rn(__ldcg(a.x + k), scale), a.out_norm[k]);
+        a.hidden[k] = __fmul_rn(__fmul_rn(__ldcg(x + k), scale), a.out_norm[k]);
 }
 
 __device__ __forceinline__ void tk_tile_src(const Seg& sg, int lt, int c, int gcb, const uint8_t*& pa,
@@ -1456,14 +1500,41 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
                 if (lane == 0) mbar_arrive(&tfree[b]);
                 if (lane < 16) res[lane] = v;
                 __syncwarp();
-                apply_epilogue(m, sg, lt, res, pos, lane, pre);
+                if (m.epi == EPI_PEER) {
+                    // this rank's partial rows to every rank's receive slot (all-reduce, one shot)
+                    const int row = 16 * lt + lane;
+                    if (lane < 16 && row < sg.out_rows)
+                        for (int r = 0; r < a.tp; ++r)
+                            a.prx[r][((size_t)P.rx_slot * a.tp + a.rank) * a.E + row] = res[lane];
+                } else if (m.epi == EPI_LOGITS && a.tp > 1) {
+                    // this rank's vocab shard to every rank's logits, argmax over global indices
+                    unsigned long long key = 0ull;
+                    const int row = 16 * lt + lane;
+                    if (lane < 16 && row < sg.out_rows) {
+                        const int g = a.vocab_off + row;
+                        for (int r = 0; r < a.tp; ++r) a.plogits[r][g] = res[lane];
+                        key = ((unsigned long long)total_order_key(res[lane]) << 32) | (unsigned)g;
+                    }
+#pragma unroll
+                    for (int o = 8; o > 0; o >>= 1) {
+                        const unsigned long long oth = __shfl_xor_sync(0xffffffffu, key, o);
+                        key = oth > key ? oth : key;
+                    }
+                    if (lane == 0 && key)
+                        for (int r = 0; r < a.tp; ++r) atomicMax(a.pkey[r], key);
+                } else {
+                    apply_epilogue(m, sg, lt, res, pos, lane, pre);
+                }
                 __syncwarp();
             }
-            if (p + 1 < a.nph) {
-                __threadfence();
+            if (p + 1 < a.nph || a.tp > 1) {
+                if (P.xrank)
+                    __threadfence_system();
+                else
+                    __threadfence();
                 __syncwarp();
                 if (lane == 0) {
-                    red_release_add_u64(&a.bars[p], 1ull);
+                    tk_arrive(a, p, P.xrank != 0);
                     tk_stamp(a, p, 3);
                 }
             }
@@ -1520,7 +1591,8 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
         const TokenPhase& P = a.ph[p];
         if (p > 0) {
             if (tid == 0) {
-                if (!grid_wait_one(&a.bars[p - 1], target)) tk_fail(a, &sh, 4u);
+                const bool xr = a.ph[p - 1].xrank != 0;
+                if (!grid_wait_one(&a.bars[p - 1], xr ? target * (unsigned)a.tp : target, xr)) tk_fail(a, &sh, 4u);
                 __threadfence();
                 *(volatile int*)&sh.started = p;
                 sh.stop = *(volatile int*)&sh.err;
@@ -1562,11 +1634,21 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
                 tk_stamp(a, p, 3);
             }
         } else {
-            tk_hidden(a, red);
+            tk_hidden(a, P, red);
+            consumer_sync();
+            if (tid == 0 && a.tp > 1) {
+                __threadfence_system();
+                tk_arrive(a, p, P.xrank != 0);
+            }
         }
     }
-    // every CTA has read the epoch once it arrived at the last barrier
-    if (tid == 0 && blockIdx.x == 0 && !*(volatile int*)&sh.err) atomicAdd(a.epoch, 1ull);
+    if (tid == 0 && blockIdx.x == 0 && !*(volatile int*)&sh.err) {
+        // tensor parallel: the kernel ends only when every rank's last phase (its
+        // stores into this rank's logits and argmax key) is done
+        if (a.tp > 1 && !grid_wait_one(&a.bars[a.nph - 1], target * (unsigned)a.tp, true)) tk_fail(a, &sh, 4u);
+        // every CTA has read the epoch once it arrived at the last barrier
+        atomicAdd(a.epoch, 1ull);
+    }
 }
 
 int token_stage_elems(int type, int K) {

@@ -17,16 +17,53 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <memory>
 #include <mutex>
 #include <string>
 #include <unordered_map>
 #include <vector>
 
+#include <dlfcn.h>
+#include <nccl.h>
+
 #include "../../include/talos_cuda.h"
 #include "kernels.cuh"
 
 using namespace talos;
+
+// ------------------------------------------------------------------ NCCL, opened on first use
+//
+// NCCL only bootstraps tensor-parallel contexts, so it is opened with dlopen
+// when the first one is made instead of being linked: a process that also loads
+// PyTorch gets one NCCL (an already loaded libnccl.so.2 is reused), and the
+// library still loads where NCCL is absent.
+
+struct NcclApi {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*);
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int);
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*CommDestroy)(ncclComm_t);
+    const char* (*GetErrorString)(ncclResult_t);
+    bool ok;
+};
+
+static const NcclApi& nccl() {
+    static NcclApi api = [] {
+        NcclApi a{};
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return a;
+        a.GetUniqueId = (decltype(a.GetUniqueId))dlsym(h, "ncclGetUniqueId");
+        a.CommInitRank = (decltype(a.CommInitRank))dlsym(h, "ncclCommInitRank");
+        a.AllGather = (decltype(a.AllGather))dlsym(h, "ncclAllGather");
+        a.CommDestroy = (decltype(a.CommDestroy))dlsym(h, "ncclCommDestroy");
+        a.GetErrorString = (decltype(a.GetErrorString))dlsym(h, "ncclGetErrorString");
+        a.ok = a.GetUniqueId && a.CommInitRank && a.AllGather && a.CommDestroy && a.GetErrorString;
+        return a;
+    }();
+    return api;
+}
 
 // ------------------------------------------------------------------ errors
 
@@ -210,6 +247,15 @@ struct talos_ctx {
     int device = 0;
     cudaStream_t stream = nullptr;
     int hd = 0, kv_dim = 0, group = 0;
+    // tensor parallelism: this rank's share of heads, kv heads, ff rows and vocab
+    // (all equal to the full sizes when tp == 1)
+    int tp = 1, rank = 0;
+    int nh_l = 0, nkv_l = 0, q_rows = 0, kv_l = 0, ff_l = 0, v_l = 0, v_off = 0;
+    ncclComm_t comm = nullptr;
+    void* shared = nullptr;  // tp > 1: IPC-exported {bars, StepParams, rx slots, logits}
+    size_t shared_bytes = 0, shared_bars_bytes = 0;
+    void* peer_base[TALOS_MAX_TP] = {};
+    float* xbuf[2] = {nullptr, nullptr};
     size_t kv_ctx = 0;  // positions the KV cache holds
 
     std::unordered_map<std::string, DevTensor> w;         // model weights by GGUF name
@@ -326,7 +372,7 @@ static talos_status alloc_kv(talos_ctx* c) {
     if (c->rope_cs) cudaFree(c->rope_cs);
     c->kcache = c->vcache = nullptr;
     c->rope_cs = nullptr;
-    size_t per = (size_t)c->cfg.n_layer * c->kv_ctx * c->kv_dim * sizeof(float);
+    size_t per = (size_t)c->cfg.n_layer * c->kv_ctx * c->kv_l * sizeof(float);
     CK(cudaMalloc(&c->kcache, per ? per : 4));
     CK(cudaMalloc(&c->vcache, per ? per : 4));
     CK(cudaMemsetAsync(c->kcache, 0, per ? per : 4, c->stream));
@@ -366,7 +412,8 @@ static talos_status alloc_arena(talos_ctx* c) {
         return o;
     };
     size_t o_x = take(E * 4), o_q = take(E * 4 + 64), o_att = take(E * 4), o_ff = take(F * 4),
-           o_log = take(V * 4), o_hid = take(E * 4), o_step = take(sizeof(StepParams));
+           o_log = take(V * 4), o_hid = take(E * 4), o_step = take(sizeof(StepParams)), o_xb0 = take(E * 4),
+           o_xb1 = take(E * 4);
     CK(cudaMalloc(&c->arena, off));
     CK(cudaMemsetAsync(c->arena, 0, off, c->stream));
     c->arena_bytes = off;
@@ -378,6 +425,8 @@ static talos_status alloc_arena(talos_ctx* c) {
     c->logits = (float*)(b + o_log);
     c->hidden = (float*)(b + o_hid);
     c->step = (StepParams*)(b + o_step);
+    c->xbuf[0] = (float*)(b + o_xb0);
+    c->xbuf[1] = (float*)(b + o_xb1);
     CK(cudaMallocHost(&c->h_out, (V > E ? V : E) * sizeof(float)));
     CK(cudaMallocHost(&c->h_step, sizeof(StepParams)));
     CK(cudaStreamSynchronize(c->stream));
@@ -388,7 +437,7 @@ static talos_status alloc_arena(talos_ctx* c) {
 // k_token, zeroed.
 static talos_status alloc_sync(talos_ctx* c) {
     const int sms = (c->device < 64 && g_sms[c->device]) ? g_sms[c->device] : 148;
-    c->nsplit = sms / (int)c->cfg.n_head_kv;
+    c->nsplit = sms / c->nkv_l;
     if (c->nsplit < 1) c->nsplit = 1;
     c->nph_max = (int)c->cfg.n_layer * 5 + 1;
     size_t off = 0;
@@ -399,8 +448,8 @@ static talos_status alloc_sync(talos_ctx* c) {
     };
     const size_t o_bars = take((size_t)c->nph_max * 8), o_epoch = take(8),
                  o_stamps = take((size_t)c->nph_max * sms * 4 * 8),
-                 o_cnt = take((size_t)c->cfg.n_head_kv * 4),
-                 o_part = take((size_t)c->cfg.n_head * c->nsplit * (c->hd + 2) * 4);
+                 o_cnt = take((size_t)c->nkv_l * 4),
+                 o_part = take((size_t)c->nh_l * c->nsplit * (c->hd + 2) * 4);
     CK(cudaMalloc(&c->sync_mem, off));
     c->sync_bytes = off;
     uint8_t* b = (uint8_t*)c->sync_mem;
@@ -419,11 +468,73 @@ static talos_status alloc_sync(talos_ctx* c) {
 static void reset_sync(talos_ctx* c) {
     if (c->sync_mem) {
         cudaMemsetAsync(c->sync_mem, 0, c->sync_bytes, c->stream);
+        if (c->shared) cudaMemsetAsync(c->shared, 0, c->shared_bars_bytes, c->stream);
         cudaStreamSynchronize(c->stream);
     }
 }
 
-extern "C" talos_status talos_ctx_create(const talos_cfg* cfg, int device, talos_ctx** out) {
+// Tensor parallel: the area other ranks write into (barrier counters, step
+// parameters with the argmax key, all-reduce receive slots [2][tp][E], full
+// logits), exported by CUDA IPC and mapped by every rank. The handles and the
+// GPUs' PCI ids travel over one NCCL all-gather.
+static talos_status alloc_shared(talos_ctx* c) {
+    const size_t E = c->cfg.n_embd, V = c->cfg.vocab_size;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off += align256(bytes);
+        return o;
+    };
+    const size_t o_bars = take((size_t)c->nph_max * 8);
+    c->shared_bars_bytes = off;
+    const size_t o_step = take(sizeof(StepParams)), o_rx = take(2 * (size_t)c->tp * E * 4), o_log = take(V * 4);
+    CK(cudaMalloc(&c->shared, off));
+    c->shared_bytes = off;
+    CK(cudaMemset(c->shared, 0, off));
+    uint8_t* b = (uint8_t*)c->shared;
+    c->bars = (unsigned long long*)(b + o_bars);
+    c->step = (StepParams*)(b + o_step);
+    c->logits = (float*)(b + o_log);
+    (void)o_rx;
+
+    struct Xch {
+        cudaIpcMemHandle_t h;
+        int pci_domain, pci_bus, pci_dev, pad;
+    };
+    Xch me{};
+    CK(cudaIpcGetMemHandle(&me.h, c->shared));
+    CK(cudaDeviceGetAttribute(&me.pci_domain, cudaDevAttrPciDomainId, c->device));
+    CK(cudaDeviceGetAttribute(&me.pci_bus, cudaDevAttrPciBusId, c->device));
+    CK(cudaDeviceGetAttribute(&me.pci_dev, cudaDevAttrPciDeviceId, c->device));
+    void* d = nullptr;
+    CK(cudaMalloc(&d, sizeof(Xch) * (c->tp + 1)));
+    CK(cudaMemcpy(d, &me, sizeof me, cudaMemcpyHostToDevice));
+    ncclResult_t nr = nccl().AllGather(d, (uint8_t*)d + sizeof(Xch), sizeof(Xch), ncclUint8, c->comm, c->stream);
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    std::vector<Xch> all(c->tp);
+    if (nr == ncclSuccess && e == cudaSuccess)
+        e = cudaMemcpy(all.data(), (uint8_t*)d + sizeof(Xch), sizeof(Xch) * c->tp, cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    if (nr != ncclSuccess)
+        return set_err(TALOS_ERR_NCCL, "all-gather of IPC handles: %s", nccl().GetErrorString(nr));
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "all-gather of IPC handles: %s", cudaGetErrorString(e));
+    for (int r = 0; r < c->tp; ++r)
+        for (int q = 0; q < r; ++q)
+            if (all[r].pci_domain == all[q].pci_domain && all[r].pci_bus == all[q].pci_bus &&
+                all[r].pci_dev == all[q].pci_dev)
+                return set_err(TALOS_ERR_UNSUPPORTED, "ranks %d and %d share one GPU (one rank per GPU)", q, r);
+    for (int r = 0; r < c->tp; ++r) {
+        if (r == c->rank) {
+            c->peer_base[r] = c->shared;
+            continue;
+        }
+        CK(cudaIpcOpenMemHandle(&c->peer_base[r], all[r].h, cudaIpcMemLazyEnablePeerAccess));
+    }
+    return TALOS_OK;
+}
+
+static talos_status ctx_create(const talos_cfg* cfg, int device, int tp, int rank, const uint8_t* id,
+                               talos_ctx** out) {
     if (!cfg || !out) return set_err(TALOS_ERR_INVALID_ARG, "cfg/out is NULL");
     *out = nullptr;
     if (cfg->n_head_kv == 0 || cfg->n_head == 0 || cfg->n_head % cfg->n_head_kv)
@@ -447,6 +558,14 @@ extern "C" talos_status talos_ctx_create(const talos_cfg* cfg, int device, talos
         return set_err(TALOS_ERR_UNSUPPORTED,
                        "head_dim %u / group %u outside this build (head_dim a multiple of 4, <= 256; "
                        "group <= 8; group * head_dim <= 1024)", hd, grp);
+    if (tp != 1) {
+        if (tp != 2 && tp != 4 && tp != 8) return set_err(TALOS_ERR_INVALID_ARG, "tp_size %d (1, 2, 4 or 8)", tp);
+        if (rank < 0 || rank >= tp) return set_err(TALOS_ERR_INVALID_ARG, "tp_rank %d of %d", rank, tp);
+        if (!id) return set_err(TALOS_ERR_INVALID_ARG, "NCCL unique id is NULL");
+        if (cfg->n_head_kv % tp || cfg->n_ff % tp)
+            return set_err(TALOS_ERR_UNSUPPORTED, "n_head_kv %u and n_ff %u must split evenly over %d ranks",
+                           cfg->n_head_kv, cfg->n_ff, tp);
+    }
     TRY(device_setup(device));
     std::unique_ptr<talos_ctx> c(new talos_ctx());
     c->cfg = *cfg;
@@ -455,12 +574,39 @@ extern "C" talos_status talos_ctx_create(const talos_cfg* cfg, int device, talos
     c->kv_dim = (int)(cfg->n_head_kv * hd);
     c->group = (int)(cfg->n_head / cfg->n_head_kv);
     c->kv_ctx = cfg->context_length;
+    c->tp = tp;
+    c->rank = rank;
+    c->nh_l = (int)cfg->n_head / tp;
+    c->nkv_l = (int)cfg->n_head_kv / tp;
+    c->q_rows = c->nh_l * (int)hd;
+    c->kv_l = c->nkv_l * (int)hd;
+    c->ff_l = (int)cfg->n_ff / tp;
+    const int vchunk = ((int)cfg->vocab_size + tp - 1) / tp;
+    c->v_off = rank * vchunk;
+    c->v_l = std::min(vchunk, (int)cfg->vocab_size - c->v_off);
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     TRY(alloc_arena(c.get()));
     TRY(alloc_kv(c.get()));
     TRY(alloc_sync(c.get()));
+    if (tp > 1) {
+        ncclUniqueId uid;
+        static_assert(sizeof(uid.internal) == 128, "NCCL unique id size");
+        memcpy(uid.internal, id, 128);
+        if (!nccl().ok) return set_err(TALOS_ERR_NCCL, "libnccl.so.2 could not be opened");
+        ncclResult_t nr = nccl().CommInitRank(&c->comm, tp, uid, rank);
+        if (nr != ncclSuccess) return set_err(TALOS_ERR_NCCL, "ncclCommInitRank: %s", nccl().GetErrorString(nr));
+        talos_status st = alloc_shared(c.get());
+        if (st != TALOS_OK) {
+            talos_ctx_destroy(c.release());
+            return st;
+        }
+    }
     *out = c.release();
     return TALOS_OK;
+}
+
+extern "C" talos_status talos_ctx_create(const talos_cfg* cfg, int device, talos_ctx** out) {
+    return ctx_create(cfg, device, 1, 0, nullptr, out);
 }
 
 extern "C" talos_status talos_ctx_destroy(talos_ctx* c) {
@@ -471,6 +617,10 @@ extern "C" talos_status talos_ctx_destroy(talos_ctx* c) {
     for (auto& kv : c->w) kv.second.release();
     for (auto& kv : c->resident) kv.second.release();
     c->staging.release();
+    for (int r = 0; r < TALOS_MAX_TP; ++r)
+        if (c->peer_base[r] && r != c->rank) cudaIpcCloseMemHandle(c->peer_base[r]);
+    if (c->shared) cudaFree(c->shared);
+    if (c->comm) nccl().CommDestroy(c->comm);
     if (c->arena) cudaFree(c->arena);
     if (c->sync_mem) cudaFree(c->sync_mem);
     if (c->kcache) cudaFree(c->kcache);
@@ -507,6 +657,38 @@ extern "C" talos_status talos_weight_upload(talos_ctx* c, const char* name, cons
         if (!want) return set_err(TALOS_ERR_UNSUPPORTED, "\"%s\": ggml type %d with %zu cols", name, type, cols);
         if (len != want)
             return set_err(TALOS_ERR_INVALID_ARG, "\"%s\": %zu bytes, expected %zu", name, len, want);
+    }
+    std::vector<uint8_t> shard;
+    if (c->tp > 1 && !is_norm && nm != "token_embd.weight") {
+        // this rank's shard: column-parallel q/k/v/gate/up/output keep a row
+        // range, row-parallel o/down a column range (whole ggml blocks)
+        const std::string rest = nm.compare(0, 4, "blk.") == 0 ? nm.substr(nm.find('.', 4) + 1) : nm;
+        size_t r0 = 0, r1 = rows, c0 = 0, c1 = cols;
+        if (rest == "attn_q.weight") {
+            r0 = (size_t)c->rank * c->q_rows, r1 = r0 + c->q_rows;
+        } else if (rest == "attn_k.weight" || rest == "attn_v.weight") {
+            r0 = (size_t)c->rank * c->kv_l, r1 = r0 + c->kv_l;
+        } else if (rest == "ffn_gate.weight" || rest == "ffn_up.weight") {
+            r0 = (size_t)c->rank * c->ff_l, r1 = r0 + c->ff_l;
+        } else if (rest == "output.weight") {
+            r0 = (size_t)c->v_off, r1 = r0 + c->v_l;
+        } else if (rest == "attn_output.weight") {
+            c0 = (size_t)c->rank * c->q_rows, c1 = c0 + c->q_rows;
+        } else if (rest == "ffn_down.weight") {
+            c0 = (size_t)c->rank * c->ff_l, c1 = c0 + c->ff_l;
+        }
+        const size_t be = (size_t)gguf_block_elems(type), bb = (size_t)gguf_block_bytes(type);
+        if (c0 % be || c1 % be)
+            return set_err(TALOS_ERR_UNSUPPORTED, "\"%s\": rank %d's columns %zu..%zu are not whole %zu-element blocks",
+                           name, c->rank, c0, c1, be);
+        const size_t rb = cols / be * bb, sb0 = c0 / be * bb, sbn = (c1 - c0) / be * bb;
+        shard.resize((r1 - r0) * sbn);
+        for (size_t r = r0; r < r1; ++r)
+            memcpy(shard.data() + (r - r0) * sbn, (const uint8_t*)bytes + r * rb + sb0, sbn);
+        bytes = shard.data();
+        len = shard.size();
+        rows = r1 - r0;
+        cols = c1 - c0;
     }
     DevTensor& t = c->w[nm];
     if (is_norm || nm == "token_embd.weight") {
@@ -750,8 +932,18 @@ static talos_status enqueue_step(talos_ctx* c, GraphMode mode) {
 // The phases of one step for k_token (llama.rs:96-183, then :89 or :181).
 static void build_phases(talos_ctx* c, GraphMode mode, std::vector<TokenPhase>& ph) {
     const talos_cfg& cfg = c->cfg;
-    const int E = (int)cfg.n_embd, F = (int)cfg.n_ff;
-    const size_t kv_layer = c->kv_ctx * (size_t)c->kv_dim;
+    const int E = (int)cfg.n_embd;
+    const bool tp = c->tp > 1;
+    const size_t kv_layer = c->kv_ctx * (size_t)c->kv_l;
+    // tensor parallel: the residual stream alternates between xbuf[0] (written by
+    // q/k/v staging) and xbuf[1] (written by gate/up staging); the o-proj partials
+    // go to receive slot 0, the down partials to slot 1
+    auto xsum = [&](TokenPhase& p, int src, int dst, int slot) {
+        p.xsum = tp;
+        p.xsrc = src;
+        p.xdst = dst;
+        p.xslot = slot;
+    };
     ph.clear();
     for (uint32_t l = 0; l < cfg.n_layer; ++l) {
         const LayerW& L = c->layers[l];
@@ -763,6 +955,7 @@ static void build_phases(talos_ctx* c, GraphMode mode, std::vector<TokenPhase>& 
         p.type = L.q->type;
         p.embed_in = l == 0;
         p.prof_kind = TALOS_K_QKV;
+        xsum(p, 1, 0, 1);
         p.mv.K = E;
         p.mv.x = c->x;
         p.mv.norm_w = (const float*)L.attn_norm->mem;
@@ -771,12 +964,12 @@ static void build_phases(talos_ctx* c, GraphMode mode, std::vector<TokenPhase>& 
         p.mv.step = c->step;
         p.mv.kcache = kc;
         p.mv.vcache = vc;
-        p.mv.kv_dim = c->kv_dim;
+        p.mv.kv_dim = c->kv_l;
         p.mv.hd = c->hd;
         p.mv.rope_cs = c->rope_cs;
-        p.mv.seg[p.mv.nseg++] = make_seg(L.q, nullptr, 0, c->q, E, 0);
-        p.mv.seg[p.mv.nseg++] = make_seg(L.k, nullptr, 0, nullptr, c->kv_dim, 1);
-        p.mv.seg[p.mv.nseg++] = make_seg(L.v, nullptr, 0, nullptr, c->kv_dim, 2);
+        p.mv.seg[p.mv.nseg++] = make_seg(L.q, nullptr, 0, c->q, c->q_rows, 0);
+        p.mv.seg[p.mv.nseg++] = make_seg(L.k, nullptr, 0, nullptr, c->kv_l, 1);
+        p.mv.seg[p.mv.nseg++] = make_seg(L.v, nullptr, 0, nullptr, c->kv_l, 2);
         ph.push_back(p);
         // attention (llama.rs:135-155)
         p = TokenPhase{};
@@ -787,10 +980,10 @@ static void build_phases(talos_ctx* c, GraphMode mode, std::vector<TokenPhase>& 
         p.at.vc = vc;
         p.at.out = c->att;
         p.at.step = c->step;
-        p.at.n_head = (int)cfg.n_head;
-        p.at.n_kv = (int)cfg.n_head_kv;
+        p.at.n_head = c->nh_l;
+        p.at.n_kv = c->nkv_l;
         p.at.hd = c->hd;
-        p.at.kv_dim = c->kv_dim;
+        p.at.kv_dim = c->kv_l;
         p.at.scale = 1.0f / sqrtf((float)c->hd);
         ph.push_back(p);
         // o-proj + residual (llama.rs:157-161)
@@ -798,9 +991,11 @@ static void build_phases(talos_ctx* c, GraphMode mode, std::vector<TokenPhase>& 
         p.kind = PH_MATVEC;
         p.type = L.o->type;
         p.prof_kind = TALOS_K_OPROJ;
-        p.mv.K = E;
+        p.mv.K = c->q_rows;
         p.mv.x = c->att;
-        p.mv.epi = EPI_ADD;
+        p.mv.epi = tp ? EPI_PEER : EPI_ADD;
+        p.rx_slot = 0;
+        p.xrank = tp;
         p.mv.step = c->step;
         p.mv.seg[p.mv.nseg++] = make_seg(L.o, nullptr, 0, c->x, E, 0);
         ph.push_back(p);
@@ -809,28 +1004,33 @@ static void build_phases(talos_ctx* c, GraphMode mode, std::vector<TokenPhase>& 
         p.kind = PH_MATVEC;
         p.type = L.gate->type;
         p.prof_kind = TALOS_K_GATEUP;
+        xsum(p, 0, 1, 0);
         p.mv.K = E;
         p.mv.x = c->x;
         p.mv.norm_w = (const float*)L.ffn_norm->mem;
         p.mv.eps = cfg.rms_eps;
         p.mv.epi = EPI_SWIGLU;
         p.mv.step = c->step;
-        p.mv.seg[p.mv.nseg++] = make_seg(L.gate, L.up, 1, c->ff, F, 0);
+        p.mv.seg[p.mv.nseg++] = make_seg(L.gate, L.up, 1, c->ff, c->ff_l, 0);
         ph.push_back(p);
         // down + residual (llama.rs:172-176)
         p = TokenPhase{};
         p.kind = PH_MATVEC;
         p.type = L.down->type;
         p.prof_kind = TALOS_K_DOWN;
-        p.mv.K = F;
+        p.mv.K = c->ff_l;
         p.mv.x = c->ff;
-        p.mv.epi = EPI_ADD;
+        p.mv.epi = tp ? EPI_PEER : EPI_ADD;
+        p.rx_slot = 1;
+        p.xrank = tp;
         p.mv.step = c->step;
         p.mv.seg[p.mv.nseg++] = make_seg(L.down, nullptr, 0, c->x, E, 0);
         ph.push_back(p);
     }
     TokenPhase p{};
     p.prof_kind = TALOS_K_OUTPUT;
+    xsum(p, 1, 0, 1);
+    p.xrank = tp;  // tensor parallel: a last barrier over every rank (logits, argmax key)
     if (mode == GM_HIDDEN) {
         p.kind = PH_HIDDEN;  // final rmsnorm (llama.rs:181)
     } else {                 // final rmsnorm + output projection (llama.rs:181, :89)
@@ -844,7 +1044,7 @@ static void build_phases(talos_ctx* c, GraphMode mode, std::vector<TokenPhase>& 
         p.mv.eps = cfg.rms_eps;
         p.mv.epi = EPI_LOGITS;
         p.mv.step = c->step;
-        p.mv.seg[p.mv.nseg++] = make_seg(&ow, nullptr, 0, c->logits, (int)cfg.vocab_size, 0);
+        p.mv.seg[p.mv.nseg++] = make_seg(&ow, nullptr, 0, c->logits, c->v_l, 0);
     }
     ph.push_back(p);
     for (auto& q : ph) {
@@ -900,6 +1100,15 @@ static void fused_check(talos_ctx* c) {
 
 static talos_status use_fused(talos_ctx* c, bool* out) {
     *out = false;
+    if (c->tp > 1) {  // the all-reduce lives inside the per-token kernel
+        if (c->step_pref == TALOS_STEP_LAYERED)
+            return set_err(TALOS_ERR_UNSUPPORTED, "tensor parallel steps run the per-token kernel only");
+        if (!c->fused_why.empty())
+            return set_err(TALOS_ERR_UNSUPPORTED, "tensor parallel: the per-token kernel cannot run this model: %s",
+                           c->fused_why.c_str());
+        *out = true;
+        return TALOS_OK;
+    }
     if (c->step_pref == TALOS_STEP_LAYERED) return TALOS_OK;
     if (c->fused_why.empty()) {
         *out = true;
@@ -932,6 +1141,25 @@ static TokenArgs token_args(talos_ctx* c, GraphMode mode, unsigned long long* st
     a.nst = c->tk_nst;
     a.union_bytes = c->tk_union;
     a.stamps = stamps;
+    a.tp = c->tp;
+    a.rank = c->rank;
+    a.vocab_off = c->v_off;
+    a.xbuf[0] = c->xbuf[0];
+    a.xbuf[1] = c->xbuf[1];
+    if (c->tp > 1) {
+        // peer addresses: the same offsets inside every rank's shared area
+        const size_t o_bars = (uint8_t*)c->bars - (uint8_t*)c->shared;
+        const size_t o_key = (uint8_t*)&c->step->argmax_key - (uint8_t*)c->shared;
+        const size_t o_log = (uint8_t*)c->logits - (uint8_t*)c->shared;
+        const size_t o_rx = align256((size_t)c->nph_max * 8) + align256(sizeof(StepParams));
+        for (int r = 0; r < c->tp; ++r) {
+            uint8_t* b = (uint8_t*)c->peer_base[r];
+            a.pbars[r] = (unsigned long long*)(b + o_bars);
+            a.pkey[r] = (unsigned long long*)(b + o_key);
+            a.plogits[r] = (float*)(b + o_log);
+            a.prx[r] = (float*)(b + o_rx);
+        }
+    }
     return a;
 }
 
@@ -1220,18 +1448,21 @@ extern "C" talos_status talos_profile_step(talos_ctx* c, uint32_t token, size_t 
     return st;
 }
 
-// ------------------------------------------------------------------ tensor parallel (not yet)
+// ------------------------------------------------------------------ tensor parallel
 
 extern "C" talos_status talos_nccl_unique_id(uint8_t out[128]) {
-    (void)out;
-    return set_err(TALOS_ERR_UNSUPPORTED, "tensor parallelism is not in this build");
+    if (!out) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    ncclUniqueId uid;
+    if (!nccl().ok) return set_err(TALOS_ERR_NCCL, "libnccl.so.2 could not be opened");
+    ncclResult_t nr = nccl().GetUniqueId(&uid);
+    if (nr != ncclSuccess) return set_err(TALOS_ERR_NCCL, "ncclGetUniqueId: %s", nccl().GetErrorString(nr));
+    memcpy(out, uid.internal, 128);
+    return TALOS_OK;
 }
 
 extern "C" talos_status talos_ctx_create_tp(const talos_cfg* cfg, int device, int tp_size, int tp_rank,
                                             const uint8_t* id, talos_ctx** out) {
-    if (tp_size == 1 && tp_rank == 0) return talos_ctx_create(cfg, device, out);
-    (void)id;
-    return set_err(TALOS_ERR_UNSUPPORTED, "tensor parallelism is not in this build");
+    return ctx_create(cfg, device, tp_size, tp_rank, id, out);
 }
 
 // ------------------------------------------------------------------ kernels as calls

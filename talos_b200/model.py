@@ -105,6 +105,14 @@ def _ptr(a) -> int:
     return a.ctypes.data if isinstance(a, np.ndarray) else C.addressof(a)
 
 
+def nccl_unique_id() -> bytes:
+    """talos_nccl_unique_id: the 128-byte id rank 0 makes and shares with the other
+    tensor-parallel ranks (out of band) before they create their contexts."""
+    buf = C.create_string_buffer(128)
+    _lib.check(_lib.load().talos_nccl_unique_id(buf))
+    return buf.raw
+
+
 class Context:
     """One ``talos_ctx``: a model's weights, KV cache and captured graphs on one GPU."""
 
