@@ -108,6 +108,7 @@ struct TokenPhase {
     int xsrc, xdst, xslot;
     int rx_slot;    // EPI_PEER: receive slot written
     int xrank;      // arrivals at this phase's barrier come from every rank
+    int att_merge;  // the input is the attention output, merged from TokenArgs::att_part
     MatvecArgs mv;  // PH_MATVEC
     AttnArgs at;    // PH_ATTN
 };
@@ -127,9 +128,8 @@ struct TokenArgs {
     float* hidden;              // PH_HIDDEN output [E]
     const float* out_norm;
     float eps;
-    float* att_part;            // [n_head][nsplit][hd + 2] split-softmax partials
-    unsigned* att_cnt;          // [n_kv] arrivals per kv head (reset by the last one)
-    int nsplit;                 // attention splits per kv head
+    float* att_part;            // [n_head][nsplit][hd + 4] split-softmax partials {m, l, -, -, o}
+    int nsplit;                 // most attention splits per kv head (<= 8)
     int nst;                    // ring stages
     int union_bytes;            // staged input / attention scratch bytes
     unsigned long long* stamps; // optional [nph][grid][4] global-timer stamps (ns): phase
@@ -146,8 +146,8 @@ struct TokenArgs {
 
 // Staged-input elements the k_token scratch region must hold for input length K.
 int token_stage_elems(int type, int K);
-// Scratch bytes attention needs for `group` heads of `hd` dims and `nsplit` splits.
-int token_attn_bytes(int group, int hd, int nsplit);
+// Scratch bytes attention needs for `group` heads of `hd` dims.
+int token_attn_bytes(int group, int hd);
 size_t token_smem_bytes(int nst, int union_bytes);
 // Ring stages that fit next to `union_bytes` of scratch (0 if none fit).
 int token_max_stages(int union_bytes);

@@ -943,7 +943,15 @@ static_assert(2 * Fmt<GT_Q8_0>::GCB <= TK_STAGE && 2 * Fmt<GT_Q6_K>::GCB <= TK_S
                   2 * Fmt<GT_F32>::GCB <= TK_STAGE,
               "ring stage too small");
 constexpr int TK_NORM_REGS = 16;               // normed-input registers per thread: K <= 16 * 512
-constexpr int TK_MAXG = 8;                     // query heads per kv head in attention
+constexpr int TK_MAX_SPLIT = 8;                // position splits per kv head in attention
+constexpr int TK_SPLIT_POS = 128;              // positions per split the split count aims for
+
+// Splits of a kv head's positions this step: about TK_SPLIT_POS positions each,
+// at most `nsplit` (short sequences need no cross-CTA merge at all).
+__device__ __forceinline__ int tk_splits(int nsplit, uint32_t pos) {
+    const int want = ((int)pos + TK_SPLIT_POS) / TK_SPLIT_POS;  // ceil((pos + 1) / TK_SPLIT_POS)
+    return want < nsplit ? want : nsplit;
+}
 constexpr int TK_BAR_BYTES = 64 * 8;           // room for the ring's mbarriers (nst <= 30)
 constexpr int TK_TAIL_BYTES = (2 * MV_CWARPS * 16 + 16 + 32) * 4;
 constexpr uint64_t TK_WAIT_NS = 2000000000ull;
@@ -1018,7 +1026,6 @@ struct TkShared {
     int err;      // any role gave up on a wait (set at any time)
     int stop;     // consumer thread 0's snapshot of err at a phase start, read after the sync
     int started;  // last phase the consumers entered (epilogue warp follows it)
-    int last;     // attention: this CTA merges the splits of its kv head
 };
 
 // Profiling stamps (TokenArgs::stamps): [phase][cta][4] = phase entered,
@@ -1080,9 +1087,10 @@ __device__ __forceinline__ void tk_sums(float* xs16, int e0, float4 v, int lane)
 // (src/math/ops.rs:5-12, (x * s) * w), the token's embedding row for the first
 // phase (src/model/weights.rs:57-62). All global loads of a round are issued
 // before any is used (one L2 round trip per round, not one per element).
-constexpr int TK_ROUND = 8;  // 128-element runs per warp and round
+constexpr int TK_ROUND = 4;  // 128-element runs per warp and round
 template <int TYPE>
-__device__ __forceinline__ void tk_stage(const TokenArgs& a, const TokenPhase& P, uint32_t tok, float* U, float* red) {
+__device__ __forceinline__ void tk_stage(const TokenArgs& a, const TokenPhase& P, uint32_t tok, uint32_t pos, float* U,
+                                         float* red) {
     const MatvecArgs& m = P.mv;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = m.K, KP = ((K + Fmt<TYPE>::CK - 1) / Fmt<TYPE>::CK) * Fmt<TYPE>::CK, nrun = KP / 128;
@@ -1134,7 +1142,54 @@ __device__ __forceinline__ void tk_stage(const TokenArgs& a, const TokenPhase& P
         for (int i = 0; i < 4; ++i) t[i] = e0 + i < K ? __ldg(m.norm_w + e0 + i) : 0.f;
         return make_float4(t[0], t[1], t[2], t[3]);
     };
-    if (m.norm_w) {
+    if (P.att_merge) {
+        // the attention output, merged from the softmax partials of each head's
+        // splits (src/math/ops.rs:15-25 normalisation, applied to the merged sums):
+        // per head the weights exp(m_q - M) / L, then o = sum_q w_q o_q
+        const int hd = m.hd, nh = K / hd, ns = tk_splits(a.nsplit, pos), hs = hd + 4;
+        float* wsm = xs16 + KP / 16;  // [nh][ns]
+        for (int h = tid; h < nh; h += MV_CONSUMERS) {
+            const float* base = a.att_part + (size_t)h * a.nsplit * hs;
+            float mv[TK_MAX_SPLIT], lv[TK_MAX_SPLIT];
+            float M = -INFINITY;
+#pragma unroll
+            for (int q = 0; q < TK_MAX_SPLIT; ++q) {
+                mv[q] = q < ns ? __ldcg(base + q * hs) : -INFINITY;
+                lv[q] = q < ns ? __ldcg(base + q * hs + 1) : 0.f;
+            }
+#pragma unroll
+            for (int q = 0; q < TK_MAX_SPLIT; ++q) M = fmaxf(M, mv[q]);
+            float L = 0.f;
+#pragma unroll
+            for (int q = 0; q < TK_MAX_SPLIT; ++q) {
+                mv[q] = mv[q] != -INFINITY ? expf(mv[q] - M) : 0.f;
+                L = fmaf(lv[q], mv[q], L);
+            }
+#pragma unroll
+            for (int q = 0; q < TK_MAX_SPLIT; ++q)
+                if (q < ns) wsm[h * ns + q] = mv[q] / L;
+        }
+        consumer_sync();
+#pragma unroll 2
+        for (int r = warp; r < nrun; r += MV_CWARPS) {
+            const int e0 = 128 * r + 4 * lane;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (e0 < K) {
+                const int h = e0 / hd;
+                const float* ob = a.att_part + (size_t)h * a.nsplit * hs + 4 + e0 % hd;
+#pragma unroll
+                for (int q = 0; q < TK_MAX_SPLIT; ++q) {
+                    if (q < ns) {
+                        const float4 o = __ldcg((const float4*)(ob + q * hs));
+                        const float w = wsm[h * ns + q];
+                        v = make_float4(fmaf(o.x, w, v.x), fmaf(o.y, w, v.y), fmaf(o.z, w, v.z), fmaf(o.w, w, v.w));
+                    }
+                }
+            }
+            tk_put4<TYPE>(U, e0, v);
+            tk_sums<TYPE>(xs16, e0, v, lane);
+        }
+    } else if (m.norm_w) {
         // the whole input in registers (K <= 16 * 128 * 4 = 8192), one reduction
         float4 xv[TK_NORM_REGS / 4], wv[TK_NORM_REGS / 4];
         float ss = 0.f;
@@ -1193,12 +1248,13 @@ __device__ __forceinline__ void tk_stage(const TokenArgs& a, const TokenPhase& P
 
 // Consumers of one matvec phase: stage the input, then every tile of this CTA.
 template <int TYPE>
-__device__ __noinline__ bool tk_matvec(const TokenArgs& a, const TokenPhase& P, int p, uint32_t tok, uint8_t* ring,
+__device__ __noinline__ bool tk_matvec(const TokenArgs& a, const TokenPhase& P, int p, uint32_t tok, uint32_t pos,
+                                       uint8_t* ring,
                                        uint64_t* full, uint64_t* empty, uint64_t* tdone, uint64_t* tfree, float* U,
                                        float* part, float* red, uint32_t& slot, uint32_t& par, int& ntile) {
     const MatvecArgs& m = P.mv;
     if ((int)blockIdx.x >= m.ntiles) return true;  // no tiles here: read nothing
-    tk_stage<TYPE>(a, P, tok, U, red);
+    tk_stage<TYPE>(a, P, tok, pos, U, red);
     if (threadIdx.x == 0) tk_stamp(a, p, 1);
     constexpr int GCB = Fmt<TYPE>::GCB, CK = Fmt<TYPE>::CK;
     const int nchunk = (m.K + CK - 1) / CK, KP = nchunk * CK;
@@ -1247,20 +1303,26 @@ __device__ __noinline__ bool tk_matvec(const TokenArgs& a, const TokenPhase& P, 
 }
 
 // Attention for one (kv head, position split) item per CTA (src/model/llama.rs:
-// 135-155): scores q.k * scale, softmax, sum of p V, as split softmax partials
-// (max m, sum l, unnormalised o) merged across warps, then across the splits of
-// the kv head by the CTA that finishes last.
-__device__ __noinline__ void tk_attention(const TokenArgs& a, const AttnArgs& A, int p, uint32_t pos, float* U,
-                                          TkShared* sh) {
+// 135-155): scores q.k * scale, softmax, sum of p V. Each warp keeps online
+// softmax state (max m, sum l, unnormalised o) over its positions, with
+// TK_ATT_UNROLL positions' K/V loads in flight; the warps merge in shared
+// memory and the split writes its partial to att_part. The o-proj phase merges
+// the splits while it stages its input (cheaper, measured, than an arrival
+// counter and a merge by the last split's CTA).
+// Instantiated per query-head group size G, so the unrolled loops hold exactly
+// the heads a model has (the kernel's code must stay small enough for the
+// instruction cache: every phase of every layer runs through it).
+constexpr int TK_ATT_UNROLL = 2;
+template <int G>
+__device__ __noinline__ void tk_attention(const TokenArgs& a, const AttnArgs& A, int p, uint32_t pos, float* U) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int nsplit = a.nsplit;
-    if ((int)blockIdx.x >= A.n_kv * nsplit) return;
-    const int kh = blockIdx.x / nsplit, s = blockIdx.x % nsplit;
-    // partial records: {m, l, o[hd]} in global memory, {m, l, pad, pad, o[hd]} in
-    // shared memory (16-byte aligned o for the float4 stores)
-    const int group = A.n_head / A.n_kv, hd = A.hd, hw = hd + 2, hs = hd + 4;
+    const int nsplit = a.nsplit, ns = tk_splits(nsplit, pos);
+    if ((int)blockIdx.x >= A.n_kv * ns) return;
+    const int kh = blockIdx.x / ns, s = blockIdx.x % ns;
+    // partial records {m, l, pad, pad, o[hd]} (16-byte aligned o), in shared and global memory
+    const int group = A.n_head / A.n_kv, hd = A.hd, hs = hd + 4;
     const int seq = (int)pos + 1;
-    const int per = (seq + nsplit - 1) / nsplit;
+    const int per = (seq + ns - 1) / ns;
     const int p0 = s * per, p1 = min(seq, p0 + per);
     float* qs = U;               // [group][hd]
     float* ws = U + group * hd;  // [16 warps][group][hd + 4]
@@ -1270,43 +1332,53 @@ __device__ __noinline__ void tk_attention(const TokenArgs& a, const AttnArgs& A,
     if (tid == 0) tk_stamp(a, p, 1);
 
     const bool act = 4 * lane < hd;
-    float m[TK_MAXG], l[TK_MAXG], o[TK_MAXG][4];
+    float m[G], l[G], o[G][4];
 #pragma unroll
-    for (int g = 0; g < TK_MAXG; ++g) {
+    for (int g = 0; g < G; ++g) {
         m[g] = -INFINITY;
         l[g] = 0.f;
         o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
     }
     const size_t hoff = (size_t)kh * hd + 4 * lane;
-    for (int t = p0 + warp; t < p1; t += MV_CWARPS) {
-        float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-        if (act) {
-            kv = __ldcg((const float4*)(A.kc + (size_t)t * A.kv_dim + hoff));
-            vv = __ldcg((const float4*)(A.vc + (size_t)t * A.kv_dim + hoff));
+    for (int t0 = p0 + warp; t0 < p1; t0 += MV_CWARPS * TK_ATT_UNROLL) {
+        float4 kv[TK_ATT_UNROLL], vv[TK_ATT_UNROLL];
+#pragma unroll
+        for (int u = 0; u < TK_ATT_UNROLL; ++u) {
+            const int t = t0 + u * MV_CWARPS;
+            kv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            vv[u] = kv[u];
+            if (act && t < p1) {
+                kv[u] = __ldcg((const float4*)(A.kc + (size_t)t * A.kv_dim + hoff));
+                vv[u] = __ldcg((const float4*)(A.vc + (size_t)t * A.kv_dim + hoff));
+            }
         }
 #pragma unroll
-        for (int g = 0; g < TK_MAXG; ++g) {
-            if (g < group) {
-                float d = 0.f;
-                if (act) {
-                    const float4 q4 = *(const float4*)(qs + g * hd + 4 * lane);
-                    d = fmaf(q4.x, kv.x, fmaf(q4.y, kv.y, fmaf(q4.z, kv.z, q4.w * kv.w)));
+        for (int u = 0; u < TK_ATT_UNROLL; ++u) {
+            if (t0 + u * MV_CWARPS >= p1) break;  // warp-uniform
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                {
+                    float d = 0.f;
+                    if (act) {
+                        const float4 q4 = *(const float4*)(qs + g * hd + 4 * lane);
+                        d = fmaf(q4.x, kv[u].x, fmaf(q4.y, kv[u].y, fmaf(q4.z, kv[u].z, q4.w * kv[u].w)));
+                    }
+                    const float sc = warp_sum(d) * A.scale;
+                    const float mn = fmaxf(m[g], sc);
+                    const float cr = expf(m[g] - mn), pe = expf(sc - mn);
+                    l[g] = fmaf(l[g], cr, pe);
+                    o[g][0] = fmaf(o[g][0], cr, pe * vv[u].x);
+                    o[g][1] = fmaf(o[g][1], cr, pe * vv[u].y);
+                    o[g][2] = fmaf(o[g][2], cr, pe * vv[u].z);
+                    o[g][3] = fmaf(o[g][3], cr, pe * vv[u].w);
+                    m[g] = mn;
                 }
-                const float sc = warp_sum(d) * A.scale;
-                const float mn = fmaxf(m[g], sc);
-                const float cr = expf(m[g] - mn), pe = expf(sc - mn);
-                l[g] = fmaf(l[g], cr, pe);
-                o[g][0] = fmaf(o[g][0], cr, pe * vv.x);
-                o[g][1] = fmaf(o[g][1], cr, pe * vv.y);
-                o[g][2] = fmaf(o[g][2], cr, pe * vv.z);
-                o[g][3] = fmaf(o[g][3], cr, pe * vv.w);
-                m[g] = mn;
             }
         }
     }
 #pragma unroll
-    for (int g = 0; g < TK_MAXG; ++g) {
-        if (g < group) {
+    for (int g = 0; g < G; ++g) {
+        {
             float* w = ws + (warp * group + g) * hs;
             if (lane == 0) {
                 w[0] = m[g];
@@ -1330,59 +1402,15 @@ __device__ __noinline__ void tk_attention(const TokenArgs& a, const AttnArgs& A,
                 O = fmaf(ww[4 + d], e, O);
             }
         }
-        float* dst = a.att_part + ((size_t)(kh * group + g) * nsplit + s) * hw;
+
+        float* dst = a.att_part + ((size_t)(kh * group + g) * nsplit + s) * hs;
         if (d == 0) {
             dst[0] = M;
             dst[1] = L;
         }
-        dst[2 + d] = O;
+        dst[4 + d] = O;
     }
-    __threadfence();
-    consumer_sync();
-    if (tid == 0) {
-        tk_stamp(a, p, 2);
-        const unsigned old = atomicAdd(&a.att_cnt[kh], 1u);
-        const int last = old == (unsigned)(nsplit - 1);
-        if (last) a.att_cnt[kh] = 0u;  // every split of this kv head has arrived
-        sh->last = last;
-    }
-    consumer_sync();
-    if (!sh->last) return;
-    __threadfence();
-    // (m, l) of every split of the group's heads into shared memory, in parallel
-    float* ml = ws;                       // [group][nsplit][2]
-    float* wq = ml + 2 * group * nsplit;  // [group][nsplit] exp(m_q - M), 0 for empty splits
-    float* lsum = wq + group * nsplit;    // [group]
-    for (int i = tid; i < group * nsplit; i += MV_CONSUMERS) {
-        const float* src = a.att_part + ((size_t)kh * group * nsplit + i) * hw;
-        ml[2 * i] = __ldcg(src);
-        ml[2 * i + 1] = __ldcg(src + 1);
-    }
-    consumer_sync();
-    if (tid < group) {
-        float M = -INFINITY;
-        for (int q = 0; q < nsplit; ++q) M = fmaxf(M, ml[2 * (tid * nsplit + q)]);
-        float L = 0.f;
-        for (int q = 0; q < nsplit; ++q) {
-            const float mq = ml[2 * (tid * nsplit + q)];
-            const float e = mq != -INFINITY ? expf(mq - M) : 0.f;
-            wq[tid * nsplit + q] = e;
-            L = fmaf(ml[2 * (tid * nsplit + q) + 1], e, L);
-        }
-        lsum[tid] = L;
-    }
-    consumer_sync();
-    // o = sum_q e_q o_q / L: one thread per (head, dim), the splits' loads in flight together
-    for (int idx = tid; idx < group * hd; idx += MV_CONSUMERS) {
-        const int g = idx / hd, d = idx % hd;
-        const float* base = a.att_part + (size_t)(kh * group + g) * nsplit * hw + 2 + d;
-        const float* w = wq + g * nsplit;
-        float O = 0.f;
-#pragma unroll 8
-        for (int q = 0; q < nsplit; ++q) O = fmaf(__ldcg(base + q * hw), w[q], O);
-        A.out[(size_t)(kh * group + g) * hd + d] = O / lsum[g];
-    }
-    __threadfence();
+    if (tid == 0) tk_stamp(a, p, 2);
 }
 
 // Final norm to the hidden state (src/model/llama.rs:181), CTA 0 only.
@@ -1459,7 +1487,6 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
         sh.err = 0;
         sh.stop = 0;
         sh.started = 0;
-        sh.last = 0;
         if (blockIdx.x == 0) a.step->argmax_key = 0ull;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -1607,16 +1634,16 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
             bool ok = true;
             switch (P.type) {
                 case GT_Q4_0:
-                    ok = tk_matvec<GT_Q4_0>(a, P, p, tok, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
+                    ok = tk_matvec<GT_Q4_0>(a, P, p, tok, pos, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
                     break;
                 case GT_Q8_0:
-                    ok = tk_matvec<GT_Q8_0>(a, P, p, tok, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
+                    ok = tk_matvec<GT_Q8_0>(a, P, p, tok, pos, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
                     break;
                 case GT_Q6_K:
-                    ok = tk_matvec<GT_Q6_K>(a, P, p, tok, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
+                    ok = tk_matvec<GT_Q6_K>(a, P, p, tok, pos, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
                     break;
                 default:
-                    ok = tk_matvec<GT_F32>(a, P, p, tok, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
+                    ok = tk_matvec<GT_F32>(a, P, p, tok, pos, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
                     break;
             }
             if (!ok) {
@@ -1626,7 +1653,14 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
                 continue;
             }
         } else if (P.kind == PH_ATTN) {
-            tk_attention(a, P.at, p, pos, U, &sh);
+            switch (P.at.n_head / P.at.n_kv) {
+                case 1: tk_attention<1>(a, P.at, p, pos, U); break;
+                case 2: tk_attention<2>(a, P.at, p, pos, U); break;
+                case 3: tk_attention<3>(a, P.at, p, pos, U); break;
+                case 4: tk_attention<4>(a, P.at, p, pos, U); break;
+                case 8: tk_attention<8>(a, P.at, p, pos, U); break;
+                default: break;  // excluded on the host (fused_check)
+            }
             consumer_sync();
             if (tid == 0 && p + 1 < a.nph) {
                 __threadfence();
@@ -1657,10 +1691,7 @@ int token_stage_elems(int type, int K) {
     return ceil_div_h(K, ck) * ck;
 }
 
-int token_attn_bytes(int group, int hd, int nsplit) {
-    const int warps = MV_CWARPS * group * (hd + 4), merge = 3 * group * nsplit + group;
-    return (group * hd + (warps > merge ? warps : merge)) * 4;
-}
+int token_attn_bytes(int group, int hd) { return (group * hd + MV_CWARPS * group * (hd + 4)) * 4; }
 
 size_t token_smem_bytes(int nst, int union_bytes) {
     return (size_t)nst * TK_STAGE + TK_BAR_BYTES + (size_t)union_bytes + TK_TAIL_BYTES;

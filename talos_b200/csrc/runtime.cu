@@ -292,7 +292,6 @@ struct talos_ctx {
     unsigned long long* bars = nullptr;
     unsigned long long* epoch = nullptr;
     unsigned long long* stamps = nullptr;
-    unsigned* att_cnt = nullptr;
     float* att_part = nullptr;
     int nsplit = 0, nph_max = 0;
     TokenPhase* d_phases[GM_COUNT] = {nullptr, nullptr, nullptr};
@@ -437,8 +436,9 @@ static talos_status alloc_arena(talos_ctx* c) {
 // k_token, zeroed.
 static talos_status alloc_sync(talos_ctx* c) {
     const int sms = (c->device < 64 && g_sms[c->device]) ? g_sms[c->device] : 148;
-    c->nsplit = sms / c->nkv_l;
-    if (c->nsplit < 1) c->nsplit = 1;
+    // attention: (kv head, position split) items; 8 splits keep ~64 CTAs busy on
+    // the 7B shape and the o-proj staging's merge short
+    c->nsplit = std::max(1, std::min(8, sms / c->nkv_l));
     c->nph_max = (int)c->cfg.n_layer * 5 + 1;
     size_t off = 0;
     auto take = [&](size_t bytes) {
@@ -448,15 +448,13 @@ static talos_status alloc_sync(talos_ctx* c) {
     };
     const size_t o_bars = take((size_t)c->nph_max * 8), o_epoch = take(8),
                  o_stamps = take((size_t)c->nph_max * sms * 4 * 8),
-                 o_cnt = take((size_t)c->nkv_l * 4),
-                 o_part = take((size_t)c->nh_l * c->nsplit * (c->hd + 2) * 4);
+                 o_part = take((size_t)c->nh_l * c->nsplit * (c->hd + 4) * 4);
     CK(cudaMalloc(&c->sync_mem, off));
     c->sync_bytes = off;
     uint8_t* b = (uint8_t*)c->sync_mem;
     c->bars = (unsigned long long*)(b + o_bars);
     c->epoch = (unsigned long long*)(b + o_epoch);
     c->stamps = (unsigned long long*)(b + o_stamps);
-    c->att_cnt = (unsigned*)(b + o_cnt);
     c->att_part = (float*)(b + o_part);
     CK(cudaMemsetAsync(c->sync_mem, 0, off, c->stream));
     CK(cudaStreamSynchronize(c->stream));
@@ -991,6 +989,8 @@ static void build_phases(talos_ctx* c, GraphMode mode, std::vector<TokenPhase>& 
         p.kind = PH_MATVEC;
         p.type = L.o->type;
         p.prof_kind = TALOS_K_OPROJ;
+        p.att_merge = 1;
+        p.mv.hd = c->hd;
         p.mv.K = c->q_rows;
         p.mv.x = c->att;
         p.mv.epi = tp ? EPI_PEER : EPI_ADD;
@@ -1062,6 +1062,11 @@ static void fused_check(talos_ctx* c) {
         c->fused_why = buf;
         return;
     }
+    if (c->group != 1 && c->group != 2 && c->group != 3 && c->group != 4 && c->group != 8) {
+        snprintf(buf, sizeof buf, "%d query heads per kv head (1, 2, 3, 4 or 8)", c->group);
+        c->fused_why = buf;
+        return;
+    }
     if (c->cfg.n_embd > 8192) {
         snprintf(buf, sizeof buf, "n_embd %u above 8192", c->cfg.n_embd);
         c->fused_why = buf;
@@ -1074,7 +1079,7 @@ static void fused_check(talos_ctx* c) {
     }
     std::vector<TokenPhase> ph;
     build_phases(c, GM_LOGITS, ph);
-    int ub = token_attn_bytes(c->group, c->hd, c->nsplit);
+    int ub = token_attn_bytes(c->group, c->hd);
     for (uint32_t l = 0; l < c->cfg.n_layer; ++l) {
         const LayerW& L = c->layers[l];
         if (L.k->type != L.q->type || L.v->type != L.q->type) {
@@ -1086,7 +1091,8 @@ static void fused_check(talos_ctx* c) {
     for (const auto& p : ph)
         if (p.kind == PH_MATVEC) {
             const int kp = token_stage_elems(p.type, p.mv.K);
-            const int b = kp * 4 + kp / 16 * 4;
+            // staged input + block sums (+ the attention merge weights of o-proj)
+            const int b = kp * 4 + kp / 16 * 4 + (p.att_merge ? c->nh_l * c->nsplit * 4 : 0);
             if (b > ub) ub = b;
         }
     ub = (ub + 15) / 16 * 16;
@@ -1136,7 +1142,6 @@ static TokenArgs token_args(talos_ctx* c, GraphMode mode, unsigned long long* st
     a.out_norm = (const float*)c->w["output_norm.weight"].mem;
     a.eps = c->cfg.rms_eps;
     a.att_part = c->att_part;
-    a.att_cnt = c->att_cnt;
     a.nsplit = c->nsplit;
     a.nst = c->tk_nst;
     a.union_bytes = c->tk_union;
