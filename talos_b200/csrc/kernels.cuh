@@ -131,6 +131,7 @@ struct TokenArgs {
     float* att_part;            // [n_head][nsplit][hd + 4] split-softmax partials {m, l, -, -, o}
     int nsplit;                 // most attention splits per kv head (<= 8)
     int nst;                    // ring stages
+    int prefetch;               // chunks of a phase streamed before its input is staged
     int union_bytes;            // staged input / attention scratch bytes
     unsigned long long* stamps; // optional [nph][grid][4] global-timer stamps (ns): phase
                                 // entered, inputs staged, compute done, barrier arrival

@@ -1013,6 +1013,17 @@ __device__ __forceinline__ bool smem_wait_geq(const volatile int* p, int v) {
         if (globaltimer_ns() - t0 > TK_WAIT_NS) return false;
     }
 }
+// Bounded wait of one thread until the shared counter reaches v, sleeping between
+// polls (the waiter shares its sub-partition's issue slots with consumer warps).
+__device__ __forceinline__ bool smem_wait_geq_sleep(const volatile int* p, int v) {
+    if (*p >= v) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        __nanosleep(100);
+        if (*p >= v) return true;
+        if (globaltimer_ns() - t0 > TK_WAIT_NS) return false;
+    }
+}
 __device__ __forceinline__ void bulk_g2s_evict_first(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
                                                      uint64_t policy) {
     asm volatile(
@@ -1026,6 +1037,7 @@ struct TkShared {
     int err;      // any role gave up on a wait (set at any time)
     int stop;     // consumer thread 0's snapshot of err at a phase start, read after the sync
     int started;  // last phase the consumers entered (epilogue warp follows it)
+    int staged;   // last phase whose input the consumers have staged (producer follows it)
 };
 
 // Profiling stamps (TokenArgs::stamps): [phase][cta][4] = phase entered,
@@ -1249,13 +1261,16 @@ __device__ __forceinline__ void tk_stage(const TokenArgs& a, const TokenPhase& P
 // Consumers of one matvec phase: stage the input, then every tile of this CTA.
 template <int TYPE>
 __device__ __noinline__ bool tk_matvec(const TokenArgs& a, const TokenPhase& P, int p, uint32_t tok, uint32_t pos,
-                                       uint8_t* ring,
+                                       TkShared* sh, uint8_t* ring,
                                        uint64_t* full, uint64_t* empty, uint64_t* tdone, uint64_t* tfree, float* U,
                                        float* part, float* red, uint32_t& slot, uint32_t& par, int& ntile) {
     const MatvecArgs& m = P.mv;
     if ((int)blockIdx.x >= m.ntiles) return true;  // no tiles here: read nothing
     tk_stage<TYPE>(a, P, tok, pos, U, red);
-    if (threadIdx.x == 0) tk_stamp(a, p, 1);
+    if (threadIdx.x == 0) {
+        *(volatile int*)&sh->staged = p;  // the producer may stream the rest of this phase
+        tk_stamp(a, p, 1);
+    }
     constexpr int GCB = Fmt<TYPE>::GCB, CK = Fmt<TYPE>::CK;
     const int nchunk = (m.K + CK - 1) / CK, KP = nchunk * CK;
     const float* stage_x = U;
@@ -1487,6 +1502,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
         sh.err = 0;
         sh.stop = 0;
         sh.started = 0;
+        sh.staged = -1;
         if (blockIdx.x == 0) a.step->argmax_key = 0ull;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -1555,10 +1571,11 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
                 __syncwarp();
             }
             if (p + 1 < a.nph || a.tp > 1) {
-                if (P.xrank)
-                    __threadfence_system();
-                else
-                    __threadfence();
+                // The release add orders every lane's stores before the arrival (the
+                // warp barrier makes them precede it; release is cumulative), so no
+                // separate fence: a fence here also waits out this SM's in-flight
+                // weight copies (about 1 us, measured).
+                if (P.xrank) __threadfence_system();
                 __syncwarp();
                 if (lane == 0) {
                     tk_arrive(a, p, P.xrank != 0);
@@ -1581,10 +1598,18 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
                 const MatvecArgs& m = P.mv;
                 const int gcb = gcb_of(P.type), ck = ck_of(P.type);
                 const int nchunk = (m.K + ck - 1) / ck;
+                int pc = 0;  // chunks of this phase issued so far
                 for (int t = blockIdx.x; t < m.ntiles && ok; t += gridDim.x) {
                     int si, lt;
                     find_seg(m, t, si, lt);
-                    for (int c = 0; c < nchunk; ++c) {
+                    for (int c = 0; c < nchunk; ++c, ++pc) {
+                        // Past the first a.prefetch chunks, wait until the consumers have
+                        // staged this phase's input: its loads then meet no queue of
+                        // weight copies in this SM's memory path at the phase start.
+                        if (pc == a.prefetch && !smem_wait_geq_sleep(&sh.staged, p)) {
+                            ok = false;
+                            break;
+                        }
                         if (!mbar_wait(&empty[slot], par ^ 1u) || *(volatile int*)&sh.err) {
                             ok = false;
                             break;
@@ -1619,8 +1644,8 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
         if (p > 0) {
             if (tid == 0) {
                 const bool xr = a.ph[p - 1].xrank != 0;
+                // the acquire load orders the phase's reads; consumer_sync passes it on
                 if (!grid_wait_one(&a.bars[p - 1], xr ? target * (unsigned)a.tp : target, xr)) tk_fail(a, &sh, 4u);
-                __threadfence();
                 *(volatile int*)&sh.started = p;
                 sh.stop = *(volatile int*)&sh.err;
                 tk_stamp(a, p, 0);
@@ -1634,16 +1659,16 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
             bool ok = true;
             switch (P.type) {
                 case GT_Q4_0:
-                    ok = tk_matvec<GT_Q4_0>(a, P, p, tok, pos, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
+                    ok = tk_matvec<GT_Q4_0>(a, P, p, tok, pos, &sh, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
                     break;
                 case GT_Q8_0:
-                    ok = tk_matvec<GT_Q8_0>(a, P, p, tok, pos, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
+                    ok = tk_matvec<GT_Q8_0>(a, P, p, tok, pos, &sh, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
                     break;
                 case GT_Q6_K:
-                    ok = tk_matvec<GT_Q6_K>(a, P, p, tok, pos, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
+                    ok = tk_matvec<GT_Q6_K>(a, P, p, tok, pos, &sh, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
                     break;
                 default:
-                    ok = tk_matvec<GT_F32>(a, P, p, tok, pos, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
+                    ok = tk_matvec<GT_F32>(a, P, p, tok, pos, &sh, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
                     break;
             }
             if (!ok) {
@@ -1661,9 +1686,8 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
                 case 8: tk_attention<8>(a, P.at, p, pos, U); break;
                 default: break;  // excluded on the host (fused_check)
             }
-            consumer_sync();
+            consumer_sync();  // every warp's partial stores precede thread 0's release
             if (tid == 0 && p + 1 < a.nph) {
-                __threadfence();
                 red_release_add_u64(&a.bars[p], 1ull);
                 tk_stamp(a, p, 3);
             }

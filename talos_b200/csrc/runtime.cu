@@ -1125,6 +1125,10 @@ static talos_status use_fused(talos_ctx* c, bool* out) {
     return TALOS_OK;
 }
 
+// Chunks of a phase's weights the per-token kernel streams before the phase's
+// input vector is staged (more would delay the staging loads behind the copies).
+static const int TK_PREFETCH = 2;
+
 static TokenArgs token_args(talos_ctx* c, GraphMode mode, unsigned long long* stamps) {
     TokenArgs a{};
     const DevTensor& embd = c->w["token_embd.weight"];
@@ -1144,6 +1148,7 @@ static TokenArgs token_args(talos_ctx* c, GraphMode mode, unsigned long long* st
     a.att_part = c->att_part;
     a.nsplit = c->nsplit;
     a.nst = c->tk_nst;
+    a.prefetch = TK_PREFETCH;
     a.union_bytes = c->tk_union;
     a.stamps = stamps;
     a.tp = c->tp;
