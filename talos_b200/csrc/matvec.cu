@@ -944,7 +944,12 @@ static_assert(2 * Fmt<GT_Q8_0>::GCB <= TK_STAGE && 2 * Fmt<GT_Q6_K>::GCB <= TK_S
               "ring stage too small");
 constexpr int TK_NORM_REGS = 16;               // normed-input registers per thread: K <= 16 * 512
 constexpr int TK_MAX_SPLIT = 8;                // position splits per kv head in attention
-constexpr int TK_SPLIT_POS = 128;              // positions per split the split count aims for
+#ifndef TK_SPLIT_POS
+#define TK_SPLIT_POS 64                        // positions per split the split count aims for
+#endif
+#ifndef TK_PAIR_CHUNKS
+#define TK_PAIR_CHUNKS 1                       // consume two ring stages per step
+#endif
 
 // Splits of a kv head's positions this step: about TK_SPLIT_POS positions each,
 // at most `nsplit` (short sequences need no cross-CTA merge at all).
@@ -1277,26 +1282,56 @@ __device__ __noinline__ bool tk_matvec(const TokenArgs& a, const TokenPhase& P, 
     const float* xs16 = U + KP;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t nst = (uint32_t)a.nst;
+    auto consume = [&](const uint8_t* sA, int c, Acc& acc) {
+        const uint8_t* sB = sA + GCB;
+        if (TYPE == GT_Q4_0)
+            consume_q4_0(sA, sB, (const uint4*)stage_x, xs16, c, acc);
+        else if (TYPE == GT_Q8_0)
+            consume_q8_0(sA, sB, (const uint4*)stage_x, xs16, c, acc);
+        else if (TYPE == GT_Q6_K)
+            consume_q6_k(sA, sB, (const uint4*)stage_x, xs16, c, acc);
+        else
+            consume_f32(sA, sB, stage_x, c, acc);
+    };
+    auto next = [&](uint32_t& s_, uint32_t& p_) {
+        if (++s_ == nst) {
+            s_ = 0;
+            p_ ^= 1u;
+        }
+    };
     for (int t = blockIdx.x; t < m.ntiles; t += gridDim.x) {
         Acc acc = {0.f, 0.f, 0.f, 0.f};
-        for (int c = 0; c < nchunk; ++c) {
+        int c = 0;
+#if TK_PAIR_CHUNKS
+        // two stages per step, two independent accumulators: twice the MMA and FMA
+        // chains in flight per warp (the consumers are latency-bound, not issue-bound)
+        for (; c + 1 < nchunk; c += 2) {
+            uint32_t s2 = slot, p2 = par;
+            next(s2, p2);
+            if (!mbar_wait(&full[slot], par) || !mbar_wait(&full[s2], p2)) return false;
+            Acc acc2 = {0.f, 0.f, 0.f, 0.f};
+            consume(ring + slot * TK_STAGE, c, acc);
+            consume(ring + s2 * TK_STAGE, c + 1, acc2);
+            acc.pA += acc2.pA;
+            acc.qA += acc2.qA;
+            acc.pB += acc2.pB;
+            acc.qB += acc2.qB;
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&empty[slot]);
+                mbar_arrive(&empty[s2]);
+            }
+            slot = s2;
+            par = p2;
+            next(slot, par);
+        }
+#endif
+        for (; c < nchunk; ++c) {
             if (!mbar_wait(&full[slot], par)) return false;
-            const uint8_t* sA = ring + slot * TK_STAGE;
-            const uint8_t* sB = sA + GCB;
-            if (TYPE == GT_Q4_0)
-                consume_q4_0(sA, sB, (const uint4*)stage_x, xs16, c, acc);
-            else if (TYPE == GT_Q8_0)
-                consume_q8_0(sA, sB, (const uint4*)stage_x, xs16, c, acc);
-            else if (TYPE == GT_Q6_K)
-                consume_q6_k(sA, sB, (const uint4*)stage_x, xs16, c, acc);
-            else
-                consume_f32(sA, sB, stage_x, c, acc);
+            consume(ring + slot * TK_STAGE, c, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            if (++slot == nst) {
-                slot = 0;
-                par ^= 1u;
-            }
+            next(slot, par);
         }
         // hand the tile's partials to the epilogue warp (double-buffered)
         const int b = ntile & 1;
