@@ -1672,10 +1672,20 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
     }
 
     // ---------------- consumers
+    // The phase descriptor is copied to shared memory while thread 0 waits at the
+    // barrier (double-buffered: a slow warp may still read the previous one), so
+    // the phase's first instructions do not wait on global loads of its fields.
+    __shared__ __align__(16) TokenPhase sph[2];
     uint32_t slot = 0, par = 0;
     int ntile = 0;
     for (int p = 0; p < a.nph; ++p) {
-        const TokenPhase& P = a.ph[p];
+        {
+            const int* src = (const int*)(a.ph + p);
+            int* dst = (int*)&sph[p & 1];
+            for (int i = tid; i < (int)(sizeof(TokenPhase) / 4); i += MV_CONSUMERS) dst[i] = __ldg(src + i);
+        }
+        const TokenPhase& P = sph[p & 1];
+        if (p == 0) consumer_sync();
         if (p > 0) {
             if (tid == 0) {
                 const bool xr = a.ph[p - 1].xrank != 0;
