@@ -1018,6 +1018,13 @@ __device__ __forceinline__ bool smem_wait_geq(const volatile int* p, int v) {
         if (globaltimer_ns() - t0 > TK_WAIT_NS) return false;
     }
 }
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_wait() {
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
 // Bounded wait of one thread until the shared counter reaches v, sleeping between
 // polls (the waiter shares its sub-partition's issue slots with consumer warps).
 __device__ __forceinline__ bool smem_wait_geq_sleep(const volatile int* p, int v) {
@@ -1054,6 +1061,25 @@ __device__ __forceinline__ void tk_stamp(const TokenArgs& a, int p, int k) {
 __device__ __forceinline__ void tk_fail(const TokenArgs& a, TkShared* sh, uint32_t code) {
     *(volatile int*)&sh->err = 1;
     atomicOr(&a.step->error, code);
+}
+
+// Inputs of phase P that do not depend on the previous phase, copied into the
+// staging area with cp.async while thread 0 waits at the barrier: the norm
+// weights of a normed matvec (the same float4s each thread reads in tk_stage).
+// (Prefetching attention's cached K/V rows the same way measured slower.)
+__device__ __noinline__ void tk_prefetch(const TokenArgs& a, const TokenPhase& P, float* U) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (P.kind == PH_MATVEC) {
+        const MatvecArgs& m = P.mv;
+        if (!m.norm_w || (m.K & 3) || (int)blockIdx.x >= m.ntiles) return;
+        const int ck = ck_of(P.type), KP = (m.K + ck - 1) / ck * ck;
+        float* wpre = U + KP + KP / 16;
+        for (int r = warp; r < KP / 128; r += MV_CWARPS) {
+            const int e0 = 128 * r + 4 * lane;
+            if (e0 < m.K) cp_async16(wpre + e0, m.norm_w + e0);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
 }
 
 // Four consecutive inputs e0 .. e0+3 (e0 % 4 == 0) into the staged layout
@@ -1105,24 +1131,27 @@ __device__ __forceinline__ void tk_sums(float* xs16, int e0, float4 v, int lane)
 // phase (src/model/weights.rs:57-62). All global loads of a round are issued
 // before any is used (one L2 round trip per round, not one per element).
 constexpr int TK_ROUND = 4;  // 128-element runs per warp and round
-template <int TYPE>
-__device__ __forceinline__ void tk_stage(const TokenArgs& a, const TokenPhase& P, uint32_t tok, uint32_t pos, float* U,
-                                         float* red) {
+// Input sources, one instantiation each (only the code a phase uses is fetched:
+// staging runs once per phase and is latency-bound, instruction fetch included).
+enum : int { SRC_PLAIN = 0, SRC_EMBED = 1, SRC_XSUM = 2, SRC_ATT = 3 };
+template <int TYPE, int SRC>
+__device__ __noinline__ void tk_stage_src(const TokenArgs& a, const TokenPhase& P, uint32_t tok, uint32_t pos,
+                                          float* U, float* red) {
     const MatvecArgs& m = P.mv;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = m.K, KP = ((K + Fmt<TYPE>::CK - 1) / Fmt<TYPE>::CK) * Fmt<TYPE>::CK, nrun = KP / 128;
     float* xs16 = U + KP;
     const uint8_t* erow = nullptr;
-    if (P.embed_in)
+    if (SRC == SRC_EMBED)
         erow = a.embd + (size_t)tok * (K / gguf_block_elems(a.embd_type)) * gguf_block_bytes(a.embd_type);
     // tensor parallel: x = xbuf[xsrc] + the ranks' partial sums, in rank order
     // (every rank computes the same bits); CTA 0 keeps it in xbuf[xdst]
-    const bool xs = a.tp > 1 && P.xsum && !erow;
+    constexpr bool xs = SRC == SRC_XSUM;
     const float* xsrc = xs ? a.xbuf[P.xsrc] : nullptr;
     const float* rxs = xs ? a.prx[a.rank] + (size_t)P.xslot * a.tp * a.E : nullptr;
     auto load4 = [&](int e0) -> float4 {
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (xs) {
+        if constexpr (xs) {
             if (e0 < K) {  // K = E, a multiple of 4
                 v = __ldcg((const float4*)(xsrc + e0));
                 for (int r = 0; r < a.tp; ++r) {
@@ -1131,7 +1160,7 @@ __device__ __forceinline__ void tk_stage(const TokenArgs& a, const TokenPhase& P
                 }
                 if (blockIdx.x == 0) *(float4*)(a.xbuf[P.xdst] + e0) = v;
             }
-        } else if (erow) {
+        } else if constexpr (SRC == SRC_EMBED) {
             float t[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) t[i] = e0 + i < K ? dequant_elem(a.embd_type, erow, e0 + i) : 0.f;
@@ -1159,7 +1188,11 @@ __device__ __forceinline__ void tk_stage(const TokenArgs& a, const TokenPhase& P
         for (int i = 0; i < 4; ++i) t[i] = e0 + i < K ? __ldg(m.norm_w + e0 + i) : 0.f;
         return make_float4(t[0], t[1], t[2], t[3]);
     };
-    if (P.att_merge) {
+    // normed phases: the norm weights were copied to wpre before the barrier
+    // (tk_prefetch) when K is a multiple of 4
+    const float* wpre = (m.norm_w && !(K & 3)) ? U + KP + KP / 16 : nullptr;
+    if (wpre) cp_async_commit_wait();
+    if constexpr (SRC == SRC_ATT) {
         // the attention output, merged from the softmax partials of each head's
         // splits (src/math/ops.rs:15-25 normalisation, applied to the merged sums):
         // per head the weights exp(m_q - M) / L, then o = sum_q w_q o_q
@@ -1217,7 +1250,7 @@ __device__ __forceinline__ void tk_stage(const TokenArgs& a, const TokenPhase& P
             wv[i] = xv[i];
             if (r < nrun) {
                 xv[i] = load4(e0);
-                wv[i] = loadw4(e0);
+                wv[i] = wpre ? (e0 < K ? *(const float4*)(wpre + e0) : make_float4(0.f, 0.f, 0.f, 0.f)) : loadw4(e0);
             }
         }
 #pragma unroll
@@ -1261,6 +1294,19 @@ __device__ __forceinline__ void tk_stage(const TokenArgs& a, const TokenPhase& P
         }
     }
     consumer_sync();
+}
+
+template <int TYPE>
+__device__ __forceinline__ void tk_stage(const TokenArgs& a, const TokenPhase& P, uint32_t tok, uint32_t pos, float* U,
+                                         float* red) {
+    if (P.embed_in)
+        tk_stage_src<TYPE, SRC_EMBED>(a, P, tok, pos, U, red);
+    else if (P.att_merge)
+        tk_stage_src<TYPE, SRC_ATT>(a, P, tok, pos, U, red);
+    else if (a.tp > 1 && P.xsum)
+        tk_stage_src<TYPE, SRC_XSUM>(a, P, tok, pos, U, red);
+    else
+        tk_stage_src<TYPE, SRC_PLAIN>(a, P, tok, pos, U, red);
 }
 
 // Consumers of one matvec phase: stage the input, then every tile of this CTA.
@@ -1685,7 +1731,8 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
             for (int i = tid; i < (int)(sizeof(TokenPhase) / 4); i += MV_CONSUMERS) dst[i] = __ldg(src + i);
         }
         const TokenPhase& P = sph[p & 1];
-        if (p == 0) consumer_sync();
+        consumer_sync();  // the descriptor is in place; every warp is done with phase p - 1
+        tk_prefetch(a, P, U);
         if (p > 0) {
             if (tid == 0) {
                 const bool xr = a.ph[p - 1].xrank != 0;

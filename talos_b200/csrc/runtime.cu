@@ -1091,8 +1091,10 @@ static void fused_check(talos_ctx* c) {
     for (const auto& p : ph)
         if (p.kind == PH_MATVEC) {
             const int kp = token_stage_elems(p.type, p.mv.K);
-            // staged input + block sums (+ the attention merge weights of o-proj)
-            const int b = kp * 4 + kp / 16 * 4 + (p.att_merge ? c->nh_l * c->nsplit * 4 : 0);
+            // staged input + block sums (+ the attention merge weights of o-proj, or
+            // the prefetched norm weights of a normed phase)
+            const int b = kp * 4 + kp / 16 * 4 + (p.att_merge ? c->nh_l * c->nsplit * 4 : 0) +
+                          (p.mv.norm_w ? kp * 4 : 0);
             if (b > ub) ub = b;
         }
     ub = (ub + 15) / 16 * 16;
