@@ -267,6 +267,25 @@ talos_status talos_matvec_dev(const talos_weight* w, const float* x_dev, float* 
                               void* stream);
 
 /*
+ * talos_matvec_dev without allocating: a split-K variant (each CTA takes one
+ * 16-row tile and one slice of the columns; the slices' partial sums meet in a
+ * fixed-size scratch array that the library holds as static device memory, and
+ * the last slice of a tile adds them in slice order). For callers that must not
+ * allocate device memory during decoding: a runtime that reserves the device's
+ * memory up front, or a loop that cannot take the device-wide synchronisation
+ * of cudaMalloc / cudaFree. Limits: at most 65,536 rows (the scratch is 2 MB of
+ * partial sums + 16 KB of arrival counters) and columns whose staged input
+ * fits shared memory (about 47,000); larger weights fail with
+ * TALOS_ERR_UNSUPPORTED. The first call on a device resolves the scratch's
+ * address (cudaGetSymbolAddress); make it before any stream capture. Calls
+ * share the scratch: two calls in flight at once (other streams, other
+ * threads) race, so serialise them. Results agree with talos_matvec_dev to
+ * rounding (another summation order) and are identical call to call. No
+ * reference counterpart.
+ */
+talos_status talos_matvec_dev_noalloc(const talos_weight* w, const float* x_dev, float* y_dev, void* stream);
+
+/*
  * Benchmark helper: capture `reps` back-to-back talos_matvec_dev launches that
  * cycle through the n weights ws[0..n-1] (same shape) into one CUDA graph, replay
  * it once to warm up and once timed with CUDA events, and write the average

@@ -58,6 +58,7 @@ SIGNATURES = {
     "talos_weight_destroy": (_i, [_vp]),
     "talos_weight_packed_bytes": (_i, [_vp, C.POINTER(_sz)]),
     "talos_matvec_dev": (_i, [_vp, _vp, _vp, _vp]),
+    "talos_matvec_dev_noalloc": (_i, [_vp, _vp, _vp, _vp]),
     "talos_matvec_bench": (_i, [C.POINTER(_vp), _i, _vp, _vp, _i, C.POINTER(C.c_float)]),
 }
 

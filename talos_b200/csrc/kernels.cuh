@@ -65,6 +65,13 @@ cudaError_t matvec_configure();  // opt-in shared memory limits, once per proces
 int matvec_ctas_per_sm(int type, int K);
 int matvec_max_k(int type);      // largest input length the staged activation fits
 
+// Split-K matvec whose partial sums live in a static device array (no allocation):
+// the array's address and limits, and the launch (nslice K slices per 16-row tile).
+cudaError_t noalloc_scratch(float** part, unsigned** cnt, int* max_tiles, int* max_slices);
+size_t noalloc_smem_bytes(int type, int K);
+cudaError_t launch_matvec_noalloc(const PackedW& w, const float* x, float* y, int nslice, float* part,
+                                  unsigned* cnt, cudaStream_t s);
+
 // ---------------------------------------------------------------- attention
 
 struct AttnArgs {

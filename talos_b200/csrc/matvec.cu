@@ -1801,6 +1801,171 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
     }
 }
 
+// ============================================================================
+// Split-K matvec with static scratch (talos_matvec_dev_noalloc)
+// ============================================================================
+//
+// y = W x like k_matvec, but each CTA takes one (16-row tile, K slice) unit, so
+// a short matrix still spreads over every SM. A unit's 16 partial row sums go
+// to a scratch array; the CTA that completes a tile's last slice (an arrival
+// counter per tile) adds the slices in slice order and writes the rows, then
+// sets the counter back to zero. The scratch is a file-scope __device__ array of
+// fixed size, so the entry point allocates nothing: it serves callers that must
+// not allocate, e.g. a decode loop driven by a runtime that reserves all device
+// memory up front, or a caller that cannot afford the device-wide
+// synchronisation cudaMalloc / cudaFree imply. Limits: at most
+// NOALLOC_MAX_TILES tiles (65,536 rows) and NOALLOC_MAX_SLICES slices.
+// Concurrent calls share the scratch and race; callers serialise them.
+
+constexpr int NOALLOC_MAX_TILES = 4096;
+constexpr int NOALLOC_MAX_SLICES = 8;
+// partial row sums [tile][slice][16] (2 MB) and arrival counters [tile], zero at
+// module load; every call leaves the counters at zero again
+static __device__ __align__(256) float g_noalloc_part[NOALLOC_MAX_TILES * NOALLOC_MAX_SLICES * 16];
+static __device__ __align__(256) unsigned g_noalloc_cnt[NOALLOC_MAX_TILES];
+
+template <int TYPE>
+__global__ void __launch_bounds__(MV_CONSUMERS, 1)
+    k_matvec_splitk(const PackedW w, const float* __restrict__ x, float* __restrict__ y, int nslice, float* part,
+                    unsigned* cnt) {
+    constexpr int GCB = Fmt<TYPE>::GCB, CK = Fmt<TYPE>::CK;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ float red[MV_CWARPS * 16];
+    __shared__ int last, sok;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = w.cols, nchunk = w.nk, KP = nchunk * CK;
+    const int tile = blockIdx.x / nslice, slice = blockIdx.x % nslice;
+    const int per = (nchunk + nslice - 1) / nslice, c0 = slice * per, c1 = min(nchunk, c0 + per);
+    uint8_t* stage = smem;                      // one chunk: two group-chunks
+    float* U = (float*)(smem + 2 * GCB);        // staged x: KP floats, then KP / 16 block sums
+    float* xs16 = U + KP;
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        sok = 1;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    // stage x (all of it: consume_* index the staged input by absolute chunk)
+    for (int r = warp; r < KP / 128; r += MV_CWARPS) {
+        const int e0 = 128 * r + 4 * lane;
+        float t4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) t4[i] = e0 + i < K ? x[e0 + i] : 0.f;
+        const float4 v = make_float4(t4[0], t4[1], t4[2], t4[3]);
+        tk_put4<TYPE>(U, e0, v);
+        tk_sums<TYPE>(xs16, e0, v, lane);
+    }
+    __syncthreads();
+    Acc acc = {0.f, 0.f, 0.f, 0.f};
+    bool ok = true;
+    int issued = 0;  // thread 0: chunks copied
+    for (int c = c0; c < c1; ++c) {
+        const uint32_t parity = (uint32_t)(c - c0) & 1u;
+        if (tid == 0 && *(volatile int*)&sok) {
+            ++issued;
+            const uint8_t* ga = (const uint8_t*)w.p0 + ((size_t)(2 * tile) * w.nk + c) * GCB;
+            const uint8_t* gb = (const uint8_t*)w.p0 + ((size_t)(2 * tile + 1) * w.nk + c) * GCB;
+            mbar_expect_tx(&bar, 2 * GCB);
+            bulk_g2s(stage, ga, GCB, &bar);
+            bulk_g2s(stage + GCB, gb, GCB, &bar);
+        }
+        if (ok && !mbar_wait(&bar, parity)) {  // bounded (2 s): record it, stop copying
+            ok = false;
+            *(volatile int*)&sok = 0;
+        }
+        if (ok) {
+            if (TYPE == GT_Q4_0)
+                consume_q4_0(stage, stage + GCB, (const uint4*)U, xs16, c, acc);
+            else if (TYPE == GT_Q8_0)
+                consume_q8_0(stage, stage + GCB, (const uint4*)U, xs16, c, acc);
+            else if (TYPE == GT_Q6_K)
+                consume_q6_k(stage, stage + GCB, (const uint4*)U, xs16, c, acc);
+            else
+                consume_f32(stage, stage + GCB, U, c, acc);
+        }
+        __syncthreads();  // the stage is free for the next chunk
+    }
+    // the 16 warps' partials of the unit -> 16 row sums
+    if (TYPE == GT_F32) {
+        const float v = warp_sum(acc.pA);
+        if (lane < 16) red[warp * 16 + lane] = (lane == warp) ? v : 0.f;
+    } else if ((lane & 3) == 0) {
+        red[warp * 16 + (lane >> 2)] = fmaf(acc.pA, kTwo24, -Zero<TYPE>::z * acc.qA);
+        red[warp * 16 + 8 + (lane >> 2)] = fmaf(acc.pB, kTwo24, -Zero<TYPE>::z * acc.qB);
+    }
+    __syncthreads();
+    if (tid < 16) {
+        float v = 0.f;
+        for (int q = 0; q < MV_CWARPS; ++q) v += red[q * 16 + tid];
+        part[((size_t)tile * nslice + slice) * 16 + tid] = v;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        // a copy still in flight after a timed-out wait lands before the CTA leaves
+        if (!sok && issued) mbar_wait(&bar, (uint32_t)(issued - 1) & 1u);
+        const unsigned old = atomicAdd(&cnt[tile], 1u);
+        last = old == (unsigned)(nslice - 1);
+        if (last) cnt[tile] = 0u;  // every slice has arrived: ready for the next call
+    }
+    __syncthreads();
+    if (!last || tid >= 16) return;
+    __threadfence();
+    float v = 0.f;
+    for (int q = 0; q < nslice; ++q) v += __ldcg(part + ((size_t)tile * nslice + q) * 16 + tid);
+    const int row = 16 * tile + tid;
+    if (row < w.rows) y[row] = sok ? v : __int_as_float(0x7fc00000);  // NaN rows: a copy timed out
+}
+
+size_t noalloc_smem_bytes(int type, int K) {
+    const int ck = fmt_ck(type);
+    if (!ck) return 0;
+    const int kp = ceil_div_h(K, ck) * ck;
+    return (size_t)2 * fmt_gcb(type) + (size_t)kp * 4 + (size_t)kp / 16 * 4;
+}
+
+cudaError_t noalloc_scratch(float** part, unsigned** cnt, int* max_tiles, int* max_slices) {
+    cudaError_t e = cudaGetSymbolAddress((void**)part, g_noalloc_part);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress((void**)cnt, g_noalloc_cnt);
+    *max_tiles = NOALLOC_MAX_TILES;
+    *max_slices = NOALLOC_MAX_SLICES;
+    return e;
+}
+
+cudaError_t launch_matvec_noalloc(const PackedW& w, const float* x, float* y, int nslice, float* part, unsigned* cnt,
+                                  cudaStream_t s) {
+    const int ntiles = w.rows_pad / 16;
+    const size_t sm = noalloc_smem_bytes(w.type, w.cols);
+    if (!sm || sm > (size_t)kMaxSmem || ntiles > NOALLOC_MAX_TILES || nslice < 1 || nslice > NOALLOC_MAX_SLICES)
+        return cudaErrorInvalidValue;
+    cudaError_t e;
+    const dim3 grid(ntiles * nslice), block(MV_CONSUMERS);
+    switch (w.type) {
+        case GT_F32:
+            if ((e = cudaFuncSetAttribute(k_matvec_splitk<GT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem)))
+                return e;
+            k_matvec_splitk<GT_F32><<<grid, block, sm, s>>>(w, x, y, nslice, part, cnt);
+            break;
+        case GT_Q8_0:
+            if ((e = cudaFuncSetAttribute(k_matvec_splitk<GT_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem)))
+                return e;
+            k_matvec_splitk<GT_Q8_0><<<grid, block, sm, s>>>(w, x, y, nslice, part, cnt);
+            break;
+        case GT_Q4_0:
+            if ((e = cudaFuncSetAttribute(k_matvec_splitk<GT_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem)))
+                return e;
+            k_matvec_splitk<GT_Q4_0><<<grid, block, sm, s>>>(w, x, y, nslice, part, cnt);
+            break;
+        case GT_Q6_K:
+            if ((e = cudaFuncSetAttribute(k_matvec_splitk<GT_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem)))
+                return e;
+            k_matvec_splitk<GT_Q6_K><<<grid, block, sm, s>>>(w, x, y, nslice, part, cnt);
+            break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
 int token_stage_elems(int type, int K) {
     const int ck = fmt_ck(type);
     if (!ck) return 0;

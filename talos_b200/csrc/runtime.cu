@@ -228,6 +228,13 @@ static talos_status device_setup(int device) {
     return TALOS_OK;
 }
 
+static int sm_count_dev(int device) {
+    if (device >= 0 && device < 64 && g_sms[device]) return g_sms[device];
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || sms <= 0) return 148;
+    return sms;
+}
+
 static int max_ctas(int device, int type, int K) {
     int sms = (device >= 0 && device < 64 && g_sms[device]) ? g_sms[device] : 148;
     return sms * matvec_ctas_per_sm(type, K);
@@ -1569,6 +1576,46 @@ extern "C" talos_status talos_matvec_dev(const talos_weight* w, const float* x_d
     if (!w || !x_dev || !y_dev) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
     CK(cudaSetDevice(w->device));
     return matvec_on(w->t, w->device, x_dev, y_dev, (cudaStream_t)stream);
+}
+
+// talos_matvec_dev_noalloc: the static scratch's address on each device,
+// resolved on the first call there (cudaGetSymbolAddress allocates nothing).
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_part_dev[64];
+static unsigned* g_noalloc_cnt_dev[64];
+static int g_noalloc_max_tiles = 0, g_noalloc_max_slices = 0;
+
+extern "C" talos_status talos_matvec_dev_noalloc(const talos_weight* w, const float* x_dev, float* y_dev,
+                                                 void* stream) {
+    if (!w || !x_dev || !y_dev) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    if (w->device < 0 || w->device >= 64) return set_err(TALOS_ERR_INVALID_ARG, "device %d", w->device);
+    CK(cudaSetDevice(w->device));
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_part_dev[w->device]) {
+            cudaError_t e = noalloc_scratch(&g_noalloc_part_dev[w->device], &g_noalloc_cnt_dev[w->device],
+                                            &g_noalloc_max_tiles, &g_noalloc_max_slices);
+            if (e != cudaSuccess) {
+                g_noalloc_part_dev[w->device] = nullptr;
+                return set_err(TALOS_ERR_CUDA, "scratch address: %s", cudaGetErrorString(e));
+            }
+        }
+    }
+    const PackedW& pw = w->t.w;
+    const int ntiles = pw.rows_pad / 16;
+    if (ntiles > g_noalloc_max_tiles)
+        return set_err(TALOS_ERR_UNSUPPORTED, "%d rows: the static scratch holds %d rows", pw.rows,
+                       16 * g_noalloc_max_tiles);
+    if (noalloc_smem_bytes(pw.type, pw.cols) > 220 * 1024)
+        return set_err(TALOS_ERR_UNSUPPORTED, "%d columns: the staged input does not fit shared memory", pw.cols);
+    // K slices per tile: enough units for two per SM, whole chunks, at most the scratch's slices
+    const int sms = sm_count_dev(w->device);
+    int nslice = (2 * sms + ntiles - 1) / ntiles;
+    nslice = std::max(1, std::min(nslice, std::min(g_noalloc_max_slices, pw.nk)));
+    cudaError_t e = launch_matvec_noalloc(pw, x_dev, y_dev, nslice, g_noalloc_part_dev[w->device],
+                                          g_noalloc_cnt_dev[w->device], (cudaStream_t)stream);
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "split-K matvec: %s", cudaGetErrorString(e));
+    return TALOS_OK;
 }
 
 extern "C" talos_status talos_matvec_bench(const talos_weight* const* ws, int n, const float* x_dev, float* y_dev,

@@ -334,6 +334,12 @@ class Weight:
     def matvec_dev(self, x_ptr: int, y_ptr: int, stream: int = 0):
         _lib.check(_lib.load().talos_matvec_dev(self.h, C.c_void_p(x_ptr), C.c_void_p(y_ptr), C.c_void_p(stream)))
 
+    def matvec_dev_noalloc(self, x_ptr: int, y_ptr: int, stream: int = 0):
+        """talos_matvec_dev_noalloc: the split-K variant that allocates nothing
+        (static scratch; calls in flight at once race)."""
+        _lib.check(_lib.load().talos_matvec_dev_noalloc(self.h, C.c_void_p(x_ptr), C.c_void_p(y_ptr),
+                                                        C.c_void_p(stream)))
+
     def close(self):
         if getattr(self, "h", None):
             _lib.load().talos_weight_destroy(self.h)
