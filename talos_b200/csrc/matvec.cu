@@ -1130,7 +1130,9 @@ __device__ __forceinline__ void tk_sums(float* xs16, int e0, float4 v, int lane)
 // (src/math/ops.rs:5-12, (x * s) * w), the token's embedding row for the first
 // phase (src/model/weights.rs:57-62). All global loads of a round are issued
 // before any is used (one L2 round trip per round, not one per element).
-constexpr int TK_ROUND = 4;  // 128-element runs per warp and round
+#ifndef TK_ROUND
+#define TK_ROUND 4  // 128-element runs per warp and round
+#endif
 // Input sources, one instantiation each (only the code a phase uses is fetched:
 // staging runs once per phase and is latency-bound, instruction fetch included).
 enum : int { SRC_PLAIN = 0, SRC_EMBED = 1, SRC_XSUM = 2, SRC_ATT = 3 };
