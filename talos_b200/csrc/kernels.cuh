@@ -144,7 +144,8 @@ struct TokenArgs {
                                 // entered, inputs staged, compute done, barrier arrival
     // tensor parallel: tp ranks, one per GPU; peer pointers are CUDA IPC mappings
     int tp, rank;
-    unsigned long long* pbars[TALOS_MAX_TP];  // each rank's barrier counters (own: bars)
+    unsigned long long* rbars;                // [nph] rank arrivals at cross-rank phases
+    unsigned long long* prbars[TALOS_MAX_TP]; // each rank's rbars (own: rbars)
     float* prx[TALOS_MAX_TP];                 // each rank's receive slots [2][tp][E]
     float* plogits[TALOS_MAX_TP];             // each rank's full logits [vocab]
     unsigned long long* pkey[TALOS_MAX_TP];   // each rank's StepParams::argmax_key

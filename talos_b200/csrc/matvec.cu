@@ -1000,13 +1000,24 @@ __device__ __noinline__ bool grid_wait_one(const unsigned long long* bar, unsign
         if (globaltimer_ns() - t0 > TK_WAIT_NS) return false;
     }
 }
-// One CTA's arrival at phase p's barrier: on this GPU, or (xrank) on every rank.
+// One CTA's arrival at phase p's barrier. A cross-rank phase (xrank) arrives at
+// system scope so that its stores into the peers' memory travel with the
+// release chain: local counter -> CTA 0 -> one add on every rank's rank counter
+// (tk_rank_wait), instead of 148 remote adds per rank on one address.
 __device__ __forceinline__ void tk_arrive(const TokenArgs& a, int p, bool xrank) {
-    if (xrank) {
-        for (int r = 0; r < a.tp; ++r) red_release_sys_add_u64(a.pbars[r] + p, 1ull);
-    } else {
+    if (xrank)
+        red_release_sys_add_u64(&a.bars[p], 1ull);
+    else
         red_release_add_u64(&a.bars[p], 1ull);
+}
+// Cross-rank barrier of phase p (thread 0 of each CTA): CTA 0 waits for this
+// rank's CTAs and signals every rank; then every CTA waits for all ranks.
+__device__ __forceinline__ bool tk_rank_wait(const TokenArgs& a, int p, unsigned long long target) {
+    if (blockIdx.x == 0) {
+        if (!grid_wait_one(&a.bars[p], target, true)) return false;
+        for (int r = 0; r < a.tp; ++r) red_release_sys_add_u64(a.prbars[r] + p, 1ull);
     }
+    return grid_wait_one(&a.rbars[p], (target / gridDim.x) * (unsigned)a.tp, true);
 }
 // Bounded spin until the shared counter reaches v.
 __device__ __forceinline__ bool smem_wait_geq(const volatile int* p, int v) {
@@ -1658,7 +1669,6 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
                 // warp barrier makes them precede it; release is cumulative), so no
                 // separate fence: a fence here also waits out this SM's in-flight
                 // weight copies (about 1 us, measured).
-                if (P.xrank) __threadfence_system();
                 __syncwarp();
                 if (lane == 0) {
                     tk_arrive(a, p, P.xrank != 0);
@@ -1739,7 +1749,8 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
             if (tid == 0) {
                 const bool xr = a.ph[p - 1].xrank != 0;
                 // the acquire load orders the phase's reads; consumer_sync passes it on
-                if (!grid_wait_one(&a.bars[p - 1], xr ? target * (unsigned)a.tp : target, xr)) tk_fail(a, &sh, 4u);
+                if (!(xr ? tk_rank_wait(a, p - 1, target) : grid_wait_one(&a.bars[p - 1], target, false)))
+                    tk_fail(a, &sh, 4u);
                 *(volatile int*)&sh.started = p;
                 sh.stop = *(volatile int*)&sh.err;
                 tk_stamp(a, p, 0);
@@ -1788,16 +1799,13 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
         } else {
             tk_hidden(a, P, red);
             consumer_sync();
-            if (tid == 0 && a.tp > 1) {
-                __threadfence_system();
-                tk_arrive(a, p, P.xrank != 0);
-            }
+            if (tid == 0 && a.tp > 1) tk_arrive(a, p, P.xrank != 0);
         }
     }
     if (tid == 0 && blockIdx.x == 0 && !*(volatile int*)&sh.err) {
         // tensor parallel: the kernel ends only when every rank's last phase (its
         // stores into this rank's logits and argmax key) is done
-        if (a.tp > 1 && !grid_wait_one(&a.bars[a.nph - 1], target * (unsigned)a.tp, true)) tk_fail(a, &sh, 4u);
+        if (a.tp > 1 && !tk_rank_wait(a, a.nph - 1, target)) tk_fail(a, &sh, 4u);
         // every CTA has read the epoch once it arrived at the last barrier
         atomicAdd(a.epoch, 1ull);
     }

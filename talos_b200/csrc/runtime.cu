@@ -297,6 +297,7 @@ struct talos_ctx {
     void* sync_mem = nullptr;         // barrier counters, epoch, attention partials
     size_t sync_bytes = 0;
     unsigned long long* bars = nullptr;
+    unsigned long long* rbars = nullptr;  // tensor parallel: rank arrivals (shared area)
     unsigned long long* epoch = nullptr;
     unsigned long long* stamps = nullptr;
     float* att_part = nullptr;
@@ -490,7 +491,7 @@ static talos_status alloc_shared(talos_ctx* c) {
         off += align256(bytes);
         return o;
     };
-    const size_t o_bars = take((size_t)c->nph_max * 8);
+    const size_t o_bars = take((size_t)c->nph_max * 8), o_rbars = take((size_t)c->nph_max * 8);
     c->shared_bars_bytes = off;
     const size_t o_step = take(sizeof(StepParams)), o_rx = take(2 * (size_t)c->tp * E * 4), o_log = take(V * 4);
     CK(cudaMalloc(&c->shared, off));
@@ -498,6 +499,7 @@ static talos_status alloc_shared(talos_ctx* c) {
     CK(cudaMemset(c->shared, 0, off));
     uint8_t* b = (uint8_t*)c->shared;
     c->bars = (unsigned long long*)(b + o_bars);
+    c->rbars = (unsigned long long*)(b + o_rbars);
     c->step = (StepParams*)(b + o_step);
     c->logits = (float*)(b + o_log);
     (void)o_rx;
@@ -1165,15 +1167,16 @@ static TokenArgs token_args(talos_ctx* c, GraphMode mode, unsigned long long* st
     a.vocab_off = c->v_off;
     a.xbuf[0] = c->xbuf[0];
     a.xbuf[1] = c->xbuf[1];
+    a.rbars = c->rbars;
     if (c->tp > 1) {
         // peer addresses: the same offsets inside every rank's shared area
-        const size_t o_bars = (uint8_t*)c->bars - (uint8_t*)c->shared;
+        const size_t o_rbars = (uint8_t*)c->rbars - (uint8_t*)c->shared;
         const size_t o_key = (uint8_t*)&c->step->argmax_key - (uint8_t*)c->shared;
         const size_t o_log = (uint8_t*)c->logits - (uint8_t*)c->shared;
-        const size_t o_rx = align256((size_t)c->nph_max * 8) + align256(sizeof(StepParams));
+        const size_t o_rx = 2 * align256((size_t)c->nph_max * 8) + align256(sizeof(StepParams));
         for (int r = 0; r < c->tp; ++r) {
             uint8_t* b = (uint8_t*)c->peer_base[r];
-            a.pbars[r] = (unsigned long long*)(b + o_bars);
+            a.prbars[r] = (unsigned long long*)(b + o_rbars);
             a.pkey[r] = (unsigned long long*)(b + o_key);
             a.plogits[r] = (float*)(b + o_log);
             a.prx[r] = (float*)(b + o_rx);
