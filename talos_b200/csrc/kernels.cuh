@@ -153,6 +153,8 @@ struct TokenArgs {
     float* xbuf[2];                           // residual stream, double-buffered (tp > 1)
 };
 
+// Whether attention items are single query heads (else kv heads with their group).
+bool token_attn_per_head();
 // Staged-input elements the k_token scratch region must hold for input length K.
 int token_stage_elems(int type, int K);
 // Scratch bytes attention needs for `group` heads of `hd` dims.

@@ -947,6 +947,9 @@ constexpr int TK_MAX_SPLIT = 8;                // position splits per kv head in
 #ifndef TK_SPLIT_POS
 #define TK_SPLIT_POS 64                        // positions per split the split count aims for
 #endif
+#ifndef TK_ATT_PER_HEAD
+#define TK_ATT_PER_HEAD 1                      // attention items per query head (else per kv head)
+#endif
 #ifndef TK_PAIR_CHUNKS
 #define TK_PAIR_CHUNKS 1                       // consume two ring stages per step
 #endif
@@ -1426,17 +1429,18 @@ template <int G>
 __device__ __noinline__ void tk_attention(const TokenArgs& a, const AttnArgs& A, int p, uint32_t pos, float* U) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nsplit = a.nsplit, ns = tk_splits(nsplit, pos);
-    if ((int)blockIdx.x >= A.n_kv * ns) return;
-    const int kh = blockIdx.x / ns, s = blockIdx.x % ns;
-    // partial records {m, l, pad, pad, o[hd]} (16-byte aligned o), in shared and global memory
+    // item = (G consecutive query heads of one kv head, position split)
+    if ((int)blockIdx.x >= A.n_head / G * ns) return;
     const int group = A.n_head / A.n_kv, hd = A.hd, hs = hd + 4;
+    const int h0 = (blockIdx.x / ns) * G, s = blockIdx.x % ns, kh = h0 / group;
+    // partial records {m, l, pad, pad, o[hd]} (16-byte aligned o), in shared and global memory
     const int seq = (int)pos + 1;
     const int per = (seq + ns - 1) / ns;
     const int p0 = s * per, p1 = min(seq, p0 + per);
-    float* qs = U;               // [group][hd]
-    float* ws = U + group * hd;  // [16 warps][group][hd + 4]
-    const float* qsrc = A.q + (size_t)kh * group * hd;
-    for (int i = tid; i < group * hd; i += MV_CONSUMERS) qs[i] = __ldcg(qsrc + i);
+    float* qs = U;           // [G][hd]
+    float* ws = U + G * hd;  // [16 warps][G][hd + 4]
+    const float* qsrc = A.q + (size_t)h0 * hd;
+    for (int i = tid; i < G * hd; i += MV_CONSUMERS) qs[i] = __ldcg(qsrc + i);
     consumer_sync();
     if (tid == 0) tk_stamp(a, p, 1);
 
@@ -1488,7 +1492,7 @@ __device__ __noinline__ void tk_attention(const TokenArgs& a, const AttnArgs& A,
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         {
-            float* w = ws + (warp * group + g) * hs;
+            float* w = ws + (warp * G + g) * hs;
             if (lane == 0) {
                 w[0] = m[g];
                 w[1] = l[g];
@@ -1498,21 +1502,21 @@ __device__ __noinline__ void tk_attention(const TokenArgs& a, const AttnArgs& A,
     }
     consumer_sync();
     // merge the 16 warps: one thread per (head, dim)
-    for (int idx = tid; idx < group * hd; idx += MV_CONSUMERS) {
+    for (int idx = tid; idx < G * hd; idx += MV_CONSUMERS) {
         const int g = idx / hd, d = idx % hd;
         float M = -INFINITY;
-        for (int w = 0; w < MV_CWARPS; ++w) M = fmaxf(M, ws[(w * group + g) * hs]);
+        for (int w = 0; w < MV_CWARPS; ++w) M = fmaxf(M, ws[(w * G + g) * hs]);
         float L = 0.f, O = 0.f;
         if (M != -INFINITY) {
             for (int w = 0; w < MV_CWARPS; ++w) {
-                const float* ww = ws + (w * group + g) * hs;
+                const float* ww = ws + (w * G + g) * hs;
                 const float e = expf(ww[0] - M);
                 L = fmaf(ww[1], e, L);
                 O = fmaf(ww[4 + d], e, O);
             }
         }
 
-        float* dst = a.att_part + ((size_t)(kh * group + g) * nsplit + s) * hs;
+        float* dst = a.att_part + ((size_t)(h0 + g) * nsplit + s) * hs;
         if (d == 0) {
             dst[0] = M;
             dst[1] = L;
@@ -1783,6 +1787,9 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
                 continue;
             }
         } else if (P.kind == PH_ATTN) {
+#if TK_ATT_PER_HEAD
+            tk_attention<1>(a, P.at, p, pos, U);  // one query head per item
+#else
             switch (P.at.n_head / P.at.n_kv) {
                 case 1: tk_attention<1>(a, P.at, p, pos, U); break;
                 case 2: tk_attention<2>(a, P.at, p, pos, U); break;
@@ -1791,6 +1798,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
                 case 8: tk_attention<8>(a, P.at, p, pos, U); break;
                 default: break;  // excluded on the host (fused_check)
             }
+#endif
             consumer_sync();  // every warp's partial stores precede thread 0's release
             if (tid == 0 && p + 1 < a.nph) {
                 red_release_add_u64(&a.bars[p], 1ull);
@@ -1982,6 +1990,7 @@ int token_stage_elems(int type, int K) {
     return ceil_div_h(K, ck) * ck;
 }
 
+bool token_attn_per_head() { return TK_ATT_PER_HEAD; }
 int token_attn_bytes(int group, int hd) { return (group * hd + MV_CWARPS * group * (hd + 4)) * 4; }
 
 size_t token_smem_bytes(int nst, int union_bytes) {

@@ -446,7 +446,7 @@ static talos_status alloc_sync(talos_ctx* c) {
     const int sms = (c->device < 64 && g_sms[c->device]) ? g_sms[c->device] : 148;
     // attention: (kv head, position split) items; 8 splits keep ~64 CTAs busy on
     // the 7B shape and the o-proj staging's merge short
-    c->nsplit = std::max(1, std::min(8, sms / c->nkv_l));
+    c->nsplit = std::max(1, std::min(8, sms / (token_attn_per_head() ? c->nh_l : c->nkv_l)));
     c->nph_max = (int)c->cfg.n_layer * 5 + 1;
     size_t off = 0;
     auto take = [&](size_t bytes) {
@@ -1071,7 +1071,8 @@ static void fused_check(talos_ctx* c) {
         c->fused_why = buf;
         return;
     }
-    if (c->group != 1 && c->group != 2 && c->group != 3 && c->group != 4 && c->group != 8) {
+    if (!token_attn_per_head() && c->group != 1 && c->group != 2 && c->group != 3 && c->group != 4 &&
+        c->group != 8) {
         snprintf(buf, sizeof buf, "%d query heads per kv head (1, 2, 3, 4 or 8)", c->group);
         c->fused_why = buf;
         return;
