@@ -188,6 +188,18 @@ talos_status talos_prefill(talos_ctx* ctx, const uint32_t* tokens, size_t n, siz
                            float* last_logits);
 
 /*
+ * Teacher-forced perplexity of tokens[0..n) (n >= 2): eval::perplexity
+ * (src/eval.rs:35-52). The tokens are scored in chunks of the context length,
+ * each from an empty KV cache; at each position the negative log-likelihood of
+ * the next token (token_nll, src/eval.rs:18-23: log-sum-exp in f64) is added on
+ * the GPU, so no logits leave the device. Writes exp(mean NLL) to *ppl_out and,
+ * if not NULL, the NLL sum and the number of scored positions. Leaves the KV
+ * cache holding the last chunk.
+ */
+talos_status talos_perplexity(talos_ctx* ctx, const uint32_t* tokens, size_t n, float* ppl_out,
+                              double* nll_sum_out, size_t* scored_out);
+
+/*
  * Run one decode step (as talos_forward, logits stay on the GPU) and add the
  * device time in milliseconds of each part of it into kernel_ms[kind] and the
  * number of such parts into launches[kind] (either may be NULL), kind =

@@ -202,6 +202,38 @@ def argmax(logits) -> int:
     return int(lib().oracle_argmax(_ptr(a), a.size))
 
 
+def token_nll(logits, target: int) -> float:
+    """src/eval.rs:18-23: -log softmax(logits)[target] via log-sum-exp in f64
+    (max over f32, exp of the f32 difference widened to f64, sum in order)."""
+    lg = np.ascontiguousarray(logits, np.float32)
+    mx = np.float32(-np.inf)
+    for v in lg:  # f32 fold with f32::max
+        mx = max(mx, v)
+    d = (lg - mx).astype(np.float32).astype(np.float64)
+    sumexp = 0.0
+    for e in np.exp(d):  # sequential f64 sum, as the iterator's .sum()
+        sumexp += float(e)
+    log_prob = float(np.float32(lg[target] - mx)) - np.log(sumexp)
+    return float(np.float32(-log_prob))
+
+
+def perplexity(model, tokens) -> float:
+    """src/eval.rs:35-52: teacher-forced perplexity in chunks of the context length,
+    each from a fresh KV cache."""
+    assert len(tokens) >= 2
+    ctx = model.cfg.context_length
+    nll, scored = 0.0, 0
+    for c0 in range(0, len(tokens), ctx):
+        chunk = tokens[c0:c0 + ctx]
+        if len(chunk) < 2:
+            break
+        model.reset()
+        for pos in range(len(chunk) - 1):
+            nll += token_nll(model.forward(chunk[pos], pos), chunk[pos + 1])
+            scored += 1
+    return float(np.float32(np.exp(nll / scored)))
+
+
 def quantize(gtype: int, x) -> np.ndarray:
     x = np.ascontiguousarray(x, np.float32)
     be, bb = BLOCK_ELEMS[gtype], BLOCK_BYTES[gtype]

@@ -49,6 +49,7 @@ SIGNATURES = {
     "talos_forward_hidden": (_i, [_vp, _u32, _sz, _vp]),
     "talos_generate_greedy": (_i, [_vp, _u32, _sz, _sz, _vp]),
     "talos_prefill": (_i, [_vp, _vp, _sz, _sz, _vp]),
+    "talos_perplexity": (_i, [_vp, _vp, _sz, C.POINTER(C.c_float), C.POINTER(C.c_double), C.POINTER(_sz)]),
     "talos_profile_step": (_i, [_vp, _u32, _sz, _vp, _vp]),
     "talos_profile_phases": (_i, [_vp, _u32, _sz, _vp, _sz, C.POINTER(_i), C.POINTER(_i)]),
     "talos_dequant": (_i, [_i, _vp, _sz, _vp]),

@@ -335,6 +335,41 @@ __global__ void k_greedy_advance(StepParams* step, uint32_t* gen, int cap) {
     step->pos = step->pos + 1;
 }
 
+// Perplexity (src/eval.rs:18-23): acc[0] += -log softmax(logits)[target], the
+// log-sum-exp in f64 like token_nll; acc[1] counts the scored positions.
+// One block of 1024 threads, fixed reduction order (deterministic).
+__global__ void k_token_nll(const float* logits, int n, uint32_t target, double* acc) {
+    __shared__ float smax[32];
+    __shared__ double ssum[32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float m = -INFINITY;
+    for (int i = tid; i < n; i += blockDim.x) m = fmaxf(m, logits[i]);
+    m = warp_max(m);
+    if (lane == 0) smax[warp] = m;
+    __syncthreads();
+    m = smax[0];
+    for (int w = 1; w < (int)(blockDim.x / 32); ++w) m = fmaxf(m, smax[w]);
+    double se = 0.0;
+    for (int i = tid; i < n; i += blockDim.x) se += exp((double)(logits[i] - m));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
+    if (lane == 0) ssum[warp] = se;
+    __syncthreads();
+    if (tid == 0) {
+        double tot = 0.0;
+        for (int w = 0; w < (int)(blockDim.x / 32); ++w) tot += ssum[w];
+        const double log_prob = (double)(logits[target] - m) - log(tot);
+        const float nll = (float)(-log_prob);
+        acc[0] += (double)nll;
+        acc[1] += 1.0;
+    }
+}
+
+cudaError_t launch_token_nll(const float* logits, int n, uint32_t target, double* acc, cudaStream_t s) {
+    k_token_nll<<<1, 1024, 0, s>>>(logits, n, target, acc);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_greedy_advance(StepParams* step, uint32_t* gen, int cap, cudaStream_t s, bool pdl) {
     return launch_ex(k_greedy_advance, dim3(1), dim3(1), 0, s, pdl, 1, step, gen, cap);
 }

@@ -95,6 +95,9 @@ cudaError_t launch_embed(const uint8_t* embd_raw, int type, int cols, int vocab,
 // out = rmsnorm(x, w)
 cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, float* out,
                            cudaStream_t s, bool pdl);
+// acc[0] += the negative log-likelihood logits[0..n) give `target` (f64 log-sum-exp),
+// acc[1] += 1 (src/eval.rs:18-23).
+cudaError_t launch_token_nll(const float* logits, int n, uint32_t target, double* acc, cudaStream_t s);
 // Greedy feedback: token = argmax, append it to gen[], pos += 1.
 cudaError_t launch_greedy_advance(StepParams* step, uint32_t* gen, int gen_cap, cudaStream_t s, bool pdl);
 

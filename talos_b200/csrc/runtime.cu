@@ -1413,6 +1413,45 @@ static talos_status profile_fused(talos_ctx* c, double* kernel_ms, uint32_t* lau
     return TALOS_OK;
 }
 
+extern "C" talos_status talos_perplexity(talos_ctx* c, const uint32_t* tokens, size_t n, float* ppl_out,
+                                         double* nll_sum_out, size_t* scored_out) {
+    if (!c || (!tokens && n) || !ppl_out) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    if (n < 2) return set_err(TALOS_ERR_INVALID_ARG, "perplexity needs at least 2 tokens, got %zu", n);
+    CK(cudaSetDevice(c->device));
+    for (size_t i = 0; i < n; ++i)
+        if (tokens[i] >= c->cfg.vocab_size)
+            return set_err(TALOS_ERR_INVALID_ARG, "token %u at %zu out of range (vocab %u)", tokens[i], i,
+                           c->cfg.vocab_size);
+    TRY(ensure_graph(c, GM_LOGITS));
+    double* acc = nullptr;  // [nll sum, scored] on the device
+    CK(cudaMalloc(&acc, 2 * sizeof(double)));
+    talos_status st = TALOS_OK;
+    cudaError_t e = cudaMemsetAsync(acc, 0, 2 * sizeof(double), c->stream);
+    // chunks of the context length, each from an empty cache (src/eval.rs:35-52)
+    const size_t chunk = c->kv_ctx;
+    for (size_t c0 = 0; e == cudaSuccess && c0 + 1 < n; c0 += chunk) {
+        const size_t len = std::min(chunk, n - c0);
+        if (len < 2) break;  // a trailing single token predicts nothing
+        for (size_t pos = 0; e == cudaSuccess && pos + 1 < len; ++pos) {
+            k_set_step<<<1, 1, 0, c->stream>>>(c->step, tokens[c0 + pos], (uint32_t)pos);
+            e = cudaGetLastError();
+            if (e == cudaSuccess) e = cudaGraphLaunch(c->graph[GM_LOGITS], c->stream);
+            if (e == cudaSuccess)
+                e = launch_token_nll(c->logits, (int)c->cfg.vocab_size, tokens[c0 + pos + 1], acc, c->stream);
+        }
+    }
+    double h[2] = {0.0, 0.0};
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h, acc, sizeof h, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) st = finish_step(c);
+    cudaFree(acc);
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "perplexity: %s", cudaGetErrorString(e));
+    TRY(st);
+    *ppl_out = (float)exp(h[0] / h[1]);
+    if (nll_sum_out) *nll_sum_out = h[0];
+    if (scored_out) *scored_out = (size_t)h[1];
+    return TALOS_OK;
+}
+
 extern "C" talos_status talos_profile_phases(talos_ctx* c, uint32_t token, size_t pos, uint64_t* out, size_t cap,
                                              int* n_phase, int* n_cta) {
     if (!c || !out || !n_phase || !n_cta) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");

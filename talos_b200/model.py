@@ -195,6 +195,14 @@ class Context:
     def reset(self):
         _lib.check(_lib.load().talos_kv_reset(self.h))
 
+    def perplexity(self, tokens) -> tuple[float, float, int]:
+        """talos_perplexity: (perplexity, NLL sum, scored positions)."""
+        toks = np.ascontiguousarray(tokens, np.uint32)
+        ppl, nll, n = C.c_float(), C.c_double(), C.c_size_t()
+        _lib.check(_lib.load().talos_perplexity(self.h, _ptr(toks), toks.size, C.byref(ppl), C.byref(nll),
+                                                C.byref(n)))
+        return ppl.value, nll.value, n.value
+
     KERNEL_KINDS = ("embed", "qkv", "attn", "oproj", "gateup", "down", "output")
 
     def profile_step(self, token: int, pos: int) -> tuple[dict, dict]:
@@ -292,6 +300,10 @@ class Model:
 
     def generate_greedy(self, token: int, pos: int, n: int) -> np.ndarray:
         return self.ctx.generate_greedy(token, pos, n)
+
+    def perplexity(self, tokens) -> float:
+        """eval::perplexity (src/eval.rs:35-52) on the GPU."""
+        return self.ctx.perplexity(tokens)[0]
 
     def prefill(self, tokens, pos0: int = 0):
         return self.ctx.prefill(tokens, pos0)

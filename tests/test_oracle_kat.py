@@ -264,3 +264,44 @@ def test_argmax_ties_take_last():
     # total_cmp: +0.0 > -0.0, NaN above everything
     assert oracle.argmax([0.0, -0.0]) == 0
     assert oracle.argmax([1.0, float("nan"), 3.0]) == 1
+
+
+# ---------------------------------------------------------------- perplexity (src/eval.rs)
+
+
+def test_token_nll_uniform_is_ln_vocab():  # eval.rs: uniform_logits_score_ln_vocab
+    v = 50
+    for target in (0, 7, v - 1):
+        assert abs(oracle.token_nll(np.zeros(v, np.float32), target) - np.log(v)) < 1e-4
+
+
+def test_token_nll_confident_is_near_zero():  # eval.rs: confident_correct_prediction_scores_near_zero
+    lg = np.zeros(16, np.float32)
+    lg[5] = 100.0
+    assert oracle.token_nll(lg, 5) < 1e-3
+
+
+def test_token_nll_hand_softmax():  # eval.rs: nll_matches_hand_computed_softmax
+    lg = np.array([1.0, 2.0, 3.0], np.float32)
+    want = -np.log(np.exp(3.0) / (np.exp(1.0) + np.exp(2.0) + np.exp(3.0)))
+    assert abs(oracle.token_nll(lg, 2) - want) < 1e-5
+
+
+def test_perplexity_chunks_from_a_fresh_cache():
+    """eval.rs:35-52: chunks of the context length, each scored from position 0."""
+    from .helpers import prompt, tiny_model
+    from talos_b200 import gguf
+
+    m = oracle.Model(data=tiny_model(gguf.F32))
+    m.cap_context(8)
+    toks = prompt(19, 4096, 3)  # chunks of 8, 8, 3
+    got = oracle.perplexity(m, toks)
+    nll, n = 0.0, 0
+    for c0 in (0, 8, 16):
+        ch = toks[c0:c0 + 8]
+        m.reset()
+        for pos in range(len(ch) - 1):
+            nll += oracle.token_nll(m.forward(ch[pos], pos), ch[pos + 1])
+            n += 1
+    assert n == 7 + 7 + 2
+    assert got == np.float32(np.exp(nll / n))
