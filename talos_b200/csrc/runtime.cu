@@ -21,6 +21,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <unordered_map>
 #include <vector>
 
@@ -125,22 +126,73 @@ static size_t raw_len(int type, size_t rows, size_t cols) {
 struct DevTensor {
     int type = -1;
     size_t rows = 0, cols = 0;
-    void* mem = nullptr;  // one allocation holding every array
+    void* mem = nullptr;  // one range holding every array
     size_t bytes = 0;
+    size_t cap = 0;       // bytes of the range (>= bytes)
+    bool in_arena = false;  // carved from a WeightArena block, not freed alone
     PackedW w{};          // packed matrix view (kind == PACKED)
     enum Kind { PACKED, FLOATS, RAW } kind = PACKED;
     void release() {
-        if (mem) cudaFree(mem);
+        if (mem && !in_arena) cudaFree(mem);
         mem = nullptr;
-        bytes = 0;
+        bytes = cap = 0;
+        in_arena = false;
     }
 };
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-// Allocate and fill a packed matrix from raw GGUF bytes already on the device.
+// Device memory for a context's weights: a few large blocks handed out by a
+// bump pointer. cudaMalloc costs milliseconds per call and cudaFree more (it
+// waits for the device), so a separate allocation per tensor made a model
+// upload allocation-bound. Blocks grow geometrically from 16 MB to 256 MB (a
+// tensor larger than that gets a block of its own), so a tiny model holds
+// little and a 7B model about 20 blocks. A re-uploaded tensor reuses its range
+// when the new one fits; otherwise the old range stays unused until the
+// context is destroyed.
+struct WeightArena {
+    static constexpr size_t kMinBlock = (size_t)16 << 20, kMaxBlock = (size_t)256 << 20;
+    struct Block {
+        uint8_t* base;
+        size_t size, used;
+    };
+    std::vector<Block> blocks;
+    size_t total = 0;
+    talos_status alloc(size_t n, void** out) {
+        n = align256(n);
+        for (Block& b : blocks)
+            if (b.size - b.used >= n) {
+                *out = b.base + b.used;
+                b.used += n;
+                return TALOS_OK;
+            }
+        size_t want = std::max(n, std::min(kMaxBlock, std::max(kMinBlock, total)));
+        void* p = nullptr;
+        CK(cudaMalloc(&p, want));
+        blocks.push_back({(uint8_t*)p, want, n});
+        total += want;
+        *out = p;
+        return TALOS_OK;
+    }
+    // a range for `t` of `n` bytes: its own when large enough, else a new one
+    talos_status place(DevTensor* t, size_t n, void** out) {
+        if (t->in_arena && t->mem && t->cap >= n) {
+            *out = t->mem;
+            return TALOS_OK;
+        }
+        return alloc(n, out);
+    }
+    void release() {
+        for (Block& b : blocks) cudaFree(b.base);
+        blocks.clear();
+        total = 0;
+    }
+};
+
+// Fill a packed matrix from raw GGUF bytes already on the device, in a range
+// of `arena` (or its own allocation when `arena` is null).
 static talos_status pack_from_device(int type, size_t rows, size_t cols, const uint8_t* raw_dev,
-                                     DevTensor* t, cudaStream_t s) {
+                                     DevTensor* t, cudaStream_t s, WeightArena* arena) {
     PackSizes ps;
     if (rows == 0 || cols == 0 || rows > (1u << 30) || cols > (1u << 30) ||
         !pack_sizes(type, (int)rows, (int)cols, &ps))
@@ -149,7 +201,10 @@ static talos_status pack_from_device(int type, size_t rows, size_t cols, const u
     size_t o1 = align256(ps.b0), o2 = o1 + align256(ps.b1), o3 = o2 + align256(ps.b2);
     size_t total = o3 + align256(ps.b3);
     void* mem = nullptr;
-    CK(cudaMalloc(&mem, total));
+    if (arena)
+        TRY(arena->place(t, total, &mem));
+    else
+        CK(cudaMalloc(&mem, total));
     PackedW w{};
     w.type = type;
     w.rows = (int)rows;
@@ -162,46 +217,117 @@ static talos_status pack_from_device(int type, size_t rows, size_t cols, const u
     w.p3 = ps.b3 ? (uint8_t*)mem + o3 : nullptr;
     cudaError_t e = launch_pack(raw_dev, w, s);
     if (e != cudaSuccess) {
-        cudaFree(mem);
+        if (!arena) cudaFree(mem);
         return set_err(TALOS_ERR_CUDA, "pack kernel: %s", cudaGetErrorString(e));
     }
-    t->release();
+    const size_t cap = arena ? (mem == t->mem ? t->cap : align256(total)) : total;
+    if (mem != t->mem) t->release();
     t->type = type;
     t->rows = rows;
     t->cols = cols;
     t->mem = mem;
     t->bytes = total;
+    t->cap = cap;
+    t->in_arena = arena != nullptr;
     t->w = w;
     t->kind = DevTensor::PACKED;
     return TALOS_OK;
 }
 
-// Staging buffer for uploads: raw bytes go host -> device here, then get packed.
+// Upload staging. Host bytes are copied into a ring of pinned chunks by a few
+// host threads, and each chunk goes to the device with cudaMemcpyAsync while
+// the next one is being filled, so the host copy, the PCIe transfer and the
+// repack kernels of earlier tensors overlap. A call returns once the caller's
+// bytes sit in pinned memory (the caller may free them); the device side
+// finishes on the stream, and `finish` waits for it. Raw GGUF bytes of a
+// packed matrix land in `dev` first, where the pack kernel reads them.
 struct Staging {
+    static constexpr int kChunks = 4;
+    static constexpr size_t kChunk = (size_t)32 << 20;
     uint8_t* dev = nullptr;
     size_t cap = 0;
+    uint8_t* host[kChunks] = {};
+    cudaEvent_t freed[kChunks] = {};
+    int next = 0;
     talos_status reserve(size_t n) {
         if (n <= cap) return TALOS_OK;
-        if (dev) cudaFree(dev);
+        if (dev) cudaFree(dev);  // waits for the kernels still reading it
         dev = nullptr;
         cap = 0;
         CK(cudaMalloc(&dev, n));
         cap = n;
         return TALOS_OK;
     }
+    talos_status ring() {
+        if (host[0]) return TALOS_OK;
+        for (int i = 0; i < kChunks; ++i) {
+            CK(cudaHostAlloc((void**)&host[i], kChunk, cudaHostAllocPortable));
+            CK(cudaEventCreateWithFlags(&freed[i], cudaEventDisableTiming));
+        }
+        return TALOS_OK;
+    }
+    // memcpy split over up to 8 threads (page faults of a freshly mapped file
+    // are taken in parallel too)
+    static void host_copy(uint8_t* dst, const uint8_t* src, size_t n) {
+        const size_t per = (size_t)4 << 20;
+        unsigned hw = std::thread::hardware_concurrency();
+        size_t nt = std::min<size_t>({(n + per - 1) / per, hw ? hw : 1, 8});
+        if (nt <= 1) {
+            memcpy(dst, src, n);
+            return;
+        }
+        const size_t part = (n / nt + 4095) & ~(size_t)4095;
+        std::vector<std::thread> th;
+        for (size_t i = 1; i < nt; ++i) {
+            const size_t o = i * part;
+            if (o >= n) break;
+            th.emplace_back([=] { memcpy(dst + o, src + o, std::min(part, n - o)); });
+        }
+        memcpy(dst, src, std::min(part, n));
+        for (auto& t : th) t.join();
+    }
+    // host -> device through the pinned ring, asynchronous on `s`
+    talos_status h2d(void* dst, const void* src, size_t n, cudaStream_t s) {
+        TRY(ring());
+        for (size_t o = 0; o < n; o += kChunk) {
+            const size_t k = std::min(kChunk, n - o);
+            const int i = next;
+            next = (next + 1) % kChunks;
+            CK(cudaEventSynchronize(freed[i]));  // the chunk's previous transfer is done
+            host_copy(host[i], (const uint8_t*)src + o, k);
+            CK(cudaMemcpyAsync((uint8_t*)dst + o, host[i], k, cudaMemcpyHostToDevice, s));
+            CK(cudaEventRecord(freed[i], s));
+        }
+        return TALOS_OK;
+    }
+    talos_status finish(cudaStream_t s) {
+        CK(cudaStreamSynchronize(s));
+        return TALOS_OK;
+    }
     void release() {
+        for (int i = 0; i < kChunks; ++i) {
+            if (freed[i]) {
+                cudaEventSynchronize(freed[i]);
+                cudaEventDestroy(freed[i]);
+            }
+            if (host[i]) cudaFreeHost(host[i]);
+            host[i] = nullptr;
+            freed[i] = nullptr;
+        }
+        next = 0;
         if (dev) cudaFree(dev);
         dev = nullptr;
         cap = 0;
     }
 };
 
+// Raw GGUF bytes -> packed device matrix. Asynchronous on `s`: the pack kernel
+// and the transfer it reads may still run when this returns.
 static talos_status upload_packed(int type, const void* bytes, size_t len, size_t rows, size_t cols,
-                                  DevTensor* t, Staging* st, cudaStream_t s) {
+                                  DevTensor* t, Staging* st, cudaStream_t s, WeightArena* arena = nullptr) {
     TRY(st->reserve(len));
-    CK(cudaMemcpyAsync(st->dev, bytes, len, cudaMemcpyHostToDevice, s));
-    TRY(pack_from_device(type, rows, cols, st->dev, t, s));
-    CK(cudaStreamSynchronize(s));
+    TRY(st->h2d(st->dev, bytes, len, s));
+    TRY(pack_from_device(type, rows, cols, st->dev, t, s, arena));
     return TALOS_OK;
 }
 
@@ -265,6 +391,7 @@ struct talos_ctx {
     float* xbuf[2] = {nullptr, nullptr};
     size_t kv_ctx = 0;  // positions the KV cache holds
 
+    WeightArena weights;                                  // device memory of `w`
     std::unordered_map<std::string, DevTensor> w;         // model weights by GGUF name
     std::unordered_map<std::string, DevTensor> resident;  // talos_matvec_resident cache
     Staging staging;
@@ -622,6 +749,7 @@ extern "C" talos_status talos_ctx_destroy(talos_ctx* c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     c->drop_graphs();
     for (auto& kv : c->w) kv.second.release();
+    c->weights.release();
     for (auto& kv : c->resident) kv.second.release();
     c->staging.release();
     for (int r = 0; r < TALOS_MAX_TP; ++r)
@@ -701,18 +829,22 @@ extern "C" talos_status talos_weight_upload(talos_ctx* c, const char* name, cons
     if (is_norm || nm == "token_embd.weight") {
         // Kept as-is: norm weights as f32, the embedding as raw GGUF blocks (one
         // row is dequantized per token on the GPU).
-        t.release();
         void* mem = nullptr;
-        CK(cudaMalloc(&mem, len));
-        CK(cudaMemcpy(mem, bytes, len, cudaMemcpyHostToDevice));
+        TRY(c->weights.place(&t, len, &mem));
+        if (mem != t.mem) {
+            t.release();
+            t.cap = align256(len);
+        }
+        TRY(c->staging.h2d(mem, bytes, len, c->stream));
         t.type = type;
         t.rows = is_norm ? 1 : rows;
         t.cols = is_norm ? ec : cols;
         t.mem = mem;
         t.bytes = len;
+        t.in_arena = true;
         t.kind = is_norm ? DevTensor::FLOATS : DevTensor::RAW;
     } else {
-        TRY(upload_packed(type, bytes, len, rows, cols, &t, &c->staging, c->stream));
+        TRY(upload_packed(type, bytes, len, rows, cols, &t, &c->staging, c->stream, &c->weights));
     }
     c->weights_dirty = true;
     c->drop_graphs();
@@ -721,8 +853,7 @@ extern "C" talos_status talos_weight_upload(talos_ctx* c, const char* name, cons
 
 extern "C" talos_status talos_ctx_device_bytes(talos_ctx* c, size_t* out) {
     if (!c || !out) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
-    size_t n = c->arena_bytes + c->kv_bytes + c->staging.cap + c->sync_bytes;
-    for (auto& kv : c->w) n += kv.second.bytes;
+    size_t n = c->arena_bytes + c->kv_bytes + c->staging.cap + c->sync_bytes + c->weights.total;
     for (auto& kv : c->resident) n += kv.second.bytes;
     *out = n;
     return TALOS_OK;
@@ -1213,6 +1344,9 @@ static talos_status enqueue_fused(talos_ctx* c, GraphMode mode, unsigned long lo
 
 static talos_status bind_if_dirty(talos_ctx* c) {
     if (c->weights_dirty) {
+        // the uploads ran asynchronously: wait for them, then drop the staging
+        TRY(c->staging.finish(c->stream));
+        c->staging.release();
         TRY(bind_layers(c));
         fused_check(c);
         c->drop_graphs();
@@ -1595,6 +1729,7 @@ extern "C" talos_status talos_weight_create(int device, int type, const void* by
     w->device = device;
     Staging st;
     talos_status s = upload_packed(type, bytes, len, rows, cols, &w->t, &st, 0);
+    if (s == TALOS_OK) s = st.finish(0);
     st.release();
     TRY(s);
     *out = w.release();
@@ -1737,6 +1872,9 @@ extern "C" talos_status talos_matvec_resident(talos_ctx* c, const char* name, in
     // src/math/metal/mod.rs:63-72: reuse the cached buffer while the byte length matches.
     bool hit = t.mem && t.type == type && t.rows == rows && t.cols == cols &&
                raw_len(t.type, t.rows, t.cols) == len;
-    if (!hit) TRY(upload_packed(type, bytes, len, rows, cols, &t, &c->staging, c->stream));
+    if (!hit) {
+        TRY(upload_packed(type, bytes, len, rows, cols, &t, &c->staging, c->stream));
+        TRY(c->staging.finish(c->stream));
+    }
     return matvec_host(t, c->device, x, y, c->stream);
 }

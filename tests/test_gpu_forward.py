@@ -10,6 +10,7 @@ import pytest
 
 import oracle
 from talos_b200 import Model, gguf, synth
+from talos_b200.model import weight_shapes
 from talos_b200._lib import TalosError
 
 from .helpers import forward_gpu_model, gqa_pair, prompt, tiny_model
@@ -174,6 +175,31 @@ def test_fused_and_layered_agree():
     assert np.max(np.abs(la - lb)) <= 1e-5
     a.close()
     b.close()
+
+
+@pytest.mark.parametrize("second", [gguf.Q4_0, gguf.Q8_0])
+def test_reupload_replaces_weights(second):
+    """Uploading every tensor again into a loaded context (same shapes; the same
+    type reuses each tensor's device range, Q8_0 after Q4_0 needs larger ones)
+    gives the second model's logits, with the first model's forward steps run
+    before the re-upload still in the stream's history."""
+    a_bytes = tiny_model(gguf.Q4_0)
+    b_bytes = synth.llama_bytes(synth.TINY, 23, wtype=second)
+    m = Model.load_bytes(a_bytes)
+    for pos, t in enumerate([5, 6, 7]):
+        m.forward_gpu(t, pos)
+    b = gguf.GgufFile.from_bytes(b_bytes)
+    for name, (rows, cols) in weight_shapes(m.cfg).items():
+        if rows == 1:
+            m.ctx.upload(name, b.tensor_f32(name), gguf.F32, 1, cols)
+        else:
+            raw, gt = b.tensor_raw(name)
+            m.ctx.upload(name, raw, gt, rows, cols)
+    m.reset()
+    cpu = oracle.Model(data=b_bytes)
+    for pos, t in enumerate([5, 6, 7, 8]):
+        assert np.max(np.abs(m.forward_gpu(t, pos) - cpu.forward(t, pos))) <= 1e-3
+    m.close()
 
 
 @pytest.mark.slow

@@ -106,6 +106,15 @@ def test_matvec_long_and_ragged_rows(gtype, rows, cols):
     rel_close(model.matvec(gtype, raw, x, rows, cols), oracle.matvec_quant(raw, gtype, x, rows, cols))
 
 
+def test_matvec_upload_spans_staging_chunks():
+    # 38.3 MB of Q8_0: more than one 32 MB pinned staging chunk, with a ragged tail
+    rows, cols = 1100, 32768
+    raw = synth.tensor(5, "big", rows, cols, gguf.Q8_0)
+    assert len(raw) > 32 << 20 and len(raw) % (32 << 20)
+    x = synth.normal(5, "x", cols, 1.0)
+    rel_close(model.matvec(gguf.Q8_0, raw, x, rows, cols), oracle.matvec_quant(raw, gguf.Q8_0, x, rows, cols))
+
+
 def test_resident_weight_is_cached():
     # src/math/metal/mod.rs:602-625: same key, different bytes -> cached result.
     rng = np.random.default_rng(1)
