@@ -1081,6 +1081,53 @@ __device__ __forceinline__ void tk_fail(const TokenArgs& a, TkShared* sh, uint32
 // staging area with cp.async while thread 0 waits at the barrier: the norm
 // weights of a normed matvec (the same float4s each thread reads in tk_stage).
 // (Prefetching attention's cached K/V rows the same way measured slower.)
+// The per-token kernel's dynamic shared memory: the weight ring, its mbarriers
+// (full, empty; tdone, tfree for the epilogue hand-off), the staging union U,
+// the epilogue's partials, the tile's reduced rows and a reduction scratch.
+struct TkSmem {
+    uint8_t* ring;
+    uint64_t *full, *empty, *tdone, *tfree;
+    float *U, *part, *res, *red;
+};
+__device__ __forceinline__ TkSmem tk_smem(const TokenArgs& a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const uint32_t nst = (uint32_t)a.nst;
+    TkSmem m;
+    m.ring = smem;
+    m.full = (uint64_t*)(smem + (size_t)nst * TK_STAGE);
+    m.empty = m.full + nst;
+    m.tdone = m.empty + nst;  // [2]
+    m.tfree = m.tdone + 2;    // [2]
+    m.U = (float*)(smem + (size_t)nst * TK_STAGE + TK_BAR_BYTES);
+    m.part = m.U + a.union_bytes / 4;     // [2][16][16]
+    m.res = m.part + 2 * MV_CWARPS * 16;  // 16
+    m.red = m.res + 16;                   // 32
+    return m;
+}
+
+// Phase entry, called by the consumers from inside the phase's code once its
+// prologue is done (that code is then fetched while the CTA waits, not after
+// the barrier): thread 0 waits for the previous phase's barrier and tells the
+// epilogue warp the phase has started; every consumer warp then reads one stop
+// snapshot. False: the kernel is stopping.
+__device__ __forceinline__ bool tk_gate(const TokenArgs& a, int p, TkShared* sh, unsigned long long target) {
+    if (p == 0) {
+        if (threadIdx.x == 0) tk_stamp(a, 0, 0);
+        return true;
+    }
+    if (threadIdx.x == 0) {
+        const bool xr = a.ph[p - 1].xrank != 0;
+        // the acquire load orders the phase's reads; consumer_sync passes it on
+        if (!(xr ? tk_rank_wait(a, p - 1, target) : grid_wait_one(&a.bars[p - 1], target, false)))
+            tk_fail(a, sh, 4u);
+        *(volatile int*)&sh->started = p;
+        sh->stop = *(volatile int*)&sh->err;
+        tk_stamp(a, p, 0);
+    }
+    consumer_sync();
+    return !sh->stop;
+}
+
 __device__ __noinline__ void tk_prefetch(const TokenArgs& a, const TokenPhase& P, float* U) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (P.kind == PH_MATVEC) {
@@ -1151,8 +1198,8 @@ __device__ __forceinline__ void tk_sums(float* xs16, int e0, float4 v, int lane)
 // staging runs once per phase and is latency-bound, instruction fetch included).
 enum : int { SRC_PLAIN = 0, SRC_EMBED = 1, SRC_XSUM = 2, SRC_ATT = 3 };
 template <int TYPE, int SRC>
-__device__ __noinline__ void tk_stage_src(const TokenArgs& a, const TokenPhase& P, uint32_t tok, uint32_t pos,
-                                          float* U, float* red) {
+__device__ __noinline__ bool tk_stage_src(const TokenArgs& a, const TokenPhase& P, uint32_t tok, uint32_t pos,
+                                          float* U, float* red, int p, TkShared* sh, unsigned long long target) {
     const MatvecArgs& m = P.mv;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = m.K, KP = ((K + Fmt<TYPE>::CK - 1) / Fmt<TYPE>::CK) * Fmt<TYPE>::CK, nrun = KP / 128;
@@ -1208,6 +1255,7 @@ __device__ __noinline__ void tk_stage_src(const TokenArgs& a, const TokenPhase& 
     // (tk_prefetch) when K is a multiple of 4
     const float* wpre = (m.norm_w && !(K & 3)) ? U + KP + KP / 16 : nullptr;
     if (wpre) cp_async_commit_wait();
+    if (!tk_gate(a, p, sh, target)) return false;
     if constexpr (SRC == SRC_ATT) {
         // the attention output, merged from the softmax partials of each head's
         // splits (src/math/ops.rs:15-25 normalisation, applied to the merged sums):
@@ -1310,30 +1358,39 @@ __device__ __noinline__ void tk_stage_src(const TokenArgs& a, const TokenPhase& 
         }
     }
     consumer_sync();
+    return true;
 }
 
 template <int TYPE>
-__device__ __forceinline__ void tk_stage(const TokenArgs& a, const TokenPhase& P, uint32_t tok, uint32_t pos, float* U,
-                                         float* red) {
-    if (P.embed_in)
-        tk_stage_src<TYPE, SRC_EMBED>(a, P, tok, pos, U, red);
-    else if (P.att_merge)
-        tk_stage_src<TYPE, SRC_ATT>(a, P, tok, pos, U, red);
-    else if (a.tp > 1 && P.xsum)
-        tk_stage_src<TYPE, SRC_XSUM>(a, P, tok, pos, U, red);
-    else
-        tk_stage_src<TYPE, SRC_PLAIN>(a, P, tok, pos, U, red);
+__device__ __forceinline__ bool tk_stage(const TokenArgs& a, const TokenPhase& P, uint32_t tok, uint32_t pos, float* U,
+                                         float* red, int p, TkShared* sh, unsigned long long target) {
+    if (P.embed_in) return tk_stage_src<TYPE, SRC_EMBED>(a, P, tok, pos, U, red, p, sh, target);
+    if (P.att_merge) return tk_stage_src<TYPE, SRC_ATT>(a, P, tok, pos, U, red, p, sh, target);
+    if (a.tp > 1 && P.xsum) return tk_stage_src<TYPE, SRC_XSUM>(a, P, tok, pos, U, red, p, sh, target);
+    return tk_stage_src<TYPE, SRC_PLAIN>(a, P, tok, pos, U, red, p, sh, target);
 }
+
+// tk_matvec results
+enum : int { TK_DONE = 0, TK_FAILED = 1, TK_STOPPED = 2 };
 
 // Consumers of one matvec phase: stage the input, then every tile of this CTA.
 template <int TYPE>
-__device__ __noinline__ bool tk_matvec(const TokenArgs& a, const TokenPhase& P, int p, uint32_t tok, uint32_t pos,
-                                       TkShared* sh, uint8_t* ring,
-                                       uint64_t* full, uint64_t* empty, uint64_t* tdone, uint64_t* tfree, float* U,
-                                       float* part, float* red, uint32_t& slot, uint32_t& par, int& ntile) {
+__device__ __noinline__ int tk_matvec(const TokenArgs& a, const TokenPhase& P, int p, uint32_t tok, uint32_t pos,
+                                      unsigned long long target, TkShared* sh, uint32_t& slot_io, uint32_t& par_io,
+                                      int& ntile_io) {
+    const TkSmem S = tk_smem(a);
+    uint8_t* ring = S.ring;
+    uint64_t *full = S.full, *empty = S.empty, *tfree = S.tfree, *tdone = S.tdone;
+    float *U = S.U, *part = S.part, *red = S.red;
     const MatvecArgs& m = P.mv;
-    if ((int)blockIdx.x >= m.ntiles) return true;  // no tiles here: read nothing
-    tk_stage<TYPE>(a, P, tok, pos, U, red);
+    if ((int)blockIdx.x >= m.ntiles)  // no tiles here: read nothing
+        return tk_gate(a, p, sh, target) ? TK_DONE : TK_STOPPED;
+    // The ring position lives in registers for the phase: the caller's variables
+    // sit in the stack frame (local memory), and every asm statement with a
+    // memory clobber in the loop would reload them from there.
+    uint32_t slot = slot_io, par = par_io;
+    int ntile = ntile_io;
+    if (!tk_stage<TYPE>(a, P, tok, pos, U, red, p, sh, target)) return TK_STOPPED;
     if (threadIdx.x == 0) {
         *(volatile int*)&sh->staged = p;  // the producer may stream the rest of this phase
         tk_stamp(a, p, 1);
@@ -1370,7 +1427,7 @@ __device__ __noinline__ bool tk_matvec(const TokenArgs& a, const TokenPhase& P, 
         for (; c + 1 < nchunk; c += 2) {
             uint32_t s2 = slot, p2 = par;
             next(s2, p2);
-            if (!mbar_wait(&full[slot], par) || !mbar_wait(&full[s2], p2)) return false;
+            if (!mbar_wait(&full[slot], par) || !mbar_wait(&full[s2], p2)) return TK_FAILED;
             Acc acc2 = {0.f, 0.f, 0.f, 0.f};
             consume(ring + slot * TK_STAGE, c, acc);
             consume(ring + s2 * TK_STAGE, c + 1, acc2);
@@ -1389,7 +1446,7 @@ __device__ __noinline__ bool tk_matvec(const TokenArgs& a, const TokenPhase& P, 
         }
 #endif
         for (; c < nchunk; ++c) {
-            if (!mbar_wait(&full[slot], par)) return false;
+            if (!mbar_wait(&full[slot], par)) return TK_FAILED;
             consume(ring + slot * TK_STAGE, c, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
@@ -1397,7 +1454,7 @@ __device__ __noinline__ bool tk_matvec(const TokenArgs& a, const TokenPhase& P, 
         }
         // hand the tile's partials to the epilogue warp (double-buffered)
         const int b = ntile & 1;
-        if (!mbar_wait(&tfree[b], ((uint32_t)(ntile >> 1) & 1u) ^ 1u)) return false;
+        if (!mbar_wait(&tfree[b], ((uint32_t)(ntile >> 1) & 1u) ^ 1u)) return TK_FAILED;
         float* pb = part + b * MV_CWARPS * 16;
         if (TYPE == GT_F32) {
             const float v = warp_sum(acc.pA);
@@ -1410,8 +1467,11 @@ __device__ __noinline__ bool tk_matvec(const TokenArgs& a, const TokenPhase& P, 
         if (lane == 0) mbar_arrive(&tdone[b]);
         ++ntile;
     }
+    slot_io = slot;
+    par_io = par;
+    ntile_io = ntile;
     if (threadIdx.x == 0) tk_stamp(a, p, 2);
-    return true;
+    return TK_DONE;
 }
 
 // Attention for one (kv head, position split) item per CTA (src/model/llama.rs:
@@ -1426,11 +1486,12 @@ __device__ __noinline__ bool tk_matvec(const TokenArgs& a, const TokenPhase& P, 
 // instruction cache: every phase of every layer runs through it).
 constexpr int TK_ATT_UNROLL = 2;
 template <int G>
-__device__ __noinline__ void tk_attention(const TokenArgs& a, const AttnArgs& A, int p, uint32_t pos, float* U) {
+__device__ __noinline__ bool tk_attention(const TokenArgs& a, const AttnArgs& A, int p, uint32_t pos, float* U,
+                                          TkShared* sh, unsigned long long target) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nsplit = a.nsplit, ns = tk_splits(nsplit, pos);
     // item = (G consecutive query heads of one kv head, position split)
-    if ((int)blockIdx.x >= A.n_head / G * ns) return;
+    if ((int)blockIdx.x >= A.n_head / G * ns) return tk_gate(a, p, sh, target);
     const int group = A.n_head / A.n_kv, hd = A.hd, hs = hd + 4;
     const int h0 = (blockIdx.x / ns) * G, s = blockIdx.x % ns, kh = h0 / group;
     // partial records {m, l, pad, pad, o[hd]} (16-byte aligned o), in shared and global memory
@@ -1440,6 +1501,7 @@ __device__ __noinline__ void tk_attention(const TokenArgs& a, const AttnArgs& A,
     float* qs = U;           // [G][hd]
     float* ws = U + G * hd;  // [16 warps][G][hd + 4]
     const float* qsrc = A.q + (size_t)h0 * hd;
+    if (!tk_gate(a, p, sh, target)) return false;
     for (int i = tid; i < G * hd; i += MV_CONSUMERS) qs[i] = __ldcg(qsrc + i);
     consumer_sync();
     if (tid == 0) tk_stamp(a, p, 1);
@@ -1524,11 +1586,14 @@ __device__ __noinline__ void tk_attention(const TokenArgs& a, const AttnArgs& A,
         dst[4 + d] = O;
     }
     if (tid == 0) tk_stamp(a, p, 2);
+    return true;
 }
 
 // Final norm to the hidden state (src/model/llama.rs:181), CTA 0 only.
-__device__ __noinline__ void tk_hidden(const TokenArgs& a, const TokenPhase& P, float* red) {
-    if (blockIdx.x != 0) return;
+__device__ __noinline__ bool tk_hidden(const TokenArgs& a, const TokenPhase& P, int p, float* red, TkShared* sh,
+                                       unsigned long long target) {
+    if (!tk_gate(a, p, sh, target)) return false;
+    if (blockIdx.x != 0) return true;
     const int tid = threadIdx.x;
     float* x = a.x;
     if (a.tp > 1 && P.xsum) {  // the last down-proj's partial sums, as in tk_stage
@@ -1554,6 +1619,7 @@ __device__ __noinline__ void tk_hidden(const TokenArgs& a, const TokenPhase& P, 
     const float scale = 1.0f / sqrtf(tot / (float)a.E + a.eps);
     for (int k = tid; k < a.E; k += MV_CONSUMERS)
         a.hidden[k] = __fmul_rn(__fmul_rn(__ldcg(x + k), scale), a.out_norm[k]);
+    return true;
 }
 
 __device__ __forceinline__ void tk_tile_src(const Seg& sg, int lt, int c, int gcb, const uint8_t*& pa,
@@ -1567,19 +1633,13 @@ __device__ __forceinline__ void tk_tile_src(const Seg& sg, int lt, int c, int gc
 }
 
 __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__ TokenArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
     __shared__ TkShared sh;
     const int tid = threadIdx.x;
     const uint32_t nst = (uint32_t)a.nst;
-    uint8_t* ring = smem;
-    uint64_t* full = (uint64_t*)(smem + (size_t)nst * TK_STAGE);
-    uint64_t* empty = full + nst;
-    uint64_t* tdone = empty + nst;  // [2]
-    uint64_t* tfree = tdone + 2;    // [2]
-    float* U = (float*)(smem + (size_t)nst * TK_STAGE + TK_BAR_BYTES);
-    float* part = U + a.union_bytes / 4;     // [2][16][16]
-    float* res = part + 2 * MV_CWARPS * 16;  // 16
-    float* red = res + 16;                   // 32
+    const TkSmem S = tk_smem(a);
+    uint8_t* ring = S.ring;
+    uint64_t *full = S.full, *empty = S.empty, *tdone = S.tdone, *tfree = S.tfree;
+    float *U = S.U, *part = S.part, *res = S.res, *red = S.red;
 
     const unsigned long long epoch = *a.epoch;
     const uint32_t pos = a.step->pos;
@@ -1749,63 +1809,53 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
         const TokenPhase& P = sph[p & 1];
         consumer_sync();  // the descriptor is in place; every warp is done with phase p - 1
         tk_prefetch(a, P, U);
-        if (p > 0) {
-            if (tid == 0) {
-                const bool xr = a.ph[p - 1].xrank != 0;
-                // the acquire load orders the phase's reads; consumer_sync passes it on
-                if (!(xr ? tk_rank_wait(a, p - 1, target) : grid_wait_one(&a.bars[p - 1], target, false)))
-                    tk_fail(a, &sh, 4u);
-                *(volatile int*)&sh.started = p;
-                sh.stop = *(volatile int*)&sh.err;
-                tk_stamp(a, p, 0);
-            }
-            consumer_sync();
-            if (sh.stop) break;  // every consumer warp reads the same snapshot
-        } else if (tid == 0) {
-            tk_stamp(a, 0, 0);
-        }
+        // Each phase's code waits for the previous phase's barrier itself (tk_gate),
+        // after its prologue. A stop is seen by every consumer warp at the same gate.
         if (P.kind == PH_MATVEC) {
-            bool ok = true;
+            int r = TK_DONE;
             switch (P.type) {
                 case GT_Q4_0:
-                    ok = tk_matvec<GT_Q4_0>(a, P, p, tok, pos, &sh, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
+                    r = tk_matvec<GT_Q4_0>(a, P, p, tok, pos, target, &sh, slot, par, ntile);
                     break;
                 case GT_Q8_0:
-                    ok = tk_matvec<GT_Q8_0>(a, P, p, tok, pos, &sh, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
+                    r = tk_matvec<GT_Q8_0>(a, P, p, tok, pos, target, &sh, slot, par, ntile);
                     break;
                 case GT_Q6_K:
-                    ok = tk_matvec<GT_Q6_K>(a, P, p, tok, pos, &sh, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
+                    r = tk_matvec<GT_Q6_K>(a, P, p, tok, pos, target, &sh, slot, par, ntile);
                     break;
                 default:
-                    ok = tk_matvec<GT_F32>(a, P, p, tok, pos, &sh, ring, full, empty, tdone, tfree, U, part, red, slot, par, ntile);
+                    r = tk_matvec<GT_F32>(a, P, p, tok, pos, target, &sh, slot, par, ntile);
                     break;
             }
-            if (!ok) {
+            if (r == TK_STOPPED) break;
+            if (r == TK_FAILED) {
                 // no early exit: the other consumer warps meet this one at the next
-                // phase's consumer_sync, see the error there and leave together
+                // phase's gate, see the error there and leave together
                 if ((tid & 31) == 0) tk_fail(a, &sh, 4u);
                 continue;
             }
         } else if (P.kind == PH_ATTN) {
+            bool go = true;
 #if TK_ATT_PER_HEAD
-            tk_attention<1>(a, P.at, p, pos, U);  // one query head per item
+            go = tk_attention<1>(a, P.at, p, pos, U, &sh, target);  // one query head per item
 #else
             switch (P.at.n_head / P.at.n_kv) {
-                case 1: tk_attention<1>(a, P.at, p, pos, U); break;
-                case 2: tk_attention<2>(a, P.at, p, pos, U); break;
-                case 3: tk_attention<3>(a, P.at, p, pos, U); break;
-                case 4: tk_attention<4>(a, P.at, p, pos, U); break;
-                case 8: tk_attention<8>(a, P.at, p, pos, U); break;
-                default: break;  // excluded on the host (fused_check)
+                case 1: go = tk_attention<1>(a, P.at, p, pos, U, &sh, target); break;
+                case 2: go = tk_attention<2>(a, P.at, p, pos, U, &sh, target); break;
+                case 3: go = tk_attention<3>(a, P.at, p, pos, U, &sh, target); break;
+                case 4: go = tk_attention<4>(a, P.at, p, pos, U, &sh, target); break;
+                case 8: go = tk_attention<8>(a, P.at, p, pos, U, &sh, target); break;
+                default: go = tk_gate(a, p, &sh, target); break;  // excluded on the host (fused_check)
             }
 #endif
+            if (!go) break;
             consumer_sync();  // every warp's partial stores precede thread 0's release
             if (tid == 0 && p + 1 < a.nph) {
                 red_release_add_u64(&a.bars[p], 1ull);
                 tk_stamp(a, p, 3);
             }
         } else {
-            tk_hidden(a, P, red);
+            if (!tk_hidden(a, P, p, red, &sh, target)) break;
             consumer_sync();
             if (tid == 0 && a.tp > 1) tk_arrive(a, p, P.xrank != 0);
         }
