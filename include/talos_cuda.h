@@ -143,6 +143,18 @@ talos_status talos_ctx_stream(talos_ctx* ctx, void** stream_out);
 talos_status talos_cap_context(talos_ctx* ctx, size_t max_ctx);
 
 /*
+ * KV cache element type: TALOS_KV_F32 (the default; the reference's KvCache
+ * holds f32, src/kv_cache.rs:9-10) or TALOS_KV_F16, opt-in: K (after RoPE) and
+ * V are rounded to f16 (nearest, ties to even) when appended and widened to f32
+ * when read, which halves the cache's memory and its traffic per token at the
+ * price of parity with the reference. Setting it reallocates and empties the
+ * cache. No reference counterpart (the reference has no KV type choice).
+ */
+enum { TALOS_KV_F32 = 0, TALOS_KV_F16 = 1 };
+talos_status talos_ctx_set_kv_dtype(talos_ctx* ctx, int dtype);
+talos_status talos_ctx_kv_dtype(talos_ctx* ctx, int* dtype_out);
+
+/*
  * Start a fresh sequence. Model::reset (src/model/llama.rs:236-238). The
  * device KV cache is indexed by position, so this only forgets the cached
  * length; positions are overwritten as they are decoded.

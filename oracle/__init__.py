@@ -96,6 +96,7 @@ def lib() -> C.CDLL:
         "oracle_model_config": (C.c_int, [vp, C.POINTER(Config)]),
         "oracle_model_cap_context": (None, [vp, sz]),
         "oracle_model_reset": (None, [vp]),
+        "oracle_model_set_kv_f16": (None, [C.c_void_p, C.c_int]),
         "oracle_forward": (C.c_int, [vp, C.c_uint32, sz, vp]),
         "oracle_forward_hidden": (C.c_int, [vp, C.c_uint32, sz, vp]),
     }
@@ -355,6 +356,11 @@ class Model:
 
     def reset(self):
         lib().oracle_model_reset(self.h)
+
+    def set_kv_f16(self, on: bool = True):
+        """The CUDA path's opt-in f16 KV cache (not in the reference): K/V are
+        rounded to f16 when appended. Empties the cache."""
+        lib().oracle_model_set_kv_f16(self.h, int(bool(on)))
 
     def cap_context(self, n: int):
         lib().oracle_model_cap_context(self.h, int(n))

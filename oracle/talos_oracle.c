@@ -908,6 +908,7 @@ struct oracle_model {
     float** vc;
     size_t* klen; /* rows appended per layer */
     size_t* kcap;
+    int kv_f16;   /* opt-in f16 cache of the CUDA path: rows rounded to f16 when appended */
 };
 
 /* config.rs:40-67 */
@@ -1066,9 +1067,26 @@ static void kv_append(oracle_model* m, size_t l, const float* k, const float* v,
         m->kc[l] = (float*)realloc(m->kc[l], sizeof(float) * m->kcap[l] * row);
         m->vc[l] = (float*)realloc(m->vc[l], sizeof(float) * m->kcap[l] * row);
     }
-    memcpy(m->kc[l] + m->klen[l] * row, k, sizeof(float) * row);
-    memcpy(m->vc[l] + m->klen[l] * row, v, sizeof(float) * row);
+    float* kd = m->kc[l] + m->klen[l] * row;
+    float* vd = m->vc[l] + m->klen[l] * row;
+    if (m->kv_f16) {
+        /* the values an f16 cache holds, widened back (round to nearest, ties to even) */
+        for (size_t i = 0; i < row; ++i) {
+            kd[i] = oracle_f16_to_f32(oracle_f32_to_f16(k[i]));
+            vd[i] = oracle_f16_to_f32(oracle_f32_to_f16(v[i]));
+        }
+    } else {
+        memcpy(kd, k, sizeof(float) * row);
+        memcpy(vd, v, sizeof(float) * row);
+    }
     m->klen[l]++;
+}
+
+/* Not in the reference: the CUDA path's opt-in f16 KV cache, for its parity tests.
+ * Empties the cache. */
+void oracle_model_set_kv_f16(oracle_model* m, int on) {
+    m->kv_f16 = on != 0;
+    oracle_model_reset(m);
 }
 
 /* llama.rs:96-183 */

@@ -100,6 +100,8 @@ void oracle_model_free(oracle_model* m);
 int oracle_model_config(const oracle_model* m, oracle_config* out);
 void oracle_model_cap_context(oracle_model* m, size_t max_ctx);
 void oracle_model_reset(oracle_model* m);
+/* The CUDA path's opt-in f16 KV cache (not in the reference): K/V rounded to f16 when appended. */
+void oracle_model_set_kv_f16(oracle_model* m, int on);
 int oracle_forward(oracle_model* m, uint32_t token, size_t pos, float* logits);
 int oracle_forward_hidden(oracle_model* m, uint32_t token, size_t pos, float* hidden);
 

@@ -12,6 +12,7 @@ from .build import CUDA_LIB
 
 OK, INVALID_ARG, OOM, CUDA, NCCL, TIMEOUT, OOB, STATE, UNSUPPORTED = range(9)
 STEP_AUTO, STEP_FUSED, STEP_LAYERED = range(3)
+KV_F32, KV_F16 = range(2)
 STATUS_NAMES = ["OK", "INVALID_ARG", "OOM", "CUDA", "NCCL", "TIMEOUT", "OOB", "STATE", "UNSUPPORTED"]
 
 
@@ -41,6 +42,8 @@ SIGNATURES = {
     "talos_weight_upload": (_i, [_vp, C.c_char_p, _vp, _sz, _i, _sz, _sz]),
     "talos_ctx_set_step_kernel": (_i, [_vp, _i]),
     "talos_ctx_step_kernel": (_i, [_vp, C.POINTER(_i)]),
+    "talos_ctx_set_kv_dtype": (_i, [_vp, _i]),
+    "talos_ctx_kv_dtype": (_i, [_vp, C.POINTER(_i)]),
     "talos_ctx_device_bytes": (_i, [_vp, C.POINTER(_sz)]),
     "talos_ctx_stream": (_i, [_vp, C.POINTER(_vp)]),
     "talos_cap_context": (_i, [_vp, _sz]),

@@ -128,8 +128,19 @@ __global__ void __launch_bounds__(AT_THREADS) k_attention(const __grid_constant_
             const int t = base + r;
             if (t >= lo && t < hi) {
                 const size_t off = (size_t)t * a.kv_dim + (size_t)kvh * hd + 4 * c4;
-                cp_async16(Ks + r * st + 4 * c4, a.kc + off);
-                cp_async16(Vs + r * st + 4 * c4, a.vc + off);
+                if (a.kv_f16) {  // widen on the way into shared memory
+                    const uint2 kr = __ldcg((const uint2*)((const __half*)a.kc + off));
+                    const uint2 vr = __ldcg((const uint2*)((const __half*)a.vc + off));
+                    const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&kr.x));
+                    const float2 k1 = __half22float2(*reinterpret_cast<const __half2*>(&kr.y));
+                    const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&vr.x));
+                    const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&vr.y));
+                    *(float4*)(Ks + r * st + 4 * c4) = make_float4(k0.x, k0.y, k1.x, k1.y);
+                    *(float4*)(Vs + r * st + 4 * c4) = make_float4(v0.x, v0.y, v1.x, v1.y);
+                } else {
+                    cp_async16(Ks + r * st + 4 * c4, (const float*)a.kc + off);
+                    cp_async16(Vs + r * st + 4 * c4, (const float*)a.vc + off);
+                }
             }
         }
     };

@@ -48,8 +48,9 @@ struct MatvecArgs {
     float eps;
     int epi;
     StepParams* step;
-    float* kcache;     // EPI_QKV: this layer's K/V cache, [ctx][kv_dim]
-    float* vcache;
+    void* kcache;      // EPI_QKV: this layer's K/V cache, [ctx][kv_dim] f32 (or f16)
+    void* vcache;
+    int kv_f16;        // the cache holds f16 (round to nearest even) instead of f32
     int kv_dim;
     int hd;
     const float2* rope_cs;  // [ctx][hd/2] (cos, sin)
@@ -76,8 +77,9 @@ cudaError_t launch_matvec_noalloc(const PackedW& w, const float* x, float* y, in
 
 struct AttnArgs {
     const float* q;     // [n_head * hd], RoPE applied
-    const float* kc;    // [ctx][kv_dim] this layer
-    const float* vc;
+    const void* kc;     // [ctx][kv_dim] this layer, f32 (or f16 when kv_f16)
+    const void* vc;
+    int kv_f16;
     float* out;         // [n_head * hd]
     StepParams* step;
     int n_head, n_kv, hd, kv_dim;

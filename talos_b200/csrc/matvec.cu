@@ -626,7 +626,13 @@ __device__ __forceinline__ void apply_epilogue(const MatvecArgs& a, const Seg& s
             if (sg.role == 2) {  // v -> cache row pos (src/kv_cache.rs:21-26)
                 if (lane < 16) {
                     const int row = 16 * lt + lane;
-                    if (row < sg.out_rows) a.vcache[(size_t)pos * a.kv_dim + row] = res[lane];
+                    if (row < sg.out_rows) {
+                        const size_t i = (size_t)pos * a.kv_dim + row;
+                        if (a.kv_f16)
+                            ((__half*)a.vcache)[i] = __float2half_rn(res[lane]);
+                        else
+                            ((float*)a.vcache)[i] = res[lane];
+                    }
                 }
             } else if (lane < 8) {  // RoPE on pairs (2i, 2i+1) (src/math/ops.rs:48-61)
                 const int r0 = 16 * lt + 2 * lane;
@@ -635,9 +641,13 @@ __device__ __forceinline__ void apply_epilogue(const MatvecArgs& a, const Seg& s
                     const float x0 = res[2 * lane], x1 = res[2 * lane + 1];
                     const float o0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
                     const float o1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
-                    float* dst = sg.role == 0 ? sg.out + r0 : a.kcache + (size_t)pos * a.kv_dim + r0;
-                    dst[0] = o0;
-                    dst[1] = o1;
+                    if (sg.role == 1 && a.kv_f16) {
+                        *(__half2*)((__half*)a.kcache + (size_t)pos * a.kv_dim + r0) = __floats2half2_rn(o0, o1);
+                    } else {
+                        float* dst = sg.role == 0 ? sg.out + r0 : (float*)a.kcache + (size_t)pos * a.kv_dim + r0;
+                        dst[0] = o0;
+                        dst[1] = o1;
+                    }
                 }
             }
         } else {
@@ -1484,8 +1494,111 @@ __device__ __noinline__ int tk_matvec(const TokenArgs& a, const TokenPhase& P, i
 // Instantiated per query-head group size G, so the unrolled loops hold exactly
 // the heads a model has (the kernel's code must stay small enough for the
 // instruction cache: every phase of every layer runs through it).
-constexpr int TK_ATT_UNROLL = 2;
-template <int G>
+#ifndef TK_ATT_UNROLL
+#define TK_ATT_UNROLL 4  // positions per warp and round
+#endif
+// The f16-cache round loop of tk_attention: LPR = hd/8 lanes hold one
+// position's row (8 halves, one 16-byte load each), so one load instruction of
+// the warp covers R = 32/LPR positions; a round is TK_ATT_UNROLL such loads for
+// K and V. Each lane keeps the V sum of its own row group's positions; the
+// running max and sum are warp-wide (maxima and sums cross the row groups by
+// shuffles), and the groups' V sums are added at the end. Writes the warp's
+// (m, l, o) record to ws like the f32 loop.
+template <int G, int LPR>
+__device__ __forceinline__ void tk_att_f16(const AttnArgs& A, const float* qs, float* ws, int p0, int p1, int kh,
+                                           float (&m)[G], float (&l)[G]) {
+    constexpr int R = 32 / LPR, RU = TK_ATT_UNROLL, hd = 8 * LPR;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gi = lane / LPR, d0 = 8 * (lane % LPR), hs = hd + 4;
+    float oh[G][8];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) oh[g][e] = 0.f;
+    const size_t hoff = (size_t)kh * hd + d0;
+    for (int t0 = p0 + warp; t0 < p1; t0 += MV_CWARPS * R * RU) {
+        uint4 kr[RU], vr[RU];
+#pragma unroll
+        for (int u = 0; u < RU; ++u) {
+            const int t = t0 + (u * R + gi) * MV_CWARPS;
+            kr[u] = make_uint4(0u, 0u, 0u, 0u);
+            vr[u] = kr[u];
+            if (t < p1) {
+                const size_t i = (size_t)t * A.kv_dim + hoff;
+                kr[u] = __ldcg((const uint4*)((const __half*)A.kc + i));
+                vr[u] = __ldcg((const uint4*)((const __half*)A.vc + i));
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float4 qa = *(const float4*)(qs + g * hd + d0), qb = *(const float4*)(qs + g * hd + d0 + 4);
+            const float q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+            float sc[RU];
+#pragma unroll
+            for (int u = 0; u < RU; ++u) {
+                const __half2* h = reinterpret_cast<const __half2*>(&kr[u]);
+                float d = 0.f;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __half22float2(h[e]);
+                    d = fmaf(q[2 * e], f.x, fmaf(q[2 * e + 1], f.y, d));
+                }
+                sc[u] = d;
+            }
+#pragma unroll
+            for (int off = LPR / 2; off > 0; off >>= 1)
+#pragma unroll
+                for (int u = 0; u < RU; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], off);
+            float mx = -INFINITY;
+#pragma unroll
+            for (int u = 0; u < RU; ++u) {
+                sc[u] = t0 + (u * R + gi) * MV_CWARPS < p1 ? sc[u] * A.scale : -INFINITY;
+                mx = fmaxf(mx, sc[u]);
+            }
+#pragma unroll
+            for (int off = LPR; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            mx = fmaxf(mx, m[g]);  // finite: position t0 is in range
+            const float cr = expf(m[g] - mx);
+            float ps = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) oh[g][e] *= cr;
+#pragma unroll
+            for (int u = 0; u < RU; ++u) {
+                const float pe = expf(sc[u] - mx);
+                ps += pe;
+                const __half2* h = reinterpret_cast<const __half2*>(&vr[u]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __half22float2(h[e]);
+                    oh[g][2 * e] = fmaf(pe, f.x, oh[g][2 * e]);
+                    oh[g][2 * e + 1] = fmaf(pe, f.y, oh[g][2 * e + 1]);
+                }
+            }
+#pragma unroll
+            for (int off = LPR; off < 32; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+            l[g] = fmaf(l[g], cr, ps);
+            m[g] = mx;
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+#pragma unroll
+            for (int off = LPR; off < 32; off <<= 1) oh[g][e] += __shfl_xor_sync(0xffffffffu, oh[g][e], off);
+        float* w = ws + (warp * G + g) * hs;
+        if (lane == 0) {
+            w[0] = m[g];
+            w[1] = l[g];
+        }
+        if (gi == 0) {
+            *(float4*)(w + 4 + d0) = make_float4(oh[g][0], oh[g][1], oh[g][2], oh[g][3]);
+            *(float4*)(w + 8 + d0) = make_float4(oh[g][4], oh[g][5], oh[g][6], oh[g][7]);
+        }
+    }
+}
+
+template <int G, bool KV16>
 __device__ __noinline__ bool tk_attention(const TokenArgs& a, const AttnArgs& A, int p, uint32_t pos, float* U,
                                           TkShared* sh, unsigned long long target) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1514,6 +1627,14 @@ __device__ __noinline__ bool tk_attention(const TokenArgs& a, const AttnArgs& A,
         l[g] = 0.f;
         o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
     }
+    if constexpr (KV16) {
+        if (hd == 128)
+            tk_att_f16<G, 16>(A, qs, ws, p0, p1, kh, m, l);
+        else if (hd == 64)
+            tk_att_f16<G, 8>(A, qs, ws, p0, p1, kh, m, l);
+        else
+            tk_att_f16<G, 4>(A, qs, ws, p0, p1, kh, m, l);  // hd == 32 (checked on the host)
+    } else {
     const size_t hoff = (size_t)kh * hd + 4 * lane;
     for (int t0 = p0 + warp; t0 < p1; t0 += MV_CWARPS * TK_ATT_UNROLL) {
         float4 kv[TK_ATT_UNROLL], vv[TK_ATT_UNROLL];
@@ -1523,32 +1644,48 @@ __device__ __noinline__ bool tk_attention(const TokenArgs& a, const AttnArgs& A,
             kv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
             vv[u] = kv[u];
             if (act && t < p1) {
-                kv[u] = __ldcg((const float4*)(A.kc + (size_t)t * A.kv_dim + hoff));
-                vv[u] = __ldcg((const float4*)(A.vc + (size_t)t * A.kv_dim + hoff));
+                const size_t i = (size_t)t * A.kv_dim + hoff;
+                kv[u] = __ldcg((const float4*)((const float*)A.kc + i));
+                vv[u] = __ldcg((const float4*)((const float*)A.vc + i));
             }
         }
+        // the round's positions at once: independent dot products and one
+        // rescale of the running state per round (t0 < p1, so the maximum is finite)
 #pragma unroll
-        for (int u = 0; u < TK_ATT_UNROLL; ++u) {
-            if (t0 + u * MV_CWARPS >= p1) break;  // warp-uniform
+        for (int g = 0; g < G; ++g) {
+            float sc[TK_ATT_UNROLL];
+            float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (act) q4 = *(const float4*)(qs + g * hd + 4 * lane);
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                {
-                    float d = 0.f;
-                    if (act) {
-                        const float4 q4 = *(const float4*)(qs + g * hd + 4 * lane);
-                        d = fmaf(q4.x, kv[u].x, fmaf(q4.y, kv[u].y, fmaf(q4.z, kv[u].z, q4.w * kv[u].w)));
-                    }
-                    const float sc = warp_sum(d) * A.scale;
-                    const float mn = fmaxf(m[g], sc);
-                    const float cr = expf(m[g] - mn), pe = expf(sc - mn);
-                    l[g] = fmaf(l[g], cr, pe);
-                    o[g][0] = fmaf(o[g][0], cr, pe * vv[u].x);
-                    o[g][1] = fmaf(o[g][1], cr, pe * vv[u].y);
-                    o[g][2] = fmaf(o[g][2], cr, pe * vv[u].z);
-                    o[g][3] = fmaf(o[g][3], cr, pe * vv[u].w);
-                    m[g] = mn;
-                }
+            for (int u = 0; u < TK_ATT_UNROLL; ++u)
+                sc[u] = act ? fmaf(q4.x, kv[u].x, fmaf(q4.y, kv[u].y, fmaf(q4.z, kv[u].z, q4.w * kv[u].w))) : 0.f;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+                for (int u = 0; u < TK_ATT_UNROLL; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], off);
+            float mx = m[g];
+#pragma unroll
+            for (int u = 0; u < TK_ATT_UNROLL; ++u) {
+                sc[u] = t0 + u * MV_CWARPS < p1 ? sc[u] * A.scale : -INFINITY;
+                mx = fmaxf(mx, sc[u]);
             }
+            const float cr = expf(m[g] - mx);
+            float ls = l[g] * cr, o0 = o[g][0] * cr, o1 = o[g][1] * cr, o2 = o[g][2] * cr, o3 = o[g][3] * cr;
+#pragma unroll
+            for (int u = 0; u < TK_ATT_UNROLL; ++u) {
+                const float pe = expf(sc[u] - mx);
+                ls += pe;
+                o0 = fmaf(pe, vv[u].x, o0);
+                o1 = fmaf(pe, vv[u].y, o1);
+                o2 = fmaf(pe, vv[u].z, o2);
+                o3 = fmaf(pe, vv[u].w, o3);
+            }
+            m[g] = mx;
+            l[g] = ls;
+            o[g][0] = o0;
+            o[g][1] = o1;
+            o[g][2] = o2;
+            o[g][3] = o3;
         }
     }
 #pragma unroll
@@ -1561,6 +1698,7 @@ __device__ __noinline__ bool tk_attention(const TokenArgs& a, const AttnArgs& A,
             }
             if (act) *(float4*)(w + 4 + 4 * lane) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
         }
+    }
     }
     consumer_sync();
     // merge the 16 warps: one thread per (head, dim)
@@ -1587,6 +1725,14 @@ __device__ __noinline__ bool tk_attention(const TokenArgs& a, const AttnArgs& A,
     }
     if (tid == 0) tk_stamp(a, p, 2);
     return true;
+}
+
+// the cache's element type picks the instantiation (the loads stay branch-free)
+template <int G>
+__device__ __forceinline__ bool tk_attention_kv(const TokenArgs& a, const AttnArgs& A, int p, uint32_t pos, float* U,
+                                                TkShared* sh, unsigned long long target) {
+    return A.kv_f16 ? tk_attention<G, true>(a, A, p, pos, U, sh, target)
+                    : tk_attention<G, false>(a, A, p, pos, U, sh, target);
 }
 
 // Final norm to the hidden state (src/model/llama.rs:181), CTA 0 only.
@@ -1837,14 +1983,14 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
         } else if (P.kind == PH_ATTN) {
             bool go = true;
 #if TK_ATT_PER_HEAD
-            go = tk_attention<1>(a, P.at, p, pos, U, &sh, target);  // one query head per item
+            go = tk_attention_kv<1>(a, P.at, p, pos, U, &sh, target);  // one query head per item
 #else
             switch (P.at.n_head / P.at.n_kv) {
-                case 1: go = tk_attention<1>(a, P.at, p, pos, U, &sh, target); break;
-                case 2: go = tk_attention<2>(a, P.at, p, pos, U, &sh, target); break;
-                case 3: go = tk_attention<3>(a, P.at, p, pos, U, &sh, target); break;
-                case 4: go = tk_attention<4>(a, P.at, p, pos, U, &sh, target); break;
-                case 8: go = tk_attention<8>(a, P.at, p, pos, U, &sh, target); break;
+                case 1: go = tk_attention_kv<1>(a, P.at, p, pos, U, &sh, target); break;
+                case 2: go = tk_attention_kv<2>(a, P.at, p, pos, U, &sh, target); break;
+                case 3: go = tk_attention_kv<3>(a, P.at, p, pos, U, &sh, target); break;
+                case 4: go = tk_attention_kv<4>(a, P.at, p, pos, U, &sh, target); break;
+                case 8: go = tk_attention_kv<8>(a, P.at, p, pos, U, &sh, target); break;
                 default: go = tk_gate(a, p, &sh, target); break;  // excluded on the host (fused_check)
             }
 #endif

@@ -403,8 +403,9 @@ struct talos_ctx {
     StepParams* step = nullptr;
     uint32_t* gen = nullptr;
     // KV + RoPE table
-    float* kcache = nullptr;
-    float* vcache = nullptr;
+    void* kcache = nullptr;  // [n_layer][kv_ctx][kv_l], f32 or (kv_f16) f16
+    void* vcache = nullptr;
+    int kv_f16 = 0;
     float2* rope_cs = nullptr;
     size_t kv_bytes = 0;
 
@@ -500,13 +501,15 @@ static bool expected_shape(const talos_ctx* c, const std::string& name, size_t* 
     return true;
 }
 
+static size_t kv_elem(const talos_ctx* c) { return c->kv_f16 ? sizeof(__half) : sizeof(float); }
+
 static talos_status alloc_kv(talos_ctx* c) {
     if (c->kcache) cudaFree(c->kcache);
     if (c->vcache) cudaFree(c->vcache);
     if (c->rope_cs) cudaFree(c->rope_cs);
     c->kcache = c->vcache = nullptr;
     c->rope_cs = nullptr;
-    size_t per = (size_t)c->cfg.n_layer * c->kv_ctx * c->kv_l * sizeof(float);
+    size_t per = (size_t)c->cfg.n_layer * c->kv_ctx * c->kv_l * kv_elem(c);
     CK(cudaMalloc(&c->kcache, per ? per : 4));
     CK(cudaMalloc(&c->vcache, per ? per : 4));
     CK(cudaMemsetAsync(c->kcache, 0, per ? per : 4, c->stream));
@@ -875,6 +878,24 @@ extern "C" talos_status talos_cap_context(talos_ctx* c, size_t max_ctx) {
     return alloc_kv(c);
 }
 
+extern "C" talos_status talos_ctx_set_kv_dtype(talos_ctx* c, int dtype) {
+    if (!c) return set_err(TALOS_ERR_INVALID_ARG, "NULL ctx");
+    if (dtype != TALOS_KV_F32 && dtype != TALOS_KV_F16)
+        return set_err(TALOS_ERR_INVALID_ARG, "KV dtype %d", dtype);
+    CK(cudaSetDevice(c->device));
+    CK(cudaStreamSynchronize(c->stream));
+    if ((dtype == TALOS_KV_F16) == (c->kv_f16 != 0)) return TALOS_OK;
+    c->kv_f16 = dtype == TALOS_KV_F16;
+    c->weights_dirty = true;  // the per-token kernel's checks run again at the next step
+    return alloc_kv(c);
+}
+
+extern "C" talos_status talos_ctx_kv_dtype(talos_ctx* c, int* out) {
+    if (!c || !out) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    *out = c->kv_f16 ? TALOS_KV_F16 : TALOS_KV_F32;
+    return TALOS_OK;
+}
+
 extern "C" talos_status talos_kv_reset(talos_ctx* c) {
     if (!c) return set_err(TALOS_ERR_INVALID_ARG, "NULL ctx");
     return TALOS_OK;
@@ -955,8 +976,8 @@ static talos_status enqueue_step(talos_ctx* c, GraphMode mode) {
     const size_t kv_layer = c->kv_ctx * (size_t)c->kv_dim;
     for (uint32_t l = 0; l < cfg.n_layer; ++l) {
         const LayerW& L = c->layers[l];
-        float* kc = c->kcache + l * kv_layer;
-        float* vc = c->vcache + l * kv_layer;
+        void* kc = (uint8_t*)c->kcache + l * kv_layer * kv_elem(c);
+        void* vc = (uint8_t*)c->vcache + l * kv_layer * kv_elem(c);
         // --- rmsnorm + q/k/v + RoPE + KV append (llama.rs:118-130)
         {
             const DevTensor* qkv[3] = {L.q, L.k, L.v};
@@ -973,6 +994,7 @@ static talos_status enqueue_step(talos_ctx* c, GraphMode mode) {
                 a.step = c->step;
                 a.kcache = kc;
                 a.vcache = vc;
+                a.kv_f16 = c->kv_f16;
                 a.kv_dim = c->kv_dim;
                 a.hd = c->hd;
                 a.rope_cs = c->rope_cs;
@@ -991,6 +1013,7 @@ static talos_status enqueue_step(talos_ctx* c, GraphMode mode) {
             a.q = c->q;
             a.kc = kc;
             a.vc = vc;
+            a.kv_f16 = c->kv_f16;
             a.out = c->att;
             a.step = c->step;
             a.n_head = (int)cfg.n_head;
@@ -1085,8 +1108,8 @@ static void build_phases(talos_ctx* c, GraphMode mode, std::vector<TokenPhase>& 
     ph.clear();
     for (uint32_t l = 0; l < cfg.n_layer; ++l) {
         const LayerW& L = c->layers[l];
-        float* kc = c->kcache + l * kv_layer;
-        float* vc = c->vcache + l * kv_layer;
+        void* kc = (uint8_t*)c->kcache + l * kv_layer * kv_elem(c);
+        void* vc = (uint8_t*)c->vcache + l * kv_layer * kv_elem(c);
         TokenPhase p{};
         // rmsnorm + q/k/v + RoPE + KV append (llama.rs:118-130); layer 0 reads the embedding row
         p.kind = PH_MATVEC;
@@ -1102,6 +1125,7 @@ static void build_phases(talos_ctx* c, GraphMode mode, std::vector<TokenPhase>& 
         p.mv.step = c->step;
         p.mv.kcache = kc;
         p.mv.vcache = vc;
+        p.mv.kv_f16 = c->kv_f16;
         p.mv.kv_dim = c->kv_l;
         p.mv.hd = c->hd;
         p.mv.rope_cs = c->rope_cs;
@@ -1116,6 +1140,7 @@ static void build_phases(talos_ctx* c, GraphMode mode, std::vector<TokenPhase>& 
         p.at.q = c->q;
         p.at.kc = kc;
         p.at.vc = vc;
+        p.at.kv_f16 = c->kv_f16;
         p.at.out = c->att;
         p.at.step = c->step;
         p.at.n_head = c->nh_l;
@@ -1199,6 +1224,11 @@ static void fused_check(talos_ctx* c) {
     char buf[256];
     if (c->hd > 128) {
         snprintf(buf, sizeof buf, "head_dim %d above 128", c->hd);
+        c->fused_why = buf;
+        return;
+    }
+    if (c->kv_f16 && c->hd != 32 && c->hd != 64 && c->hd != 128) {
+        snprintf(buf, sizeof buf, "f16 KV cache with head_dim %d (32, 64 or 128)", c->hd);
         c->fused_why = buf;
         return;
     }

@@ -158,6 +158,17 @@ class Context:
         _lib.check(_lib.load().talos_ctx_step_kernel(self.h, C.byref(k)))
         return "fused" if k.value == _lib.STEP_FUSED else "layered"
 
+    def set_kv_dtype(self, dtype: str):
+        """"f32" (the reference's cache) or "f16" (opt-in: half the cache bytes;
+        K/V rounded to f16 when appended). Empties the cache."""
+        k = {"f32": _lib.KV_F32, "f16": _lib.KV_F16}[dtype]
+        _lib.check(_lib.load().talos_ctx_set_kv_dtype(self.h, k))
+
+    def kv_dtype(self) -> str:
+        k = C.c_int()
+        _lib.check(_lib.load().talos_ctx_kv_dtype(self.h, C.byref(k)))
+        return "f16" if k.value == _lib.KV_F16 else "f32"
+
     def device_bytes(self) -> int:
         n = C.c_size_t()
         _lib.check(_lib.load().talos_ctx_device_bytes(self.h, C.byref(n)))
@@ -242,7 +253,8 @@ class Model:
     """``Model`` (src/model/llama.rs:20-238) with the CUDA backend."""
 
     def __init__(self, gguf: GgufFile, device: int = 0, tp_size: int = 1, tp_rank: int = 0,
-                 nccl_id: bytes | None = None, max_ctx: int | None = None, step_kernel: str = "auto"):
+                 nccl_id: bytes | None = None, max_ctx: int | None = None, step_kernel: str = "auto",
+                 kv_dtype: str = "f32"):
         cfg = Config.from_gguf(gguf)
         if cfg.n_head_kv == 0 or cfg.n_head % cfg.n_head_kv != 0:
             raise GgufError(f"head_count {cfg.n_head} must be a positive multiple of head_count_kv "
@@ -254,6 +266,8 @@ class Model:
         self.ctx = Context(cfg, device, tp_size, tp_rank, nccl_id)
         if step_kernel != "auto":
             self.ctx.set_step_kernel(step_kernel)
+        if kv_dtype != "f32":
+            self.ctx.set_kv_dtype(kv_dtype)
         for name, (rows, cols) in weight_shapes(cfg).items():
             if rows == 1:
                 data = gguf.tensor_f32(name)
