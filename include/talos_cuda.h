@@ -200,6 +200,26 @@ talos_status talos_prefill(talos_ctx* ctx, const uint32_t* tokens, size_t n, siz
                            float* last_logits);
 
 /*
+ * Batched decode: up to TALOS_MAX_BATCH independent sequences per step, each
+ * with its own KV cache slot and position; every weight is read once per step
+ * for all of them. talos_ctx_set_batch reserves `max_seqs` cache slots (0
+ * frees them; reserving empties them) for the context's model, which must have
+ * Q4_0 / Q8_0 / Q6_K matrices and head_dim <= 128 (TALOS_ERR_UNSUPPORTED
+ * otherwise, and under tensor parallelism). talos_forward_batch runs one step
+ * for sequences 0 .. n-1 (n <= max_seqs): sequence i feeds tokens[i] at
+ * position pos[i] into slot i and gets its vocab_size logits at
+ * logits_out + i * vocab_size (host). Each sequence computes what
+ * Model::forward (src/model/llama.rs:85-183) computes for it alone; this is the
+ * batched decode of the multi-prompt workload, which the reference runs as
+ * separate token-by-token loops (src/main.rs:88-113). No reference counterpart
+ * as an entry point.
+ */
+#define TALOS_MAX_BATCH 4
+talos_status talos_ctx_set_batch(talos_ctx* ctx, int max_seqs);
+talos_status talos_forward_batch(talos_ctx* ctx, const uint32_t* tokens, const size_t* pos, int n,
+                                 float* logits_out);
+
+/*
  * Teacher-forced perplexity of tokens[0..n) (n >= 2): eval::perplexity
  * (src/eval.rs:35-52). The tokens are scored in chunks of the context length,
  * each from an empty KV cache; at each position the negative log-likelihood of

@@ -43,6 +43,8 @@ SIGNATURES = {
     "talos_ctx_set_step_kernel": (_i, [_vp, _i]),
     "talos_ctx_step_kernel": (_i, [_vp, C.POINTER(_i)]),
     "talos_ctx_set_kv_dtype": (_i, [_vp, _i]),
+    "talos_ctx_set_batch": (_i, [_vp, _i]),
+    "talos_forward_batch": (_i, [_vp, C.POINTER(C.c_uint32), C.POINTER(_sz), _i, C.POINTER(C.c_float)]),
     "talos_ctx_kv_dtype": (_i, [_vp, C.POINTER(_i)]),
     "talos_ctx_device_bytes": (_i, [_vp, C.POINTER(_sz)]),
     "talos_ctx_stream": (_i, [_vp, C.POINTER(_vp)]),

@@ -43,6 +43,11 @@ struct StepParams {
     unsigned long long argmax_key;  // packed (total-order key << 32) | index
 };
 
+__device__ __forceinline__ float silu_ref(float g) {
+    // src/math/ops.rs:28-30: x / (1 + exp(-x))
+    return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -385,4 +385,174 @@ cudaError_t launch_greedy_advance(StepParams* step, uint32_t* gen, int cap, cuda
     return launch_ex(k_greedy_advance, dim3(1), dim3(1), 0, s, pdl, 1, step, gen, cap);
 }
 
+
+// ----------------------------------------------------------------------------
+// Batched decode: the small per-sequence steps around the batched matvec
+// ----------------------------------------------------------------------------
+
+__global__ void k_embed_b(const uint8_t* raw, int type, int cols, int vocab, const BatchParams* bp, float* x,
+                          int ldx) {
+    const int s = blockIdx.y;
+    if (s >= bp->n) return;
+    uint32_t tok = bp->token[s];
+    if (tok >= (uint32_t)vocab) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr((unsigned*)&bp->error, 1u);
+        tok = 0;
+    }
+    const int be = type == GT_F32 ? 1 : (type == GT_Q6_K ? 256 : 32);
+    const int bb = type == GT_F32 ? 4 : (type == GT_Q6_K ? 210 : (type == GT_Q8_0 ? 34 : 18));
+    const uint8_t* row = raw + (size_t)tok * (cols / be) * bb;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < cols) x[(size_t)s * ldx + i] = dequant_elem(type, row, i);
+}
+
+cudaError_t launch_embed_b(const uint8_t* raw, int type, int cols, int vocab, const BatchParams* bp, float* x,
+                           int ldx, cudaStream_t s) {
+    k_embed_b<<<dim3((cols + 255) / 256, MB_SEQ), 256, 0, s>>>(raw, type, cols, vocab, bp, x, ldx);
+    return cudaGetLastError();
+}
+
+// RoPE on interleaved pairs (2i, 2i+1) with the step's (cos, sin) table row of
+// the sequence's position; the rotated k and the v row go to the sequence's cache.
+__global__ void k_rope_kv_b(float* q, int ldq, int q_rows, const float* k, const float* v, int ldkv, int kv_dim,
+                            int hd, const float2* cs, float* kc, float* vc, size_t seq_stride, const BatchParams* bp) {
+    const int s = blockIdx.x;
+    if (s >= bp->n) return;
+    const uint32_t pos = bp->pos[s];
+    const float2* row = cs + (size_t)pos * (hd >> 1);
+    auto rot = [&](float x0, float x1, int r0, float* o) {
+        const float2 c = row[(r0 % hd) >> 1];
+        o[0] = __fsub_rn(__fmul_rn(x0, c.x), __fmul_rn(x1, c.y));
+        o[1] = __fadd_rn(__fmul_rn(x0, c.y), __fmul_rn(x1, c.x));
+    };
+    float* qs = q + (size_t)s * ldq;
+    for (int i = threadIdx.x; i < q_rows / 2; i += blockDim.x) {
+        float o[2];
+        rot(qs[2 * i], qs[2 * i + 1], 2 * i, o);
+        qs[2 * i] = o[0];
+        qs[2 * i + 1] = o[1];
+    }
+    const float* ks = k + (size_t)s * ldkv;
+    float* kd = kc + (size_t)s * seq_stride + (size_t)pos * kv_dim;
+    for (int i = threadIdx.x; i < kv_dim / 2; i += blockDim.x) rot(ks[2 * i], ks[2 * i + 1], 2 * i, kd + 2 * i);
+    const float* vs = v + (size_t)s * ldkv;
+    float* vd = vc + (size_t)s * seq_stride + (size_t)pos * kv_dim;
+    for (int i = threadIdx.x; i < kv_dim; i += blockDim.x) vd[i] = vs[i];
+}
+
+cudaError_t launch_rope_kv_b(float* q, int ldq, int q_rows, const float* k, const float* v, int ldkv, int kv_dim,
+                             int hd, const float2* rope_cs, float* kc, float* vc, size_t seq_stride,
+                             const BatchParams* bp, cudaStream_t s) {
+    k_rope_kv_b<<<MB_SEQ, 256, 0, s>>>(q, ldq, q_rows, k, v, ldkv, kv_dim, hd, rope_cs, kc, vc, seq_stride, bp);
+    return cudaGetLastError();
+}
+
+// One CTA per (query head, sequence), 8 warps: warp w takes positions w, w+8, ...
+// in rounds of 4 (all K/V loads of a round in flight), keeps an online softmax
+// (max m, sum l, unnormalised o; lane = 4 dims), and the warps merge in shared
+// memory: out = o / l (src/math/ops.rs:15-25 applied to the merged sums).
+constexpr int ATB_WARPS = 8, ATB_ROUND = 4;
+__global__ void __launch_bounds__(ATB_WARPS * 32) k_attention_b(const float* q, int ldq, const float* kc,
+                                                                const float* vc, size_t seq_stride, int kv_dim,
+                                                                int n_head, int n_kv, int hd, float* out, int ldo,
+                                                                const BatchParams* bp) {
+    const int h = blockIdx.x, s = blockIdx.y;
+    if (s >= bp->n) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int seq = (int)bp->pos[s] + 1, kh = h / (n_head / n_kv), hs = hd + 4;
+    const float scale = 1.0f / sqrtf((float)hd);
+    extern __shared__ float wsm[];  // [8 warps][hd + 4]
+    const bool act = 4 * lane < hd;
+    float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (act) q4 = *(const float4*)(q + (size_t)s * ldq + (size_t)h * hd + 4 * lane);
+    const float* K0 = kc + (size_t)s * seq_stride + (size_t)kh * hd + 4 * lane;
+    const float* V0 = vc + (size_t)s * seq_stride + (size_t)kh * hd + 4 * lane;
+    float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+    for (int t0 = warp; t0 < seq; t0 += ATB_WARPS * ATB_ROUND) {
+        float4 kv[ATB_ROUND], vv[ATB_ROUND];
+#pragma unroll
+        for (int u = 0; u < ATB_ROUND; ++u) {
+            const int t = t0 + u * ATB_WARPS;
+            kv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            vv[u] = kv[u];
+            if (act && t < seq) {
+                kv[u] = *(const float4*)(K0 + (size_t)t * kv_dim);
+                vv[u] = *(const float4*)(V0 + (size_t)t * kv_dim);
+            }
+        }
+        float sc[ATB_ROUND];
+#pragma unroll
+        for (int u = 0; u < ATB_ROUND; ++u)
+            sc[u] = fmaf(q4.x, kv[u].x, fmaf(q4.y, kv[u].y, fmaf(q4.z, kv[u].z, q4.w * kv[u].w)));
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+            for (int u = 0; u < ATB_ROUND; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], off);
+        float mx = m;
+#pragma unroll
+        for (int u = 0; u < ATB_ROUND; ++u) {
+            sc[u] = t0 + u * ATB_WARPS < seq ? sc[u] * scale : -INFINITY;
+            mx = fmaxf(mx, sc[u]);
+        }
+        const float cr = expf(m - mx);
+        l *= cr;
+        o0 *= cr, o1 *= cr, o2 *= cr, o3 *= cr;
+#pragma unroll
+        for (int u = 0; u < ATB_ROUND; ++u) {
+            const float pe = expf(sc[u] - mx);
+            l += pe;
+            o0 = fmaf(pe, vv[u].x, o0);
+            o1 = fmaf(pe, vv[u].y, o1);
+            o2 = fmaf(pe, vv[u].z, o2);
+            o3 = fmaf(pe, vv[u].w, o3);
+        }
+        m = mx;
+    }
+    float* w = wsm + warp * hs;
+    if (lane == 0) {
+        w[0] = m;
+        w[1] = l;
+    }
+    if (act) *(float4*)(w + 4 + 4 * lane) = make_float4(o0, o1, o2, o3);
+    __syncthreads();
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float M = -INFINITY;
+        for (int ww = 0; ww < ATB_WARPS; ++ww) M = fmaxf(M, wsm[ww * hs]);
+        float L = 0.f, O = 0.f;
+        for (int ww = 0; ww < ATB_WARPS; ++ww) {
+            const float* r = wsm + ww * hs;
+            const float e = r[0] == -INFINITY ? 0.f : expf(r[0] - M);
+            L = fmaf(r[1], e, L);
+            O = fmaf(r[4 + d], e, O);
+        }
+        out[(size_t)s * ldo + (size_t)h * hd + d] = O / L;
+    }
+}
+
+cudaError_t launch_attention_b(const float* q, int ldq, const float* kc, const float* vc, size_t seq_stride,
+                               int kv_dim, int n_head, int n_kv, int hd, float* out, int ldo, const BatchParams* bp,
+                               cudaStream_t s) {
+    if (hd > 128 || hd % 4) return cudaErrorInvalidValue;
+    const size_t sm = (size_t)ATB_WARPS * (hd + 4) * 4;
+    k_attention_b<<<dim3(n_head, MB_SEQ), ATB_WARPS * 32, sm, s>>>(q, ldq, kc, vc, seq_stride, kv_dim, n_head, n_kv,
+                                                                   hd, out, ldo, bp);
+    return cudaGetLastError();
+}
+
+__global__ void k_swiglu_b(const float* g, const float* u, float* h, int ld, int n_ff, const BatchParams* bp) {
+    const int s = blockIdx.y;
+    if (s >= bp->n) return;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n_ff) {
+        const size_t o = (size_t)s * ld + i;
+        h[o] = __fmul_rn(silu_ref(g[o]), u[o]);
+    }
+}
+
+cudaError_t launch_swiglu_b(const float* g, const float* u, float* h, int ld, int n_ff, const BatchParams* bp,
+                            cudaStream_t s) {
+    k_swiglu_b<<<dim3((n_ff + 255) / 256, MB_SEQ), 256, 0, s>>>(g, u, h, ld, n_ff, bp);
+    return cudaGetLastError();
+}
+
 }  // namespace talos

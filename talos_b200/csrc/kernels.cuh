@@ -73,6 +73,63 @@ size_t noalloc_smem_bytes(int type, int K);
 cudaError_t launch_matvec_noalloc(const PackedW& w, const float* x, float* y, int nslice, float* part,
                                   unsigned* cnt, cudaStream_t s);
 
+// ---------------------------------------------------------------- batched decode
+//
+// Up to MB_SEQ sequences per weight pass: the MMA's 8 B columns hold four
+// sequences' f16 hi / lo activation parts. Activations are formatted once per
+// matvec input (k_xfmt_b) into per-block B fragments and block sums, which the
+// batched matvec streams through its ring together with the weights.
+
+constexpr int MB_SEQ = 4;
+
+struct BatchParams {
+    int n;                     // active sequences (1 .. MB_SEQ)
+    uint32_t token[MB_SEQ];
+    uint32_t pos[MB_SEQ];
+    uint32_t error;            // device-side error bits (2: a bounded wait expired)
+};
+
+// Formatted activation of [MB_SEQ][K] inputs for weights of `type`: fragments
+// (KP/32 blocks x 32 lanes x 16 bytes) and block sums ([KP/32] or, Q6_K,
+// [KP/16] x MB_SEQ floats). KP = K rounded up to the type's chunk.
+size_t xfmt_frag_bytes(int type, int K);
+size_t xfmt_sum_bytes(int type, int K);
+// x: [n][ldx] f32; norm_w: optional RMSNorm weight (eps); sequences n .. MB_SEQ-1 get zeros.
+cudaError_t launch_xfmt_b(int type, const float* x, int ldx, int K, const float* norm_w, float eps,
+                          const BatchParams* bp, void* frag, float* sums, cudaStream_t s);
+
+enum { EPI_B_STORE = 0, EPI_B_ADD = 1 };
+struct BatchMvArgs {
+    PackedW w;
+    int ntiles;             // 16-row tiles
+    int K;
+    const void* frag;       // formatted activation (launch_xfmt_b for w.type)
+    const float* sums;
+    float* y;               // [MB_SEQ][ldy]: y[s][row] = (or +=) row value of sequence s
+    int ldy;
+    int epi;
+    const BatchParams* bp;  // active sequence count, error bits
+};
+cudaError_t launch_matvec_b(const BatchMvArgs& a, int max_ctas, cudaStream_t s);
+cudaError_t matvec_b_configure();
+
+// x[s] = dequant(token_embd row of token[s]) (src/model/weights.rs:57-62)
+cudaError_t launch_embed_b(const uint8_t* embd_raw, int type, int cols, int vocab, const BatchParams* bp, float* x,
+                           int ldx, cudaStream_t s);
+// q / k RoPE at each sequence's position (src/math/ops.rs:48-61); k and v appended
+// to that sequence's cache row (src/kv_cache.rs:21-26). kc/vc: sequence s's layer
+// cache at kc + s * seq_stride, rows of kv_dim floats.
+cudaError_t launch_rope_kv_b(float* q, int ldq, int q_rows, const float* k, const float* v, int ldkv, int kv_dim,
+                             int hd, const float2* rope_cs, float* kc, float* vc, size_t seq_stride,
+                             const BatchParams* bp, cudaStream_t s);
+// GQA attention per (head, sequence) over positions 0 .. pos[s] (src/model/llama.rs:135-155)
+cudaError_t launch_attention_b(const float* q, int ldq, const float* kc, const float* vc, size_t seq_stride,
+                               int kv_dim, int n_head, int n_kv, int hd, float* out, int ldo, const BatchParams* bp,
+                               cudaStream_t s);
+// h[s][i] = silu(g[s][i]) * u[s][i] (src/math/ops.rs:28-37)
+cudaError_t launch_swiglu_b(const float* g, const float* u, float* h, int ld, int n_ff, const BatchParams* bp,
+                            cudaStream_t s);
+
 // ---------------------------------------------------------------- attention
 
 struct AttnArgs {

@@ -508,10 +508,6 @@ struct Zero<GT_F32> {
     static constexpr float z = 0.f;
 };
 
-__device__ __forceinline__ float silu_ref(float g) {
-    // src/math/ops.rs:28-30: x / (1 + exp(-x))
-    return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-}
 
 __device__ __forceinline__ void split_pair(float v0, float v1, uint32_t& hi, uint32_t& lo) {
     const half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
@@ -2229,6 +2225,379 @@ cudaError_t launch_token(const TokenArgs& a, int grid, cudaStream_t s, bool coop
     cfg.attrs = attr;
     cfg.numAttrs = cooperative ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, k_token, a);
+}
+
+
+// ============================================================================
+// Batched decode (up to MB_SEQ sequences per weight pass)
+// ============================================================================
+//
+// The same weight fragments and MMAs as k_matvec, but the B operand's eight
+// columns are four sequences' (hi, lo) activation parts instead of one
+// sequence's: lane 8s + 4h + t of a block's fragment record holds sequence s,
+// part h (0 hi, 1 lo), k pair t. The MMA's D fragment then gives lane l the
+// row value of sequence l % 4, so the per-lane math of the single-sequence
+// consumers is unchanged; only where the B fragment and the block sums come
+// from differs. The activation cannot be staged whole (4 x K floats), so each
+// ring stage carries, after the tile's two group-chunks, the chunk of
+// formatted activation they meet (fragments + block sums, one bulk copy each).
+
+template <int TYPE>
+struct FmtB {
+    static constexpr int NSUM = TYPE == GT_Q6_K ? Fmt<TYPE>::CK / 16 : Fmt<TYPE>::CK / 32;  // sums per chunk, per seq
+    static constexpr int XFB = Fmt<TYPE>::CK / 32 * 512;  // fragment bytes per chunk
+    static constexpr int XSB = NSUM * MB_SEQ * 4;         // sum bytes per chunk
+    static constexpr int WB = 2 * Fmt<TYPE>::GCB;
+    static constexpr int STAGE = WB + XFB + XSB;
+    static constexpr int NST = 4;
+};
+
+static int ck_host(int type) { return fmt_ck(type); }
+
+size_t xfmt_frag_bytes(int type, int K) {
+    const int ck = ck_host(type);
+    if (!ck || type == GT_F32) return 0;
+    const size_t kp = (size_t)ceil_div_h(K, ck) * ck;
+    return kp / 32 * 512;
+}
+size_t xfmt_sum_bytes(int type, int K) {
+    const int ck = ck_host(type);
+    if (!ck || type == GT_F32) return 0;
+    const size_t kp = (size_t)ceil_div_h(K, ck) * ck;
+    return (type == GT_Q6_K ? kp / 16 : kp / 32) * MB_SEQ * 4;
+}
+
+// One CTA per (8 blocks, sequence): RMSNorm scale of the sequence (summed over
+// all of K by every CTA of that sequence, in one fixed order), then lane l of
+// warp w formats element 32 j + l of block j = 8 bx + w, like k_matvec's staging.
+template <int TYPE>
+__global__ void __launch_bounds__(256) k_xfmt_b(const float* x, int ldx, int K, int KP, const float* norm_w, float eps,
+                                                const BatchParams* bp, half* frag, float* sums) {
+    const int s = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const bool live = s < bp->n;
+    const float* xs = x + (size_t)s * ldx;
+    __shared__ float red[8];
+    float scale = 1.f;
+    if (norm_w && live) {  // src/math/ops.rs:5-12
+        float ss = 0.f;
+        for (int k = tid; k < K; k += 256) {
+            const float v = xs[k];
+            ss = fmaf(v, v, ss);
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) tot += red[w];
+        scale = 1.0f / sqrtf(tot / (float)K + eps);
+    }
+    const int j = blockIdx.x * 8 + warp;
+    if (32 * j >= KP) return;
+    const int e = 32 * j + lane;
+    float v = 0.f;
+    if (live && e < K) {
+        v = xs[e];
+        if (norm_w) v = __fmul_rn(__fmul_rn(v, scale), norm_w[e]);
+    }
+    const int s16 = lane >> 4, r16 = lane & 15;
+    const int m = 2 * s16 + (r16 >> 3), t = (r16 & 7) >> 1, hp = r16 & 1;
+    const float vv = (TYPE == GT_Q4_0 && (r16 >> 3)) ? v * 0.0625f : v;
+    const half hi = __float2half_rn(vv);
+    const half lo = __float2half_rn(vv - __half2float(hi));
+    frag[((j * 32 + 8 * s + t) * 4 + m) * 2 + hp] = hi;
+    frag[((j * 32 + 8 * s + 4 + t) * 4 + m) * 2 + hp] = lo;
+    float sm = v;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+    if (TYPE == GT_Q6_K) {
+        if (r16 == 0) sums[(2 * j + s16) * MB_SEQ + s] = sm;
+    } else {
+        sm += __shfl_xor_sync(0xffffffffu, sm, 16);
+        if (lane == 0) sums[j * MB_SEQ + s] = sm;
+    }
+}
+
+cudaError_t launch_xfmt_b(int type, const float* x, int ldx, int K, const float* norm_w, float eps,
+                          const BatchParams* bp, void* frag, float* sums, cudaStream_t s) {
+    const int ck = ck_host(type);
+    if (!ck || type == GT_F32) return cudaErrorInvalidValue;
+    const int KP = ceil_div_h(K, ck) * ck;
+    const dim3 grid(ceil_div_h(KP / 32, 8), MB_SEQ);
+    switch (type) {
+        case GT_Q4_0: k_xfmt_b<GT_Q4_0><<<grid, 256, 0, s>>>(x, ldx, K, KP, norm_w, eps, bp, (half*)frag, sums); break;
+        case GT_Q8_0: k_xfmt_b<GT_Q8_0><<<grid, 256, 0, s>>>(x, ldx, K, KP, norm_w, eps, bp, (half*)frag, sums); break;
+        case GT_Q6_K: k_xfmt_b<GT_Q6_K><<<grid, 256, 0, s>>>(x, ldx, K, KP, norm_w, eps, bp, (half*)frag, sums); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+// Batched consumers: one stage (group-chunks A, B; activation chunk xf / xs) ->
+// per-lane partial sums of row (lane / 4) (+8 for B) of sequence lane % 4.
+__device__ __forceinline__ void consume_q4_0_b(const uint8_t* sA, const uint8_t* sB, const uint4* xf, const float* xs,
+                                               Acc& acc) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sq = lane & 3;
+    constexpr int QPC = Fmt<GT_Q4_0>::CK / 128;
+    const uint4 wa = *(const uint4*)(sA + (warp * 32 + lane) * 16);
+    const uint4 wb = *(const uint4*)(sB + (warp * 32 + lane) * 16);
+    const uint2 ca = *(const uint2*)(sA + QPC * 512 + (warp * 8 + (lane >> 2)) * 8);
+    const uint2 cb = *(const uint2*)(sB + QPC * 512 + (warp * 8 + (lane >> 2)) * 8);
+    const float2 a01 = __half22float2(*reinterpret_cast<const half2*>(&ca.x));
+    const float2 a23 = __half22float2(*reinterpret_cast<const half2*>(&ca.y));
+    const float2 b01 = __half22float2(*reinterpret_cast<const half2*>(&cb.x));
+    const float2 b23 = __half22float2(*reinterpret_cast<const half2*>(&cb.y));
+    const float dA[4] = {a01.x, a01.y, a23.x, a23.y};
+    const float dB[4] = {b01.x, b01.y, b23.x, b23.y};
+    const uint32_t xa[4] = {wa.x, wa.y, wa.z, wa.w};
+    const uint32_t xb[4] = {wb.x, wb.y, wb.z, wb.w};
+    const int blk0 = warp * 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint4 bx = xf[(blk0 + j) * 32 + lane];
+        const float S = xs[(blk0 + j) * MB_SEQ + sq];
+        float d[4];
+        mma_z(d, xa[j] & 0x000F000Fu, xb[j] & 0x000F000Fu, xa[j] & 0x00F000F0u, xb[j] & 0x00F000F0u, bx.x, bx.y);
+        const uint32_t ya = xa[j] >> 8, yb = xb[j] >> 8;
+        mma_acc(d, ya & 0x000F000Fu, yb & 0x000F000Fu, ya & 0x00F000F0u, yb & 0x00F000F0u, bx.z, bx.w);
+        acc.pA = fmaf(dA[j], d[0], fmaf(dA[j], d[1], acc.pA));
+        acc.pB = fmaf(dB[j], d[2], fmaf(dB[j], d[3], acc.pB));
+        acc.qA = fmaf(dA[j], S, acc.qA);
+        acc.qB = fmaf(dB[j], S, acc.qB);
+    }
+}
+
+__device__ __forceinline__ void consume_q8_0_b(const uint8_t* sA, const uint8_t* sB, const uint4* xf, const float* xs,
+                                               Acc& acc) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sq = lane & 3;
+    const int quad = warp >> 1, half_ = warp & 1;
+    const uint4 wa = *(const uint4*)(sA + (quad * 32 + lane) * 32 + half_ * 16);
+    const uint4 wb = *(const uint4*)(sB + (quad * 32 + lane) * 32 + half_ * 16);
+    const uint32_t ca = *(const uint32_t*)(sA + 8 * 1024 + (quad * 8 + (lane >> 2)) * 8 + half_ * 4);
+    const uint32_t cb = *(const uint32_t*)(sB + 8 * 1024 + (quad * 8 + (lane >> 2)) * 8 + half_ * 4);
+    const float2 fa = __half22float2(*reinterpret_cast<const half2*>(&ca));
+    const float2 fb = __half22float2(*reinterpret_cast<const half2*>(&cb));
+    const float dA[2] = {fa.x, fa.y};
+    const float dB[2] = {fb.x, fb.y};
+    const uint32_t A[4] = {wa.x ^ 0x80808080u, wa.y ^ 0x80808080u, wa.z ^ 0x80808080u, wa.w ^ 0x80808080u};
+    const uint32_t B[4] = {wb.x ^ 0x80808080u, wb.y ^ 0x80808080u, wb.z ^ 0x80808080u, wb.w ^ 0x80808080u};
+    const int blk0 = warp * 2;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const uint4 bx = xf[(blk0 + j) * 32 + lane];
+        const float S = xs[(blk0 + j) * MB_SEQ + sq];
+        float d[4];
+        mma_z(d, bytes_sub(A[2 * j], 0x4140), bytes_sub(B[2 * j], 0x4140), bytes_sub(A[2 * j], 0x4342),
+              bytes_sub(B[2 * j], 0x4342), bx.x, bx.y);
+        mma_acc(d, bytes_sub(A[2 * j + 1], 0x4140), bytes_sub(B[2 * j + 1], 0x4140), bytes_sub(A[2 * j + 1], 0x4342),
+                bytes_sub(B[2 * j + 1], 0x4342), bx.z, bx.w);
+        acc.pA = fmaf(dA[j], d[0], fmaf(dA[j], d[1], acc.pA));
+        acc.pB = fmaf(dB[j], d[2], fmaf(dB[j], d[3], acc.pB));
+        acc.qA = fmaf(dA[j], S, acc.qA);
+        acc.qB = fmaf(dB[j], S, acc.qB);
+    }
+}
+
+__device__ __forceinline__ void consume_q6_k_b(const uint8_t* sA, const uint8_t* sB, const uint4* xf, const float* xs,
+                                               Acc& acc) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sq = lane & 3;
+    const int row = lane >> 2;
+    const uint32_t scA = *(const uint32_t*)(sA + 16 * 512 + row * 64 + warp * 4);
+    const uint32_t scB = *(const uint32_t*)(sB + 16 * 512 + row * 64 + warp * 4);
+    const float dA = __half2float(*(const half*)(sA + 16 * 512 + 8 * 64 + (row * 4 + (warp >> 2)) * 2));
+    const float dB = __half2float(*(const half*)(sB + 16 * 512 + 8 * 64 + (row * 4 + (warp >> 2)) * 2));
+    const uint4 wa = *(const uint4*)(sA + (warp * 32 + lane) * 16);
+    const uint4 wb = *(const uint4*)(sB + (warp * 32 + lane) * 16);
+    const uint32_t A[4] = {wa.x, wa.y, wa.z, wa.w};
+    const uint32_t B[4] = {wb.x, wb.y, wb.z, wb.w};
+    const int step0 = warp * 4;
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+        const int blk = (step0 + 2 * p) / 2;
+        const uint4 bx = xf[blk * 32 + lane];
+        const float s0 = xs[(step0 + 2 * p) * MB_SEQ + sq], s1 = xs[(step0 + 2 * p + 1) * MB_SEQ + sq];
+        float d0[4], d1[4];
+        mma_z(d0, bytes_sub(A[2 * p], 0x4140), bytes_sub(B[2 * p], 0x4140), bytes_sub(A[2 * p], 0x4342),
+              bytes_sub(B[2 * p], 0x4342), bx.x, bx.y);
+        mma_z(d1, bytes_sub(A[2 * p + 1], 0x4140), bytes_sub(B[2 * p + 1], 0x4140), bytes_sub(A[2 * p + 1], 0x4342),
+              bytes_sub(B[2 * p + 1], 0x4342), bx.z, bx.w);
+        const float a0 = __fmul_rn(dA, (float)(int8_t)(scA >> (16 * p))),
+                    a1 = __fmul_rn(dA, (float)(int8_t)(scA >> (16 * p + 8)));
+        const float b0 = __fmul_rn(dB, (float)(int8_t)(scB >> (16 * p))),
+                    b1 = __fmul_rn(dB, (float)(int8_t)(scB >> (16 * p + 8)));
+        acc.pA = fmaf(a0, d0[0] + d0[1], acc.pA);
+        acc.pA = fmaf(a1, d1[0] + d1[1], acc.pA);
+        acc.qA = fmaf(a0, s0, fmaf(a1, s1, acc.qA));
+        acc.pB = fmaf(b0, d0[2] + d0[3], acc.pB);
+        acc.pB = fmaf(b1, d1[2] + d1[3], acc.pB);
+        acc.qB = fmaf(b0, s0, fmaf(b1, s1, acc.qB));
+    }
+}
+
+// Roles as k_matvec: producer warp (weights + activation chunk per stage), 16
+// consumer warps, epilogue warp (reduces a tile's 16 x 64 partials in warp
+// order and stores / adds the 16 rows x 4 sequences).
+template <int TYPE>
+__global__ void __launch_bounds__(MV_THREADS, 1) k_matvec_b(const __grid_constant__ BatchMvArgs a) {
+    using F = FmtB<TYPE>;
+    constexpr int NST = F::NST, GCB = Fmt<TYPE>::GCB, CK = Fmt<TYPE>::CK;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x;
+    const int nchunk = (a.K + CK - 1) / CK;
+    uint8_t* ring = smem;
+    uint64_t* full = (uint64_t*)(smem + NST * F::STAGE);
+    uint64_t* empty = full + NST;
+    uint64_t* tdone = empty + NST;  // [2]
+    uint64_t* tfree = tdone + 2;    // [2]
+    float* part = (float*)(tfree + 2);  // [2][16 warps][64]
+    __shared__ int s_err;
+    if (tid == 0) {
+        for (int i = 0; i < NST; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], MV_CWARPS);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tdone[i], MV_CWARPS);
+            mbar_init(&tfree[i], 1);
+        }
+        s_err = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    const int lane = tid & 31;
+
+    if (tid >= MV_CONSUMERS + 32) {
+        // ---------------- epilogue warp
+        const int n = a.bp->n;
+        int it = 0;
+        for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, ++it) {
+            const int b = it & 1;
+            if (!mbar_wait(&tdone[b], (uint32_t)(it >> 1) & 1)) {
+                s_err = 1;
+                atomicOr((unsigned*)&a.bp->error, 2u);
+                return;
+            }
+            const float* pb = part + b * MV_CWARPS * 64;
+            float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+            for (int w = 0; w < MV_CWARPS; ++w) {
+                v0 += pb[w * 64 + lane];
+                v1 += pb[w * 64 + 32 + lane];
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tfree[b]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int idx = lane + 32 * h, row = 16 * t + idx / 4, sq = idx % 4;
+                const float v = h ? v1 : v0;
+                if (sq < n && row < a.w.rows) {
+                    float* dst = a.y + (size_t)sq * a.ldy + row;
+                    *dst = a.epi == EPI_B_ADD ? __fadd_rn(*dst, v) : v;
+                }
+            }
+        }
+        return;
+    }
+    if (tid >= MV_CONSUMERS) {
+        // ---------------- producer warp
+        if (tid == MV_CONSUMERS) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < a.ntiles && ok; t += gridDim.x) {
+                const uint8_t* ga0 = (const uint8_t*)a.w.p0 + (size_t)(2 * t) * a.w.nk * GCB;
+                const uint8_t* gb0 = (const uint8_t*)a.w.p0 + (size_t)(2 * t + 1) * a.w.nk * GCB;
+                for (int c = 0; c < nchunk; ++c, ++it) {
+                    const int slot = it % NST;
+                    if (!mbar_wait(&empty[slot], ((it / NST) & 1) ^ 1) || *(volatile int*)&s_err) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* dst = ring + slot * F::STAGE;
+                    mbar_expect_tx(&full[slot], F::STAGE);
+                    bulk_g2s(dst, ga0 + (size_t)c * GCB, GCB, &full[slot]);
+                    bulk_g2s(dst + GCB, gb0 + (size_t)c * GCB, GCB, &full[slot]);
+                    bulk_g2s(dst + F::WB, (const uint8_t*)a.frag + (size_t)c * F::XFB, F::XFB, &full[slot]);
+                    bulk_g2s(dst + F::WB + F::XFB, (const uint8_t*)a.sums + (size_t)c * F::XSB, F::XSB, &full[slot]);
+                }
+            }
+            const uint32_t first = it > (uint32_t)NST ? it - NST : 0;
+            for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % NST], (j / NST) & 1);
+            if (!ok) {
+                s_err = 1;
+                atomicOr((unsigned*)&a.bp->error, 2u);
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers
+    const int warp = tid >> 5;
+    uint32_t it = 0;
+    int nt = 0;
+    for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, ++nt) {
+        Acc acc = {0.f, 0.f, 0.f, 0.f};
+        for (int c = 0; c < nchunk; ++c, ++it) {
+            const int slot = it % NST;
+            if (!mbar_wait(&full[slot], (it / NST) & 1)) {
+                s_err = 1;
+                atomicOr((unsigned*)&a.bp->error, 2u);
+                return;
+            }
+            const uint8_t* st = ring + slot * F::STAGE;
+            const uint4* xf = (const uint4*)(st + F::WB);
+            const float* xs = (const float*)(st + F::WB + F::XFB);
+            if (TYPE == GT_Q4_0)
+                consume_q4_0_b(st, st + GCB, xf, xs, acc);
+            else if (TYPE == GT_Q8_0)
+                consume_q8_0_b(st, st + GCB, xf, xs, acc);
+            else
+                consume_q6_k_b(st, st + GCB, xf, xs, acc);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        const int b = nt & 1;
+        if (!mbar_wait(&tfree[b], ((uint32_t)(nt >> 1) & 1u) ^ 1u)) {
+            s_err = 1;
+            atomicOr((unsigned*)&a.bp->error, 2u);
+            return;
+        }
+        float* pb = part + b * MV_CWARPS * 64 + warp * 64;
+        // row r (A: lane / 4, B: + 8) of sequence lane % 4 -> index 4 r + s
+        pb[(lane >> 2) * 4 + (lane & 3)] = fmaf(acc.pA, kTwo24, -Zero<TYPE>::z * acc.qA);
+        pb[((lane >> 2) + 8) * 4 + (lane & 3)] = fmaf(acc.pB, kTwo24, -Zero<TYPE>::z * acc.qB);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tdone[b]);
+    }
+}
+
+template <int TYPE>
+static size_t matvec_b_smem() {
+    using F = FmtB<TYPE>;
+    return (size_t)F::NST * F::STAGE + (2 * F::NST + 4) * 8 + 2 * MV_CWARPS * 64 * 4;
+}
+
+cudaError_t matvec_b_configure() {
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(k_matvec_b<GT_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)matvec_b_smem<GT_Q4_0>())))
+        return e;
+    if ((e = cudaFuncSetAttribute(k_matvec_b<GT_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)matvec_b_smem<GT_Q8_0>())))
+        return e;
+    return cudaFuncSetAttribute(k_matvec_b<GT_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)matvec_b_smem<GT_Q6_K>());
+}
+
+cudaError_t launch_matvec_b(const BatchMvArgs& a, int max_ctas, cudaStream_t s) {
+    if (a.ntiles <= 0) return cudaSuccess;
+    const int grid = a.ntiles < max_ctas ? a.ntiles : max_ctas;
+    switch (a.w.type) {
+        case GT_Q4_0: k_matvec_b<GT_Q4_0><<<grid, MV_THREADS, matvec_b_smem<GT_Q4_0>(), s>>>(a); break;
+        case GT_Q8_0: k_matvec_b<GT_Q8_0><<<grid, MV_THREADS, matvec_b_smem<GT_Q8_0>(), s>>>(a); break;
+        case GT_Q6_K: k_matvec_b<GT_Q6_K><<<grid, MV_THREADS, matvec_b_smem<GT_Q6_K>(), s>>>(a); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
 }
 
 }  // namespace talos

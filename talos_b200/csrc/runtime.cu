@@ -344,6 +344,7 @@ static talos_status device_setup(int device) {
         g_cfg_err = matvec_configure();
         if (g_cfg_err == cudaSuccess) g_cfg_err = attention_configure();
         if (g_cfg_err == cudaSuccess) g_cfg_err = token_configure();
+        if (g_cfg_err == cudaSuccess) g_cfg_err = matvec_b_configure();
     });
     if (g_cfg_err != cudaSuccess) return set_err(TALOS_ERR_CUDA, "matvec_configure: %s", cudaGetErrorString(g_cfg_err));
     if (device < 64 && g_sms[device] == 0) {
@@ -438,12 +439,31 @@ struct talos_ctx {
     std::vector<std::pair<cudaEvent_t, int>>* prof = nullptr;
     std::vector<LayerW> layers;
 
+    // batched decode (talos_ctx_set_batch): one allocation for the parameters,
+    // the [MB_SEQ][..] activations, the formatted-input scratch and the caches
+    int bmax = 0;
+    void* bmem = nullptr;
+    size_t bbytes = 0;
+    BatchParams* bp = nullptr;
+    BatchParams* h_bp = nullptr;  // pinned
+    float *bx = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr, *batt = nullptr;
+    float *bg = nullptr, *bu = nullptr, *bh = nullptr, *blog = nullptr, *bsums = nullptr;
+    void* bfrag = nullptr;
+    float *bkc = nullptr, *bvc = nullptr;  // [bmax][n_layer][kv_ctx][kv_dim]
+    size_t bseq_stride = 0;                // floats per sequence in bkc / bvc
+    float* h_blog = nullptr;               // pinned [MB_SEQ][V]
+    cudaGraphExec_t bgraph = nullptr;
+
     void drop_graphs() {
         for (auto& g : graph)
             if (g) {
                 cudaGraphExecDestroy(g);
                 g = nullptr;
             }
+        if (bgraph) {
+            cudaGraphExecDestroy(bgraph);
+            bgraph = nullptr;
+        }
         for (auto& p : d_phases)
             if (p) {
                 cudaFree(p);
@@ -751,6 +771,9 @@ extern "C" talos_status talos_ctx_destroy(talos_ctx* c) {
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     c->drop_graphs();
+    if (c->bmem) cudaFree(c->bmem);
+    if (c->h_bp) cudaFreeHost(c->h_bp);
+    if (c->h_blog) cudaFreeHost(c->h_blog);
     for (auto& kv : c->w) kv.second.release();
     c->weights.release();
     for (auto& kv : c->resident) kv.second.release();
@@ -856,7 +879,7 @@ extern "C" talos_status talos_weight_upload(talos_ctx* c, const char* name, cons
 
 extern "C" talos_status talos_ctx_device_bytes(talos_ctx* c, size_t* out) {
     if (!c || !out) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
-    size_t n = c->arena_bytes + c->kv_bytes + c->staging.cap + c->sync_bytes + c->weights.total;
+    size_t n = c->arena_bytes + c->kv_bytes + c->staging.cap + c->sync_bytes + c->weights.total + c->bbytes;
     for (auto& kv : c->resident) n += kv.second.bytes;
     *out = n;
     return TALOS_OK;
@@ -1576,6 +1599,196 @@ static talos_status profile_fused(talos_ctx* c, double* kernel_ms, uint32_t* lau
         if (kernel_ms) kernel_ms[k] += ms;
         if (launches) launches[k] += 1;
     }
+    return TALOS_OK;
+}
+
+// ------------------------------------------------------------------ batched decode
+//
+// Up to MB_SEQ independent sequences per step (the batched drivers of the
+// workload: several prompts decoded together). Each weight is read once per
+// step for all of them: the batched matvec puts four sequences in the MMA's B
+// columns. The step is the layered sequence of src/model/llama.rs:96-183 with
+// per-sequence positions and caches, captured once as a CUDA graph that reads
+// the sequence count, tokens and positions from device memory.
+
+static talos_status batch_free(talos_ctx* c) {
+    CK(cudaStreamSynchronize(c->stream));
+    if (c->bgraph) {
+        cudaGraphExecDestroy(c->bgraph);
+        c->bgraph = nullptr;
+    }
+    if (c->bmem) cudaFree(c->bmem);
+    c->bmem = nullptr;
+    c->bbytes = 0;
+    c->bmax = 0;
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_ctx_set_batch(talos_ctx* c, int max_seqs) {
+    if (!c) return set_err(TALOS_ERR_INVALID_ARG, "NULL ctx");
+    if (max_seqs < 0 || max_seqs > MB_SEQ)
+        return set_err(TALOS_ERR_INVALID_ARG, "batch of %d sequences (at most %d)", max_seqs, MB_SEQ);
+    if (c->tp > 1) return set_err(TALOS_ERR_UNSUPPORTED, "batched decode under tensor parallelism");
+    CK(cudaSetDevice(c->device));
+    TRY(batch_free(c));
+    if (max_seqs == 0) return TALOS_OK;
+    const size_t E = c->cfg.n_embd, F = c->cfg.n_ff, V = c->cfg.vocab_size, L = c->cfg.n_layer;
+    const size_t KPmax = ((std::max(E, F) + 2047) / 2048) * 2048;  // largest chunk-rounded input
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off += align256(bytes);
+        return o;
+    };
+    const size_t o_bp = take(sizeof(BatchParams));
+    const size_t o_x = take(MB_SEQ * E * 4), o_q = take(MB_SEQ * c->q_rows * 4), o_k = take(MB_SEQ * c->kv_dim * 4),
+                 o_v = take(MB_SEQ * c->kv_dim * 4), o_att = take(MB_SEQ * E * 4), o_g = take(MB_SEQ * F * 4),
+                 o_u = take(MB_SEQ * F * 4), o_h = take(MB_SEQ * F * 4), o_log = take(MB_SEQ * V * 4);
+    const size_t o_frag = take(KPmax / 32 * 512), o_sums = take(KPmax / 16 * MB_SEQ * 4);
+    const size_t seq_stride = L * c->kv_ctx * (size_t)c->kv_dim;
+    const size_t o_kc = take((size_t)max_seqs * seq_stride * 4), o_vc = take((size_t)max_seqs * seq_stride * 4);
+    void* mem = nullptr;
+    CK(cudaMalloc(&mem, off));
+    CK(cudaMemsetAsync(mem, 0, off, c->stream));
+    uint8_t* b = (uint8_t*)mem;
+    c->bmem = mem;
+    c->bbytes = off;
+    c->bp = (BatchParams*)(b + o_bp);
+    c->bx = (float*)(b + o_x), c->bq = (float*)(b + o_q), c->bk = (float*)(b + o_k), c->bv = (float*)(b + o_v);
+    c->batt = (float*)(b + o_att), c->bg = (float*)(b + o_g), c->bu = (float*)(b + o_u), c->bh = (float*)(b + o_h);
+    c->blog = (float*)(b + o_log), c->bfrag = b + o_frag, c->bsums = (float*)(b + o_sums);
+    c->bkc = (float*)(b + o_kc), c->bvc = (float*)(b + o_vc);
+    c->bseq_stride = seq_stride;
+    if (!c->h_bp) CK(cudaMallocHost(&c->h_bp, sizeof(BatchParams)));
+    if (!c->h_blog) CK(cudaMallocHost(&c->h_blog, MB_SEQ * V * 4));
+    c->bmax = max_seqs;
+    CK(cudaStreamSynchronize(c->stream));
+    return TALOS_OK;
+}
+
+// x formatted for weight w (skipped when the previous matvec read the same input
+// the same way), then y (+)= w x for every live sequence.
+struct BatchFmtCache {
+    const float* in = nullptr;
+    const float* norm = nullptr;
+    int type = -1;
+};
+
+static talos_status mv_b(talos_ctx* c, BatchFmtCache& fc, const DevTensor* w, const float* in, int K,
+                         const float* norm, float* y, int ldy, int epi) {
+    cudaError_t e = cudaSuccess;
+    if (fc.in != in || fc.norm != norm || fc.type != w->type) {
+        e = launch_xfmt_b(w->type, in, K, K, norm, c->cfg.rms_eps, c->bp, c->bfrag, c->bsums, c->stream);
+        if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched input format: %s", cudaGetErrorString(e));
+        fc = BatchFmtCache{in, norm, w->type};
+    }
+    BatchMvArgs a{};
+    a.w = w->w;
+    a.ntiles = w->w.rows_pad / 16;
+    a.K = (int)w->cols;
+    a.frag = c->bfrag;
+    a.sums = c->bsums;
+    a.y = y;
+    a.ldy = ldy;
+    a.epi = epi;
+    a.bp = c->bp;
+    e = launch_matvec_b(a, sm_count(c), c->stream);
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched matvec: %s", cudaGetErrorString(e));
+    return TALOS_OK;
+}
+
+static talos_status enqueue_batch(talos_ctx* c) {
+    const talos_cfg& cfg = c->cfg;
+    const int E = (int)cfg.n_embd, F = (int)cfg.n_ff, V = (int)cfg.vocab_size;
+    const DevTensor& embd = c->w["token_embd.weight"];
+    cudaError_t e = launch_embed_b((const uint8_t*)embd.mem, embd.type, E, V, c->bp, c->bx, E, c->stream);
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched embed: %s", cudaGetErrorString(e));
+    BatchFmtCache fc;
+    const size_t kv_layer = c->kv_ctx * (size_t)c->kv_dim;
+    for (uint32_t l = 0; l < cfg.n_layer; ++l) {
+        const LayerW& L = c->layers[l];
+        const float* an = (const float*)L.attn_norm->mem;
+        // rmsnorm + q/k/v + RoPE + KV append (llama.rs:118-130)
+        TRY(mv_b(c, fc, L.q, c->bx, E, an, c->bq, c->q_rows, EPI_B_STORE));
+        TRY(mv_b(c, fc, L.k, c->bx, E, an, c->bk, c->kv_dim, EPI_B_STORE));
+        TRY(mv_b(c, fc, L.v, c->bx, E, an, c->bv, c->kv_dim, EPI_B_STORE));
+        float* kc = c->bkc + l * kv_layer;
+        float* vc = c->bvc + l * kv_layer;
+        e = launch_rope_kv_b(c->bq, c->q_rows, c->q_rows, c->bk, c->bv, c->kv_dim, c->kv_dim, c->hd, c->rope_cs, kc, vc,
+                             c->bseq_stride, c->bp, c->stream);
+        if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched rope: %s", cudaGetErrorString(e));
+        // attention (llama.rs:135-155), o-proj + residual (:157-161)
+        e = launch_attention_b(c->bq, c->q_rows, kc, vc, c->bseq_stride, c->kv_dim, (int)cfg.n_head,
+                               (int)cfg.n_head_kv, c->hd, c->batt, E, c->bp, c->stream);
+        if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched attention: %s", cudaGetErrorString(e));
+        TRY(mv_b(c, fc, L.o, c->batt, E, nullptr, c->bx, E, EPI_B_ADD));
+        // rmsnorm + SwiGLU FFN + residual (:163-176)
+        const float* fn = (const float*)L.ffn_norm->mem;
+        TRY(mv_b(c, fc, L.gate, c->bx, E, fn, c->bg, F, EPI_B_STORE));
+        TRY(mv_b(c, fc, L.up, c->bx, E, fn, c->bu, F, EPI_B_STORE));
+        e = launch_swiglu_b(c->bg, c->bu, c->bh, F, F, c->bp, c->stream);
+        if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched swiglu: %s", cudaGetErrorString(e));
+        TRY(mv_b(c, fc, L.down, c->bh, F, nullptr, c->bx, E, EPI_B_ADD));
+        fc = BatchFmtCache{};  // bx changed in place
+    }
+    // final norm + logits (:89, :181)
+    const DevTensor& ow = c->w["output.weight"];
+    TRY(mv_b(c, fc, &ow, c->bx, E, (const float*)c->w["output_norm.weight"].mem, c->blog, V, EPI_B_STORE));
+    return TALOS_OK;
+}
+
+static talos_status batch_check(talos_ctx* c) {
+    auto ok = [](const DevTensor* t) { return t->type == GT_Q4_0 || t->type == GT_Q8_0 || t->type == GT_Q6_K; };
+    for (const LayerW& L : c->layers)
+        if (!ok(L.q) || !ok(L.k) || !ok(L.v) || !ok(L.o) || !ok(L.gate) || !ok(L.up) || !ok(L.down))
+            return set_err(TALOS_ERR_UNSUPPORTED, "batched decode needs Q4_0 / Q8_0 / Q6_K matrices");
+    if (!ok(&c->w["output.weight"]))
+        return set_err(TALOS_ERR_UNSUPPORTED, "batched decode needs a Q4_0 / Q8_0 / Q6_K output matrix");
+    if (c->hd > 128 || c->hd % 4) return set_err(TALOS_ERR_UNSUPPORTED, "batched attention needs head_dim <= 128");
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_forward_batch(talos_ctx* c, const uint32_t* tokens, const size_t* pos, int n,
+                                            float* logits_out) {
+    if (!c || !tokens || !pos || !logits_out) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    if (n < 1 || n > c->bmax)
+        return set_err(TALOS_ERR_INVALID_ARG, "%d sequences (the context holds %d; talos_ctx_set_batch)", n, c->bmax);
+    CK(cudaSetDevice(c->device));
+    for (int i = 0; i < n; ++i) TRY(check_tok_pos(c, tokens[i], pos[i]));
+    TRY(bind_if_dirty(c));
+    TRY(batch_check(c));
+    if (!c->bgraph) {
+        cudaGraph_t g = nullptr;
+        CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        talos_status st = enqueue_batch(c);
+        cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+        if (st != TALOS_OK) {
+            if (g) cudaGraphDestroy(g);
+            cudaGetLastError();
+            return st;
+        }
+        if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched graph capture: %s", cudaGetErrorString(e));
+        e = cudaGraphInstantiate(&c->bgraph, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched graph instantiate: %s", cudaGetErrorString(e));
+    }
+    CK(cudaStreamSynchronize(c->stream));  // the previous step no longer reads the parameters
+    BatchParams& hp = *c->h_bp;
+    memset(&hp, 0, sizeof hp);
+    hp.n = n;
+    for (int i = 0; i < n; ++i) {
+        hp.token[i] = tokens[i];
+        hp.pos[i] = (uint32_t)pos[i];
+    }
+    CK(cudaMemcpyAsync(c->bp, &hp, sizeof hp, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaGraphLaunch(c->bgraph, c->stream));
+    const size_t V = c->cfg.vocab_size;
+    CK(cudaMemcpyAsync(c->h_blog, c->blog, (size_t)n * V * 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaMemcpyAsync(&hp, c->bp, sizeof hp, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    if (hp.error & 2u) return set_err(TALOS_ERR_TIMEOUT, "batched step: a bounded wait expired");
+    if (hp.error) return set_err(TALOS_ERR_OOB, "batched step: device check failed (%u)", hp.error);
+    memcpy(logits_out, c->h_blog, (size_t)n * V * 4);
     return TALOS_OK;
 }
 

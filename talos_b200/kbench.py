@@ -18,6 +18,13 @@ profiling; its weights still exceed the L2):
 
 builds the Mistral-7B shape (seed 1, Q4_0, Q6_K output) with L layers, feeds a
 16-token prompt and times K device-side greedy steps.
+
+Batched decode on the same model:
+
+    python -m talos_b200.kbench --batch N [--layers L] [--steps K]
+
+times K talos_forward_batch steps of N sequences (each at its own position,
+host logits out, wall clock per call) and reports the aggregate tokens/s.
 """
 from __future__ import annotations
 
@@ -46,7 +53,10 @@ def main(argv=None):
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--step-kernel", default="auto", choices=["auto", "fused", "layered"])
+    ap.add_argument("--batch", type=int, default=0)
     a = ap.parse_args(argv)
+    if a.batch:
+        return batch_bench(a)
     if a.step:
         return step_bench(a)
 
@@ -118,6 +128,34 @@ def step_bench(a) -> int:
     wbytes = a.layers * (2 * E * E + 2 * shape.kv_dim * E + 3 * E * F) * 18 // 32 + V * E * 210 // 256
     out = {"kernel": "decode_step", "step_kernel": m.ctx.step_kernel(), "layers": a.layers,
            "ms_per_step": ms, "weight_bytes": wbytes, "gbs": wbytes / (ms * 1e-3) / 1e9, "model_gen_s": gen_s}
+    print(json.dumps(out), flush=True)
+    m.close()
+    return 0
+
+
+def batch_bench(a) -> int:
+    import dataclasses
+    import time
+
+    from talos_b200 import Model, build, gguf, synth
+
+    build.build()
+    shape = dataclasses.replace(synth.MISTRAL_7B, n_layer=a.layers, ctx=1024)
+    data = synth.llama_bytes(shape, 1, wtype=gguf.Q4_0, out_type=gguf.Q6_K)
+    m = Model.load_bytes(data, device=a.device, max_ctx=1024)
+    del data
+    m.ctx.set_batch(a.batch)
+    toks = synth.token_ids(3, a.batch, shape.vocab)
+    pos = [128 + 17 * i for i in range(a.batch)]
+    for i in range(3):
+        m.ctx.forward_batch(toks, [p + i for p in pos])
+    t0 = time.perf_counter()
+    for i in range(a.steps):
+        lg = m.ctx.forward_batch(toks, [p + 3 + i for p in pos])
+        toks = [int(np.argmax(r)) for r in lg]
+    dt = time.perf_counter() - t0
+    out = {"kernel": "decode_batch", "batch": a.batch, "layers": a.layers, "steps": a.steps,
+           "ms_per_step": dt / a.steps * 1e3, "tok_s": a.batch * a.steps / dt}
     print(json.dumps(out), flush=True)
     m.close()
     return 0

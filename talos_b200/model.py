@@ -169,6 +169,25 @@ class Context:
         _lib.check(_lib.load().talos_ctx_kv_dtype(self.h, C.byref(k)))
         return "f16" if k.value == _lib.KV_F16 else "f32"
 
+    def set_batch(self, max_seqs: int):
+        """Reserve KV cache slots for up to ``max_seqs`` (<= 4) sequences decoded
+        together by ``forward_batch`` (0 frees them)."""
+        _lib.check(_lib.load().talos_ctx_set_batch(self.h, int(max_seqs)))
+
+    def forward_batch(self, tokens, positions) -> np.ndarray:
+        """One step for sequences 0 .. n-1 (token i at positions[i] into cache slot
+        i); returns [n, vocab_size] logits."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        p = np.ascontiguousarray(positions, np.uint64)
+        n = len(t)
+        if len(p) != n:
+            raise ValueError("tokens and positions differ in length")
+        out = np.empty((n, self.cfg.vocab_size), np.float32)
+        _lib.check(_lib.load().talos_forward_batch(self.h, t.ctypes.data_as(C.POINTER(C.c_uint32)),
+                                                   p.ctypes.data_as(C.POINTER(C.c_size_t)), n,
+                                                   out.ctypes.data_as(C.POINTER(C.c_float))))
+        return out
+
     def device_bytes(self) -> int:
         n = C.c_size_t()
         _lib.check(_lib.load().talos_ctx_device_bytes(self.h, C.byref(n)))

@@ -1,0 +1,96 @@
+"""Batched decode (talos_ctx_set_batch / talos_forward_batch): up to 4
+sequences per step, each with its own cache slot and position, against one
+oracle model per sequence. Bars as for one sequence: logits within 1e-3
+max-abs (quantized weights), greedy tokens identical, reruns bit-identical."""
+import numpy as np
+import pytest
+
+import oracle
+from talos_b200 import Model, gguf, synth
+from talos_b200._lib import TalosError
+
+from .helpers import prompt, tiny_model
+
+pytestmark = pytest.mark.gpu
+
+SHAPE_Q6K = synth.Shape(n_embd=512, n_layer=2, n_head=4, n_head_kv=2, n_ff=768, vocab=512, ctx=128)
+
+
+def run_batch(data, prompts, start, steps, m=None):
+    """Slot i joins at step start[i] (position 0) and then takes one token per
+    step: its prompt, then its greedy choice. Returns per-slot logits lists."""
+    cpu = [oracle.Model(data=data) for _ in prompts]
+    own = m is None
+    if own:
+        m = Model.load_bytes(data)
+        m.ctx.set_batch(len(prompts))
+    pos = [0] * len(prompts)
+    nxt = [p[0] for p in prompts]
+    gpu_out, cpu_out = [[] for _ in prompts], [[] for _ in prompts]
+    for step in range(steps):
+        live = [i for i in range(len(prompts)) if start[i] <= step]
+        n = max(live) + 1  # slots 0 .. n-1; a slot that has not joined yet re-feeds position 0
+        toks = [nxt[i] if start[i] <= step else prompts[i][0] for i in range(n)]
+        ps = [pos[i] if start[i] <= step else 0 for i in range(n)]
+        lg = m.ctx.forward_batch(toks, ps)
+        for i in live:
+            c = cpu[i].forward(toks[i], ps[i])
+            gpu_out[i].append(lg[i])
+            cpu_out[i].append(c)
+            pos[i] += 1
+            k = pos[i]
+            nxt[i] = prompts[i][k] if k < len(prompts[i]) else oracle.argmax(c)
+            if k >= len(prompts[i]):
+                assert oracle.argmax(lg[i]) == nxt[i], f"slot {i} greedy token differs at pos {k}"
+    if own:
+        m.close()
+    return gpu_out, cpu_out
+
+
+def max_err(gpu_out, cpu_out):
+    return max(float(np.max(np.abs(g - c))) for gs, cs in zip(gpu_out, cpu_out) for g, c in zip(gs, cs))
+
+
+@pytest.mark.parametrize("wtype", [gguf.Q4_0, gguf.Q8_0])
+def test_batch_matches_oracle_per_sequence(wtype):
+    data = tiny_model(wtype)
+    prompts = [prompt(n, 4096, 20 + i) for i, n in enumerate([6, 9, 4, 12])]
+    g, c = run_batch(data, prompts, start=[0, 0, 0, 3], steps=16)
+    assert max_err(g, c) <= 1e-3
+
+
+def test_batch_q6_k_output_and_fewer_slots():
+    data = synth.llama_bytes(SHAPE_Q6K, 8, wtype=gguf.Q4_0, out_type=gguf.Q6_K)
+    prompts = [prompt(n, 512, 40 + i) for i, n in enumerate([5, 7])]
+    g, c = run_batch(data, prompts, start=[0, 2], steps=12)
+    assert max_err(g, c) <= 1e-3
+
+
+def test_batch_rerun_bit_identical():
+    data = tiny_model(gguf.Q4_0)
+    prompts = [prompt(5, 4096, 60 + i) for i in range(4)]
+    m = Model.load_bytes(data)
+    m.ctx.set_batch(4)
+    a, _ = run_batch(data, prompts, [0, 0, 1, 2], 8, m=m)
+    b, _ = run_batch(data, prompts, [0, 0, 1, 2], 8, m=m)
+    assert all(np.array_equal(x, y) for xs, ys in zip(a, b) for x, y in zip(xs, ys))
+    m.close()
+
+
+def test_batch_argument_errors():
+    m = Model.load_bytes(tiny_model(gguf.Q4_0))
+    with pytest.raises(TalosError, match="INVALID_ARG"):
+        m.ctx.forward_batch([1], [0])  # no slots reserved
+    m.ctx.set_batch(2)
+    with pytest.raises(TalosError, match="INVALID_ARG"):
+        m.ctx.forward_batch([1, 2, 3], [0, 0, 0])
+    with pytest.raises(TalosError, match="INVALID_ARG"):
+        m.ctx.forward_batch([4096, 1], [0, 0])  # token == vocab
+    with pytest.raises(TalosError, match="INVALID_ARG"):
+        m.ctx.set_batch(5)
+    m.close()
+    f = Model.load_bytes(tiny_model(gguf.F32))
+    f.ctx.set_batch(1)
+    with pytest.raises(TalosError, match="UNSUPPORTED"):
+        f.ctx.forward_batch([1], [0])
+    f.close()
