@@ -412,41 +412,6 @@ cudaError_t launch_embed_b(const uint8_t* raw, int type, int cols, int vocab, co
     return cudaGetLastError();
 }
 
-// RoPE on interleaved pairs (2i, 2i+1) with the step's (cos, sin) table row of
-// the sequence's position; the rotated k and the v row go to the sequence's cache.
-__global__ void k_rope_kv_b(float* q, int ldq, int q_rows, const float* k, const float* v, int ldkv, int kv_dim,
-                            int hd, const float2* cs, float* kc, float* vc, size_t seq_stride, const BatchParams* bp) {
-    const int s = blockIdx.x;
-    if (s >= bp->n) return;
-    const uint32_t pos = bp->pos[s];
-    const float2* row = cs + (size_t)pos * (hd >> 1);
-    auto rot = [&](float x0, float x1, int r0, float* o) {
-        const float2 c = row[(r0 % hd) >> 1];
-        o[0] = __fsub_rn(__fmul_rn(x0, c.x), __fmul_rn(x1, c.y));
-        o[1] = __fadd_rn(__fmul_rn(x0, c.y), __fmul_rn(x1, c.x));
-    };
-    float* qs = q + (size_t)s * ldq;
-    for (int i = threadIdx.x; i < q_rows / 2; i += blockDim.x) {
-        float o[2];
-        rot(qs[2 * i], qs[2 * i + 1], 2 * i, o);
-        qs[2 * i] = o[0];
-        qs[2 * i + 1] = o[1];
-    }
-    const float* ks = k + (size_t)s * ldkv;
-    float* kd = kc + (size_t)s * seq_stride + (size_t)pos * kv_dim;
-    for (int i = threadIdx.x; i < kv_dim / 2; i += blockDim.x) rot(ks[2 * i], ks[2 * i + 1], 2 * i, kd + 2 * i);
-    const float* vs = v + (size_t)s * ldkv;
-    float* vd = vc + (size_t)s * seq_stride + (size_t)pos * kv_dim;
-    for (int i = threadIdx.x; i < kv_dim; i += blockDim.x) vd[i] = vs[i];
-}
-
-cudaError_t launch_rope_kv_b(float* q, int ldq, int q_rows, const float* k, const float* v, int ldkv, int kv_dim,
-                             int hd, const float2* rope_cs, float* kc, float* vc, size_t seq_stride,
-                             const BatchParams* bp, cudaStream_t s) {
-    k_rope_kv_b<<<MB_SEQ, 256, 0, s>>>(q, ldq, q_rows, k, v, ldkv, kv_dim, hd, rope_cs, kc, vc, seq_stride, bp);
-    return cudaGetLastError();
-}
-
 // One CTA per (query head, sequence), 8 warps: warp w takes positions w, w+8, ...
 // in rounds of 4 (all K/V loads of a round in flight), keeps an online softmax
 // (max m, sum l, unnormalised o; lane = 4 dims), and the warps merge in shared

@@ -98,17 +98,33 @@ size_t xfmt_sum_bytes(int type, int K);
 cudaError_t launch_xfmt_b(int type, const float* x, int ldx, int K, const float* norm_w, float eps,
                           const BatchParams* bp, void* frag, float* sums, cudaStream_t s);
 
-enum { EPI_B_STORE = 0, EPI_B_ADD = 1 };
-struct BatchMvArgs {
-    PackedW w;
-    int ntiles;             // 16-row tiles
-    int K;
-    const void* frag;       // formatted activation (launch_xfmt_b for w.type)
-    const float* sums;
-    float* y;               // [MB_SEQ][ldy]: y[s][row] = (or +=) row value of sequence s
+// Batched epilogues: store / add rows; SwiGLU of paired gate (A) / up (B) rows;
+// RoPE of q rows (stored to y); RoPE of k rows and v rows, appended to the
+// sequence's cache row at its position.
+enum { EPI_B_STORE = 0, EPI_B_ADD = 1, EPI_B_SWIGLU = 2, EPI_B_ROPE = 3, EPI_B_KCACHE = 4, EPI_B_VCACHE = 5 };
+struct BatchSeg {
+    PackedW A, B;  // B: the up matrix of a SwiGLU pair (tile = 8 rows of A + the same 8 of B)
+    int pair;
+    int ntiles;
+    float* y;      // [MB_SEQ][ldy]
     int ldy;
+    int rows;      // logical output rows
     int epi;
-    const BatchParams* bp;  // active sequence count, error bits
+};
+struct BatchMvArgs {
+    BatchSeg seg[3];  // same type and input; tiles numbered across segments
+    int nseg;
+    int ntiles;
+    int K;
+    const void* frag;  // formatted activation (launch_xfmt_b for the type)
+    const float* sums;
+    const float2* rope_cs;  // RoPE (cos, sin) [ctx][hd/2]
+    int hd;
+    int kv_dim;
+    float* kc;  // this layer's caches: sequence s's rows at kc + s * seq_stride
+    float* vc;
+    size_t seq_stride;
+    const BatchParams* bp;  // active sequence count, positions, error bits
 };
 cudaError_t launch_matvec_b(const BatchMvArgs& a, int max_ctas, cudaStream_t s);
 cudaError_t matvec_b_configure();
@@ -116,12 +132,6 @@ cudaError_t matvec_b_configure();
 // x[s] = dequant(token_embd row of token[s]) (src/model/weights.rs:57-62)
 cudaError_t launch_embed_b(const uint8_t* embd_raw, int type, int cols, int vocab, const BatchParams* bp, float* x,
                            int ldx, cudaStream_t s);
-// q / k RoPE at each sequence's position (src/math/ops.rs:48-61); k and v appended
-// to that sequence's cache row (src/kv_cache.rs:21-26). kc/vc: sequence s's layer
-// cache at kc + s * seq_stride, rows of kv_dim floats.
-cudaError_t launch_rope_kv_b(float* q, int ldq, int q_rows, const float* k, const float* v, int ldkv, int kv_dim,
-                             int hd, const float2* rope_cs, float* kc, float* vc, size_t seq_stride,
-                             const BatchParams* bp, cudaStream_t s);
 // GQA attention per (head, sequence) over positions 0 .. pos[s] (src/model/llama.rs:135-155)
 cudaError_t launch_attention_b(const float* q, int ldq, const float* kc, const float* vc, size_t seq_stride,
                                int kv_dim, int n_head, int n_kv, int hd, float* out, int ldo, const BatchParams* bp,

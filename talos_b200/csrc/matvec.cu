@@ -2468,9 +2468,13 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec_b(const __grid_constan
 
     if (tid >= MV_CONSUMERS + 32) {
         // ---------------- epilogue warp
-        const int n = a.bp->n;
+        const int n = a.bp->n, sq = lane & 3, r = lane >> 2;
+        const uint32_t pos = sq < n ? a.bp->pos[sq] : 0u;
         int it = 0;
         for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, ++it) {
+            int si = 0, lt = t;
+            while (si + 1 < a.nseg && lt >= a.seg[si].ntiles) lt -= a.seg[si++].ntiles;
+            const BatchSeg& sg = a.seg[si];
             const int b = it & 1;
             if (!mbar_wait(&tdone[b], (uint32_t)(it >> 1) & 1)) {
                 s_err = 1;
@@ -2478,6 +2482,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec_b(const __grid_constan
                 return;
             }
             const float* pb = part + b * MV_CWARPS * 64;
+            // v0: row r of sequence sq, v1: row r + 8 (for a pair: gate row r, up row r)
             float v0 = 0.f, v1 = 0.f;
 #pragma unroll
             for (int w = 0; w < MV_CWARPS; ++w) {
@@ -2486,13 +2491,34 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec_b(const __grid_constan
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&tfree[b]);
+            const bool live = sq < n;
+            float* ys = sg.y + (size_t)sq * sg.ldy;
+            if (sg.epi == EPI_B_SWIGLU) {  // src/math/ops.rs:33-37
+                const int row = 8 * lt + r;
+                if (live && row < sg.rows) ys[row] = __fmul_rn(silu_ref(v0), v1);
+            } else if (sg.epi >= EPI_B_ROPE) {
+                // pairs (2i, 2i+1) sit on lanes l and l ^ 4 (src/math/ops.rs:48-61)
+                const float p0 = __shfl_xor_sync(0xffffffffu, v0, 4), p1 = __shfl_xor_sync(0xffffffffu, v1, 4);
+                float* dst = sg.epi == EPI_B_ROPE ? ys
+                             : (sg.epi == EPI_B_KCACHE ? a.kc : a.vc) + (size_t)sq * a.seq_stride + (size_t)pos * a.kv_dim;
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int idx = lane + 32 * h, row = 16 * t + idx / 4, sq = idx % 4;
-                const float v = h ? v1 : v0;
-                if (sq < n && row < a.w.rows) {
-                    float* dst = a.y + (size_t)sq * a.ldy + row;
-                    *dst = a.epi == EPI_B_ADD ? __fadd_rn(*dst, v) : v;
+                for (int h = 0; h < 2; ++h) {
+                    const int row = 16 * lt + r + 8 * h;
+                    const float v = h ? v1 : v0, pv = h ? p1 : p0;
+                    float o = v;
+                    if (sg.epi != EPI_B_VCACHE) {
+                        const float2 c = a.rope_cs[(size_t)pos * (a.hd >> 1) + ((row % a.hd) >> 1)];
+                        o = (row & 1) ? __fadd_rn(__fmul_rn(pv, c.y), __fmul_rn(v, c.x))
+                                      : __fsub_rn(__fmul_rn(v, c.x), __fmul_rn(pv, c.y));
+                    }
+                    if (live && row < sg.rows) dst[row] = o;
+                }
+            } else {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int row = 16 * lt + r + 8 * h;
+                    const float v = h ? v1 : v0;
+                    if (live && row < sg.rows) ys[row] = sg.epi == EPI_B_ADD ? __fadd_rn(ys[row], v) : v;
                 }
             }
         }
@@ -2504,8 +2530,12 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec_b(const __grid_constan
             uint32_t it = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < a.ntiles && ok; t += gridDim.x) {
-                const uint8_t* ga0 = (const uint8_t*)a.w.p0 + (size_t)(2 * t) * a.w.nk * GCB;
-                const uint8_t* gb0 = (const uint8_t*)a.w.p0 + (size_t)(2 * t + 1) * a.w.nk * GCB;
+                int si = 0, lt = t;
+                while (si + 1 < a.nseg && lt >= a.seg[si].ntiles) lt -= a.seg[si++].ntiles;
+                const BatchSeg& sg = a.seg[si];
+                const PackedW& WB = sg.pair ? sg.B : sg.A;
+                const uint8_t* ga0 = (const uint8_t*)sg.A.p0 + (size_t)(sg.pair ? lt : 2 * lt) * sg.A.nk * GCB;
+                const uint8_t* gb0 = (const uint8_t*)WB.p0 + (size_t)(sg.pair ? lt : 2 * lt + 1) * WB.nk * GCB;
                 for (int c = 0; c < nchunk; ++c, ++it) {
                     const int slot = it % NST;
                     if (!mbar_wait(&empty[slot], ((it / NST) & 1) ^ 1) || *(volatile int*)&s_err) {
@@ -2591,7 +2621,7 @@ cudaError_t matvec_b_configure() {
 cudaError_t launch_matvec_b(const BatchMvArgs& a, int max_ctas, cudaStream_t s) {
     if (a.ntiles <= 0) return cudaSuccess;
     const int grid = a.ntiles < max_ctas ? a.ntiles : max_ctas;
-    switch (a.w.type) {
+    switch (a.seg[0].A.type) {
         case GT_Q4_0: k_matvec_b<GT_Q4_0><<<grid, MV_THREADS, matvec_b_smem<GT_Q4_0>(), s>>>(a); break;
         case GT_Q8_0: k_matvec_b<GT_Q8_0><<<grid, MV_THREADS, matvec_b_smem<GT_Q8_0>(), s>>>(a); break;
         case GT_Q6_K: k_matvec_b<GT_Q6_K><<<grid, MV_THREADS, matvec_b_smem<GT_Q6_K>(), s>>>(a); break;

@@ -446,7 +446,7 @@ struct talos_ctx {
     size_t bbytes = 0;
     BatchParams* bp = nullptr;
     BatchParams* h_bp = nullptr;  // pinned
-    float *bx = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr, *batt = nullptr;
+    float *bx = nullptr, *bq = nullptr, *batt = nullptr;
     float *bg = nullptr, *bu = nullptr, *bh = nullptr, *blog = nullptr, *bsums = nullptr;
     void* bfrag = nullptr;
     float *bkc = nullptr, *bvc = nullptr;  // [bmax][n_layer][kv_ctx][kv_dim]
@@ -1641,8 +1641,8 @@ extern "C" talos_status talos_ctx_set_batch(talos_ctx* c, int max_seqs) {
         return o;
     };
     const size_t o_bp = take(sizeof(BatchParams));
-    const size_t o_x = take(MB_SEQ * E * 4), o_q = take(MB_SEQ * c->q_rows * 4), o_k = take(MB_SEQ * c->kv_dim * 4),
-                 o_v = take(MB_SEQ * c->kv_dim * 4), o_att = take(MB_SEQ * E * 4), o_g = take(MB_SEQ * F * 4),
+    const size_t o_x = take(MB_SEQ * E * 4), o_q = take(MB_SEQ * c->q_rows * 4), o_att = take(MB_SEQ * E * 4),
+                 o_g = take(MB_SEQ * F * 4),
                  o_u = take(MB_SEQ * F * 4), o_h = take(MB_SEQ * F * 4), o_log = take(MB_SEQ * V * 4);
     const size_t o_frag = take(KPmax / 32 * 512), o_sums = take(KPmax / 16 * MB_SEQ * 4);
     const size_t seq_stride = L * c->kv_ctx * (size_t)c->kv_dim;
@@ -1654,7 +1654,7 @@ extern "C" talos_status talos_ctx_set_batch(talos_ctx* c, int max_seqs) {
     c->bmem = mem;
     c->bbytes = off;
     c->bp = (BatchParams*)(b + o_bp);
-    c->bx = (float*)(b + o_x), c->bq = (float*)(b + o_q), c->bk = (float*)(b + o_k), c->bv = (float*)(b + o_v);
+    c->bx = (float*)(b + o_x), c->bq = (float*)(b + o_q);
     c->batt = (float*)(b + o_att), c->bg = (float*)(b + o_g), c->bu = (float*)(b + o_u), c->bh = (float*)(b + o_h);
     c->blog = (float*)(b + o_log), c->bfrag = b + o_frag, c->bsums = (float*)(b + o_sums);
     c->bkc = (float*)(b + o_kc), c->bvc = (float*)(b + o_vc);
@@ -1666,31 +1666,40 @@ extern "C" talos_status talos_ctx_set_batch(talos_ctx* c, int max_seqs) {
     return TALOS_OK;
 }
 
-// x formatted for weight w (skipped when the previous matvec read the same input
-// the same way), then y (+)= w x for every live sequence.
+// x formatted for the segments' weight type (skipped when the previous matvec
+// read the same input the same way), then every segment's rows for every live
+// sequence in one launch.
 struct BatchFmtCache {
     const float* in = nullptr;
     const float* norm = nullptr;
     int type = -1;
 };
 
-static talos_status mv_b(talos_ctx* c, BatchFmtCache& fc, const DevTensor* w, const float* in, int K,
-                         const float* norm, float* y, int ldy, int epi) {
+static BatchSeg bseg(const DevTensor* A, const DevTensor* B, float* y, int ldy, int rows, int epi) {
+    BatchSeg g{};
+    g.A = A->w;
+    g.pair = B != nullptr;
+    if (B) g.B = B->w;
+    g.ntiles = B ? A->w.rows_pad / 8 : A->w.rows_pad / 16;
+    g.y = y;
+    g.ldy = ldy;
+    g.rows = rows;
+    g.epi = epi;
+    return g;
+}
+
+static talos_status mv_b(talos_ctx* c, BatchFmtCache& fc, BatchMvArgs a, const float* in, const float* norm) {
+    const int type = a.seg[0].A.type;
     cudaError_t e = cudaSuccess;
-    if (fc.in != in || fc.norm != norm || fc.type != w->type) {
-        e = launch_xfmt_b(w->type, in, K, K, norm, c->cfg.rms_eps, c->bp, c->bfrag, c->bsums, c->stream);
+    if (fc.in != in || fc.norm != norm || fc.type != type) {
+        e = launch_xfmt_b(type, in, a.K, a.K, norm, c->cfg.rms_eps, c->bp, c->bfrag, c->bsums, c->stream);
         if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched input format: %s", cudaGetErrorString(e));
-        fc = BatchFmtCache{in, norm, w->type};
+        fc = BatchFmtCache{in, norm, type};
     }
-    BatchMvArgs a{};
-    a.w = w->w;
-    a.ntiles = w->w.rows_pad / 16;
-    a.K = (int)w->cols;
+    a.ntiles = 0;
+    for (int i = 0; i < a.nseg; ++i) a.ntiles += a.seg[i].ntiles;
     a.frag = c->bfrag;
     a.sums = c->bsums;
-    a.y = y;
-    a.ldy = ldy;
-    a.epi = epi;
     a.bp = c->bp;
     e = launch_matvec_b(a, sm_count(c), c->stream);
     if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched matvec: %s", cudaGetErrorString(e));
@@ -1707,33 +1716,70 @@ static talos_status enqueue_batch(talos_ctx* c) {
     const size_t kv_layer = c->kv_ctx * (size_t)c->kv_dim;
     for (uint32_t l = 0; l < cfg.n_layer; ++l) {
         const LayerW& L = c->layers[l];
-        const float* an = (const float*)L.attn_norm->mem;
-        // rmsnorm + q/k/v + RoPE + KV append (llama.rs:118-130)
-        TRY(mv_b(c, fc, L.q, c->bx, E, an, c->bq, c->q_rows, EPI_B_STORE));
-        TRY(mv_b(c, fc, L.k, c->bx, E, an, c->bk, c->kv_dim, EPI_B_STORE));
-        TRY(mv_b(c, fc, L.v, c->bx, E, an, c->bv, c->kv_dim, EPI_B_STORE));
         float* kc = c->bkc + l * kv_layer;
         float* vc = c->bvc + l * kv_layer;
-        e = launch_rope_kv_b(c->bq, c->q_rows, c->q_rows, c->bk, c->bv, c->kv_dim, c->kv_dim, c->hd, c->rope_cs, kc, vc,
-                             c->bseq_stride, c->bp, c->stream);
-        if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched rope: %s", cudaGetErrorString(e));
+        // rmsnorm + q/k/v + RoPE + KV append (llama.rs:118-130): one launch when
+        // the three share a type
+        {
+            const DevTensor* w3[3] = {L.q, L.k, L.v};
+            const int epi3[3] = {EPI_B_ROPE, EPI_B_KCACHE, EPI_B_VCACHE};
+            const int rows3[3] = {c->q_rows, c->kv_dim, c->kv_dim};
+            for (int i = 0; i < 3;) {
+                BatchMvArgs a{};
+                a.K = E;
+                a.rope_cs = c->rope_cs;
+                a.hd = c->hd;
+                a.kv_dim = c->kv_dim;
+                a.kc = kc;
+                a.vc = vc;
+                a.seq_stride = c->bseq_stride;
+                do {
+                    a.seg[a.nseg++] = bseg(w3[i], nullptr, c->bq, c->q_rows, rows3[i], epi3[i]);
+                    ++i;
+                } while (i < 3 && a.seg[0].A.type == w3[i]->type);
+                TRY(mv_b(c, fc, a, c->bx, (const float*)L.attn_norm->mem));
+            }
+        }
         // attention (llama.rs:135-155), o-proj + residual (:157-161)
         e = launch_attention_b(c->bq, c->q_rows, kc, vc, c->bseq_stride, c->kv_dim, (int)cfg.n_head,
                                (int)cfg.n_head_kv, c->hd, c->batt, E, c->bp, c->stream);
         if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched attention: %s", cudaGetErrorString(e));
-        TRY(mv_b(c, fc, L.o, c->batt, E, nullptr, c->bx, E, EPI_B_ADD));
-        // rmsnorm + SwiGLU FFN + residual (:163-176)
+        {
+            BatchMvArgs a{};
+            a.K = E;
+            a.seg[a.nseg++] = bseg(L.o, nullptr, c->bx, E, E, EPI_B_ADD);
+            TRY(mv_b(c, fc, a, c->batt, nullptr));
+        }
+        // rmsnorm + SwiGLU FFN (gate/up paired when they share a type) + residual (:163-176)
         const float* fn = (const float*)L.ffn_norm->mem;
-        TRY(mv_b(c, fc, L.gate, c->bx, E, fn, c->bg, F, EPI_B_STORE));
-        TRY(mv_b(c, fc, L.up, c->bx, E, fn, c->bu, F, EPI_B_STORE));
-        e = launch_swiglu_b(c->bg, c->bu, c->bh, F, F, c->bp, c->stream);
-        if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched swiglu: %s", cudaGetErrorString(e));
-        TRY(mv_b(c, fc, L.down, c->bh, F, nullptr, c->bx, E, EPI_B_ADD));
+        if (L.gate->type == L.up->type) {
+            BatchMvArgs a{};
+            a.K = E;
+            a.seg[a.nseg++] = bseg(L.gate, L.up, c->bh, F, F, EPI_B_SWIGLU);
+            TRY(mv_b(c, fc, a, c->bx, fn));
+        } else {
+            BatchMvArgs a{};
+            a.K = E;
+            a.seg[a.nseg++] = bseg(L.gate, nullptr, c->bg, F, F, EPI_B_STORE);
+            TRY(mv_b(c, fc, a, c->bx, fn));
+            a.seg[0] = bseg(L.up, nullptr, c->bu, F, F, EPI_B_STORE);
+            TRY(mv_b(c, fc, a, c->bx, fn));
+            e = launch_swiglu_b(c->bg, c->bu, c->bh, F, F, c->bp, c->stream);
+            if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched swiglu: %s", cudaGetErrorString(e));
+        }
+        {
+            BatchMvArgs a{};
+            a.K = F;
+            a.seg[a.nseg++] = bseg(L.down, nullptr, c->bx, E, E, EPI_B_ADD);
+            TRY(mv_b(c, fc, a, c->bh, nullptr));
+        }
         fc = BatchFmtCache{};  // bx changed in place
     }
     // final norm + logits (:89, :181)
-    const DevTensor& ow = c->w["output.weight"];
-    TRY(mv_b(c, fc, &ow, c->bx, E, (const float*)c->w["output_norm.weight"].mem, c->blog, V, EPI_B_STORE));
+    BatchMvArgs a{};
+    a.K = E;
+    a.seg[a.nseg++] = bseg(&c->w["output.weight"], nullptr, c->blog, V, V, EPI_B_STORE);
+    TRY(mv_b(c, fc, a, c->bx, (const float*)c->w["output_norm.weight"].mem));
     return TALOS_OK;
 }
 
