@@ -9,24 +9,19 @@ namespace talos {
 
 enum GType : int { GT_F32 = 0, GT_Q4_0 = 2, GT_Q8_0 = 8, GT_Q6_K = 14 };
 
-// A weight matrix after repacking on the device. Row counts are padded to a
-// multiple of 16 (two 8-row groups); pad rows hold zeros.
-//
-//  F32 : p0 = float [rows_pad][cols]
-//  Q8_0: p0 = int8  [rows_pad][nb*32] (quants of each block, row-contiguous)
-//        p1 = half  [rows_pad][nb]    (block scales)
-//  Q4_0: p0 = uint4 [rows_pad/8][nq][32 lanes]  (one 16-byte word set per lane and
-//        block-quad; see pack_q4_0 in kernels.cu for the nibble order)
-//        p1 = uint2 [rows_pad/8][nq][8 rows]    (4 block scales per row, f16)
-//  Q6_K: p0 = uint32 [rows_pad][nsb][32] (ql bytes l, l+32, 64+l, 96+l per lane)
-//        p1 = uint16 [rows_pad][nsb][32] (qh bytes l, 32+l per lane)
-//        p2 = int8   [rows_pad][nsb][16] (sub-block scales)
-//        p3 = half   [rows_pad][nsb]     (super-block scale d)
+// A weight matrix after repacking on the device (k_pack_* in matvec.cu): one
+// array p0 of group-chunks, each 8 rows x CK input elements, contiguous and in
+// the register order the consumers read, ordered [row group][chunk]; a 16-row
+// tile is two group-chunks. CK and bytes per group-chunk: Q4_0 2048, 9216 B
+// (nibbles + f16 block scales); Q8_0 1024, 8704 B; Q6_K 1024, 8768 B (6-bit
+// quants widened to bytes, sub-block scales, f16 super-block scales); F32 256,
+// 8192 B. Rows pad to a multiple of 16 and columns to CK with entries that add
+// nothing (quant at the zero point, scale 0). p1 .. p3 are unused (null).
 struct PackedW {
     int type;
     int rows, cols;   // logical shape [rows, cols]
     int rows_pad;     // multiple of 16
-    int nk;           // F32: cols; Q8_0: blocks; Q4_0: block quads; Q6_K: super-blocks
+    int nk;           // chunks per row group (cols rounded up to CK)
     const void* p0;
     const void* p1;
     const void* p2;
