@@ -194,7 +194,9 @@ talos_status talos_generate_greedy(talos_ctx* ctx, uint32_t token, size_t pos, s
 /*
  * Feed `n` prompt tokens at positions pos0 .. pos0+n-1 (the prefill loop of
  * src/main.rs:88-95) and write the logits after the last one to `last_logits`
- * (host, may be NULL).
+ * (host, may be NULL). On one GPU with an f32 cache and Q4_0 / Q8_0 / Q6_K
+ * matrices the prompt goes through the batched step, 4 consecutive positions
+ * per weight pass; otherwise one token per step.
  */
 talos_status talos_prefill(talos_ctx* ctx, const uint32_t* tokens, size_t n, size_t pos0,
                            float* last_logits);

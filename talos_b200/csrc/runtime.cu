@@ -453,6 +453,7 @@ struct talos_ctx {
     size_t bseq_stride = 0;                // floats per sequence in bkc / bvc
     float* h_blog = nullptr;               // pinned [MB_SEQ][V]
     cudaGraphExec_t bgraph = nullptr;
+    cudaGraphExec_t bgraph_pf = nullptr;  // the same step on the main cache: chunked prefill
 
     void drop_graphs() {
         for (auto& g : graph)
@@ -463,6 +464,10 @@ struct talos_ctx {
         if (bgraph) {
             cudaGraphExecDestroy(bgraph);
             bgraph = nullptr;
+        }
+        if (bgraph_pf) {
+            cudaGraphExecDestroy(bgraph_pf);
+            bgraph_pf = nullptr;
         }
         for (auto& p : d_phases)
             if (p) {
@@ -1542,12 +1547,18 @@ __global__ void k_set_step(StepParams* s, uint32_t token, uint32_t pos) {
     s->pos = pos;
 }
 
+static talos_status prefill_chunked(talos_ctx* c, const uint32_t* tokens, size_t n, size_t pos0, float* last_logits,
+                                    bool* taken);
+
 extern "C" talos_status talos_prefill(talos_ctx* c, const uint32_t* tokens, size_t n, size_t pos0,
                                       float* last_logits) {
     if (!c || (!tokens && n)) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
     if (n == 0) return TALOS_OK;
     CK(cudaSetDevice(c->device));
     for (size_t i = 0; i < n; ++i) TRY(check_tok_pos(c, tokens[i], pos0 + i));
+    bool taken = false;
+    TRY(prefill_chunked(c, tokens, n, pos0, last_logits, &taken));
+    if (taken) return TALOS_OK;
     TRY(ensure_graph(c, GM_LOGITS));
     TRY(set_step(c, tokens[0], pos0));
     for (size_t i = 0; i < n; ++i) {
@@ -1613,10 +1624,11 @@ static talos_status profile_fused(talos_ctx* c, double* kernel_ms, uint32_t* lau
 
 static talos_status batch_free(talos_ctx* c) {
     CK(cudaStreamSynchronize(c->stream));
-    if (c->bgraph) {
-        cudaGraphExecDestroy(c->bgraph);
-        c->bgraph = nullptr;
-    }
+    for (cudaGraphExec_t* g : {&c->bgraph, &c->bgraph_pf})
+        if (*g) {
+            cudaGraphExecDestroy(*g);
+            *g = nullptr;
+        }
     if (c->bmem) cudaFree(c->bmem);
     c->bmem = nullptr;
     c->bbytes = 0;
@@ -1624,14 +1636,10 @@ static talos_status batch_free(talos_ctx* c) {
     return TALOS_OK;
 }
 
-extern "C" talos_status talos_ctx_set_batch(talos_ctx* c, int max_seqs) {
-    if (!c) return set_err(TALOS_ERR_INVALID_ARG, "NULL ctx");
-    if (max_seqs < 0 || max_seqs > MB_SEQ)
-        return set_err(TALOS_ERR_INVALID_ARG, "batch of %d sequences (at most %d)", max_seqs, MB_SEQ);
-    if (c->tp > 1) return set_err(TALOS_ERR_UNSUPPORTED, "batched decode under tensor parallelism");
-    CK(cudaSetDevice(c->device));
+// The batched step's buffers, with cache slots for max_seqs sequences (0: the
+// activations only, for the chunked prefill on the main cache).
+static talos_status batch_alloc(talos_ctx* c, int max_seqs) {
     TRY(batch_free(c));
-    if (max_seqs == 0) return TALOS_OK;
     const size_t E = c->cfg.n_embd, F = c->cfg.n_ff, V = c->cfg.vocab_size, L = c->cfg.n_layer;
     const size_t KPmax = ((std::max(E, F) + 2047) / 2048) * 2048;  // largest chunk-rounded input
     size_t off = 0;
@@ -1646,7 +1654,7 @@ extern "C" talos_status talos_ctx_set_batch(talos_ctx* c, int max_seqs) {
                  o_u = take(MB_SEQ * F * 4), o_h = take(MB_SEQ * F * 4), o_log = take(MB_SEQ * V * 4);
     const size_t o_frag = take(KPmax / 32 * 512), o_sums = take(KPmax / 16 * MB_SEQ * 4);
     const size_t seq_stride = L * c->kv_ctx * (size_t)c->kv_dim;
-    const size_t o_kc = take((size_t)max_seqs * seq_stride * 4), o_vc = take((size_t)max_seqs * seq_stride * 4);
+    const size_t o_kc = take((size_t)max_seqs * seq_stride * 4 + 4), o_vc = take((size_t)max_seqs * seq_stride * 4 + 4);
     void* mem = nullptr;
     CK(cudaMalloc(&mem, off));
     CK(cudaMemsetAsync(mem, 0, off, c->stream));
@@ -1664,6 +1672,16 @@ extern "C" talos_status talos_ctx_set_batch(talos_ctx* c, int max_seqs) {
     c->bmax = max_seqs;
     CK(cudaStreamSynchronize(c->stream));
     return TALOS_OK;
+}
+
+extern "C" talos_status talos_ctx_set_batch(talos_ctx* c, int max_seqs) {
+    if (!c) return set_err(TALOS_ERR_INVALID_ARG, "NULL ctx");
+    if (max_seqs < 0 || max_seqs > MB_SEQ)
+        return set_err(TALOS_ERR_INVALID_ARG, "batch of %d sequences (at most %d)", max_seqs, MB_SEQ);
+    if (c->tp > 1) return set_err(TALOS_ERR_UNSUPPORTED, "batched decode under tensor parallelism");
+    CK(cudaSetDevice(c->device));
+    if (max_seqs == 0) return batch_free(c);
+    return batch_alloc(c, max_seqs);
 }
 
 // x formatted for the segments' weight type (skipped when the previous matvec
@@ -1706,7 +1724,10 @@ static talos_status mv_b(talos_ctx* c, BatchFmtCache& fc, BatchMvArgs a, const f
     return TALOS_OK;
 }
 
-static talos_status enqueue_batch(talos_ctx* c) {
+// prefill: the slots are consecutive positions of the one sequence of the main
+// cache (f32), so every slot's K/V row lands there and attention sees the rows
+// the other slots of the step appended.
+static talos_status enqueue_batch(talos_ctx* c, bool prefill) {
     const talos_cfg& cfg = c->cfg;
     const int E = (int)cfg.n_embd, F = (int)cfg.n_ff, V = (int)cfg.vocab_size;
     const DevTensor& embd = c->w["token_embd.weight"];
@@ -1714,10 +1735,11 @@ static talos_status enqueue_batch(talos_ctx* c) {
     if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched embed: %s", cudaGetErrorString(e));
     BatchFmtCache fc;
     const size_t kv_layer = c->kv_ctx * (size_t)c->kv_dim;
+    const size_t seq_stride = prefill ? 0 : c->bseq_stride;
     for (uint32_t l = 0; l < cfg.n_layer; ++l) {
         const LayerW& L = c->layers[l];
-        float* kc = c->bkc + l * kv_layer;
-        float* vc = c->bvc + l * kv_layer;
+        float* kc = (prefill ? (float*)c->kcache : c->bkc) + l * kv_layer;
+        float* vc = (prefill ? (float*)c->vcache : c->bvc) + l * kv_layer;
         // rmsnorm + q/k/v + RoPE + KV append (llama.rs:118-130): one launch when
         // the three share a type
         {
@@ -1732,7 +1754,7 @@ static talos_status enqueue_batch(talos_ctx* c) {
                 a.kv_dim = c->kv_dim;
                 a.kc = kc;
                 a.vc = vc;
-                a.seq_stride = c->bseq_stride;
+                a.seq_stride = seq_stride;
                 do {
                     a.seg[a.nseg++] = bseg(w3[i], nullptr, c->bq, c->q_rows, rows3[i], epi3[i]);
                     ++i;
@@ -1741,7 +1763,7 @@ static talos_status enqueue_batch(talos_ctx* c) {
             }
         }
         // attention (llama.rs:135-155), o-proj + residual (:157-161)
-        e = launch_attention_b(c->bq, c->q_rows, kc, vc, c->bseq_stride, c->kv_dim, (int)cfg.n_head,
+        e = launch_attention_b(c->bq, c->q_rows, kc, vc, seq_stride, c->kv_dim, (int)cfg.n_head,
                                (int)cfg.n_head_kv, c->hd, c->batt, E, c->bp, c->stream);
         if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched attention: %s", cudaGetErrorString(e));
         {
@@ -1794,6 +1816,59 @@ static talos_status batch_check(talos_ctx* c) {
     return TALOS_OK;
 }
 
+// keep_err: the error bits of the call's earlier steps stay for batch_finish
+__global__ void k_set_batch(BatchParams* d, BatchParams v, bool keep_err) {
+    if (keep_err) v.error = d->error;
+    *d = v;
+}
+
+static talos_status batch_graph(talos_ctx* c, bool prefill, cudaGraphExec_t* out) {
+    if (*out) return TALOS_OK;
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    talos_status st = enqueue_batch(c, prefill);
+    cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+    if (st != TALOS_OK) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        return st;
+    }
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched graph capture: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched graph instantiate: %s", cudaGetErrorString(e));
+    return TALOS_OK;
+}
+
+// One batched step: parameters set by a kernel (stream-ordered, so the host never
+// rewrites a buffer a pending copy reads), then the graph.
+static talos_status batch_step(talos_ctx* c, cudaGraphExec_t g, const uint32_t* tokens, const size_t* pos, int n,
+                               bool first) {
+    BatchParams v{};
+    v.n = n;
+    for (int i = 0; i < n; ++i) {
+        v.token[i] = tokens[i];
+        v.pos[i] = (uint32_t)pos[i];
+    }
+    k_set_batch<<<1, 1, 0, c->stream>>>(c->bp, v, !first);
+    CK(cudaGetLastError());
+    CK(cudaGraphLaunch(g, c->stream));
+    return TALOS_OK;
+}
+
+// Copy n x V logits of the last batched step (host may be NULL) and check its errors.
+static talos_status batch_finish(talos_ctx* c, int n, float* logits_out) {
+    const size_t V = c->cfg.vocab_size;
+    if (logits_out) CK(cudaMemcpyAsync(c->h_blog, c->blog, (size_t)n * V * 4, cudaMemcpyDeviceToHost, c->stream));
+    BatchParams& hp = *c->h_bp;
+    CK(cudaMemcpyAsync(&hp, c->bp, sizeof hp, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    if (hp.error & 2u) return set_err(TALOS_ERR_TIMEOUT, "batched step: a bounded wait expired");
+    if (hp.error) return set_err(TALOS_ERR_OOB, "batched step: device check failed (%u)", hp.error);
+    if (logits_out) memcpy(logits_out, c->h_blog, (size_t)n * V * 4);
+    return TALOS_OK;
+}
+
 extern "C" talos_status talos_forward_batch(talos_ctx* c, const uint32_t* tokens, const size_t* pos, int n,
                                             float* logits_out) {
     if (!c || !tokens || !pos || !logits_out) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
@@ -1803,38 +1878,36 @@ extern "C" talos_status talos_forward_batch(talos_ctx* c, const uint32_t* tokens
     for (int i = 0; i < n; ++i) TRY(check_tok_pos(c, tokens[i], pos[i]));
     TRY(bind_if_dirty(c));
     TRY(batch_check(c));
-    if (!c->bgraph) {
-        cudaGraph_t g = nullptr;
-        CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-        talos_status st = enqueue_batch(c);
-        cudaError_t e = cudaStreamEndCapture(c->stream, &g);
-        if (st != TALOS_OK) {
-            if (g) cudaGraphDestroy(g);
-            cudaGetLastError();
-            return st;
-        }
-        if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched graph capture: %s", cudaGetErrorString(e));
-        e = cudaGraphInstantiate(&c->bgraph, g, 0);
-        cudaGraphDestroy(g);
-        if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched graph instantiate: %s", cudaGetErrorString(e));
+    TRY(batch_graph(c, false, &c->bgraph));
+    TRY(batch_step(c, c->bgraph, tokens, pos, n, true));
+    return batch_finish(c, n, logits_out);
+}
+
+// talos_prefill in steps of MB_SEQ consecutive prompt positions: one weight pass
+// per step instead of one per token. Taken when the batched step runs the model
+// and the main cache is f32 on one GPU; false in *taken otherwise.
+static talos_status prefill_chunked(talos_ctx* c, const uint32_t* tokens, size_t n, size_t pos0, float* last_logits,
+                                    bool* taken) {
+    *taken = false;
+    if (c->tp > 1 || c->kv_f16 || n < 2) return TALOS_OK;
+    TRY(bind_if_dirty(c));
+    if (batch_check(c) != TALOS_OK) return TALOS_OK;
+    if (!c->bmem) TRY(batch_alloc(c, 0));
+    TRY(batch_graph(c, true, &c->bgraph_pf));
+    *taken = true;
+    int last_n = 1;
+    for (size_t i = 0; i < n; i += MB_SEQ) {
+        const int k = (int)std::min<size_t>(MB_SEQ, n - i);
+        size_t pos[MB_SEQ];
+        for (int j = 0; j < k; ++j) pos[j] = pos0 + i + j;
+        TRY(batch_step(c, c->bgraph_pf, tokens + i, pos, k, i == 0));
+        last_n = k;
     }
-    CK(cudaStreamSynchronize(c->stream));  // the previous step no longer reads the parameters
-    BatchParams& hp = *c->h_bp;
-    memset(&hp, 0, sizeof hp);
-    hp.n = n;
-    for (int i = 0; i < n; ++i) {
-        hp.token[i] = tokens[i];
-        hp.pos[i] = (uint32_t)pos[i];
-    }
-    CK(cudaMemcpyAsync(c->bp, &hp, sizeof hp, cudaMemcpyHostToDevice, c->stream));
-    CK(cudaGraphLaunch(c->bgraph, c->stream));
-    const size_t V = c->cfg.vocab_size;
-    CK(cudaMemcpyAsync(c->h_blog, c->blog, (size_t)n * V * 4, cudaMemcpyDeviceToHost, c->stream));
-    CK(cudaMemcpyAsync(&hp, c->bp, sizeof hp, cudaMemcpyDeviceToHost, c->stream));
-    CK(cudaStreamSynchronize(c->stream));
-    if (hp.error & 2u) return set_err(TALOS_ERR_TIMEOUT, "batched step: a bounded wait expired");
-    if (hp.error) return set_err(TALOS_ERR_OOB, "batched step: device check failed (%u)", hp.error);
-    memcpy(logits_out, c->h_blog, (size_t)n * V * 4);
+    std::vector<float> all;
+    if (last_logits) all.resize((size_t)last_n * c->cfg.vocab_size);
+    TRY(batch_finish(c, last_n, last_logits ? all.data() : nullptr));
+    if (last_logits)
+        memcpy(last_logits, all.data() + (size_t)(last_n - 1) * c->cfg.vocab_size, c->cfg.vocab_size * 4);
     return TALOS_OK;
 }
 

@@ -94,3 +94,27 @@ def test_batch_argument_errors():
     with pytest.raises(TalosError, match="UNSUPPORTED"):
         f.ctx.forward_batch([1], [0])
     f.close()
+
+
+@pytest.mark.parametrize("n,pos0", [(1, 0), (5, 0), (11, 0), (6, 3)])
+def test_prefill_in_batched_steps(n, pos0):
+    """talos_prefill runs 4 consecutive prompt positions per weight pass on the
+    main cache: the last logits and the decode steps after it match the oracle."""
+    data = tiny_model(gguf.Q8_0)
+    cpu = oracle.Model(data=data)
+    gpu = Model.load_bytes(data)
+    head = prompt(pos0, 4096, 70)
+    toks = prompt(n, 4096, 71)
+    if pos0:
+        gpu.prefill(head, 0)
+    for p, t in enumerate(head + toks):
+        ref = cpu.forward(t, p)
+    last = gpu.prefill(toks, pos0)
+    assert np.max(np.abs(last - ref)) <= 1e-3
+    pos = pos0 + n
+    t = oracle.argmax(ref)
+    for _ in range(6):  # the cache rows the batched steps wrote serve the per-token kernel
+        g, c = gpu.forward_gpu(t, pos), cpu.forward(t, pos)
+        assert np.max(np.abs(g - c)) <= 1e-3
+        t, pos = oracle.argmax(c), pos + 1
+    gpu.close()
