@@ -226,7 +226,8 @@ talos_status talos_forward_batch(talos_ctx* ctx, const uint32_t* tokens, const s
  * (src/eval.rs:35-52). The tokens are scored in chunks of the context length,
  * each from an empty KV cache; at each position the negative log-likelihood of
  * the next token (token_nll, src/eval.rs:18-23: log-sum-exp in f64) is added on
- * the GPU, so no logits leave the device. Writes exp(mean NLL) to *ppl_out and,
+ * the GPU, so no logits leave the device (4 positions per weight pass where
+ * talos_prefill takes its batched steps). Writes exp(mean NLL) to *ppl_out and,
  * if not NULL, the NLL sum and the number of scored positions. Leaves the KV
  * cache holding the last chunk.
  */

@@ -1886,15 +1886,25 @@ extern "C" talos_status talos_forward_batch(talos_ctx* c, const uint32_t* tokens
 // talos_prefill in steps of MB_SEQ consecutive prompt positions: one weight pass
 // per step instead of one per token. Taken when the batched step runs the model
 // and the main cache is f32 on one GPU; false in *taken otherwise.
-static talos_status prefill_chunked(talos_ctx* c, const uint32_t* tokens, size_t n, size_t pos0, float* last_logits,
-                                    bool* taken) {
-    *taken = false;
-    if (c->tp > 1 || c->kv_f16 || n < 2) return TALOS_OK;
+// Whether the batched step can run consecutive positions of the main cache
+// (one GPU, f32 cache, Q4_0 / Q8_0 / Q6_K matrices); if so its graph is ready.
+static talos_status chunked_ready(talos_ctx* c, bool* ok) {
+    *ok = false;
+    if (c->tp > 1 || c->kv_f16) return TALOS_OK;
     TRY(bind_if_dirty(c));
     if (batch_check(c) != TALOS_OK) return TALOS_OK;
     if (!c->bmem) TRY(batch_alloc(c, 0));
     TRY(batch_graph(c, true, &c->bgraph_pf));
-    *taken = true;
+    *ok = true;
+    return TALOS_OK;
+}
+
+static talos_status prefill_chunked(talos_ctx* c, const uint32_t* tokens, size_t n, size_t pos0, float* last_logits,
+                                    bool* taken) {
+    *taken = false;
+    if (n < 2) return TALOS_OK;
+    TRY(chunked_ready(c, taken));
+    if (!*taken) return TALOS_OK;
     int last_n = 1;
     for (size_t i = 0; i < n; i += MB_SEQ) {
         const int k = (int)std::min<size_t>(MB_SEQ, n - i);
@@ -1920,27 +1930,45 @@ extern "C" talos_status talos_perplexity(talos_ctx* c, const uint32_t* tokens, s
         if (tokens[i] >= c->cfg.vocab_size)
             return set_err(TALOS_ERR_INVALID_ARG, "token %u at %zu out of range (vocab %u)", tokens[i], i,
                            c->cfg.vocab_size);
-    TRY(ensure_graph(c, GM_LOGITS));
+    // positions in steps of 4 through the batched step where it runs the model
+    bool chunked = false;
+    TRY(chunked_ready(c, &chunked));
+    if (!chunked) TRY(ensure_graph(c, GM_LOGITS));
     double* acc = nullptr;  // [nll sum, scored] on the device
     CK(cudaMalloc(&acc, 2 * sizeof(double)));
     talos_status st = TALOS_OK;
     cudaError_t e = cudaMemsetAsync(acc, 0, 2 * sizeof(double), c->stream);
+    const int V = (int)c->cfg.vocab_size;
+    bool first = true;
     // chunks of the context length, each from an empty cache (src/eval.rs:35-52)
     const size_t chunk = c->kv_ctx;
-    for (size_t c0 = 0; e == cudaSuccess && c0 + 1 < n; c0 += chunk) {
+    for (size_t c0 = 0; e == cudaSuccess && st == TALOS_OK && c0 + 1 < n; c0 += chunk) {
         const size_t len = std::min(chunk, n - c0);
         if (len < 2) break;  // a trailing single token predicts nothing
+        if (chunked) {
+            // scored positions 0 .. len-2, MB_SEQ per step, NLLs added in position order
+            for (size_t p0 = 0; e == cudaSuccess && st == TALOS_OK && p0 + 1 < len; p0 += MB_SEQ) {
+                const int k = (int)std::min<size_t>(MB_SEQ, len - 1 - p0);
+                size_t pos[MB_SEQ];
+                for (int j = 0; j < k; ++j) pos[j] = p0 + j;
+                st = batch_step(c, c->bgraph_pf, tokens + c0 + p0, pos, k, first);
+                first = false;
+                for (int j = 0; j < k && st == TALOS_OK && e == cudaSuccess; ++j)
+                    e = launch_token_nll(c->blog + (size_t)j * V, V, tokens[c0 + p0 + j + 1], acc, c->stream);
+            }
+            continue;
+        }
         for (size_t pos = 0; e == cudaSuccess && pos + 1 < len; ++pos) {
             k_set_step<<<1, 1, 0, c->stream>>>(c->step, tokens[c0 + pos], (uint32_t)pos);
             e = cudaGetLastError();
             if (e == cudaSuccess) e = cudaGraphLaunch(c->graph[GM_LOGITS], c->stream);
             if (e == cudaSuccess)
-                e = launch_token_nll(c->logits, (int)c->cfg.vocab_size, tokens[c0 + pos + 1], acc, c->stream);
+                e = launch_token_nll(c->logits, V, tokens[c0 + pos + 1], acc, c->stream);
         }
     }
     double h[2] = {0.0, 0.0};
-    if (e == cudaSuccess) e = cudaMemcpyAsync(h, acc, sizeof h, cudaMemcpyDeviceToHost, c->stream);
-    if (e == cudaSuccess) st = finish_step(c);
+    if (e == cudaSuccess && st == TALOS_OK) e = cudaMemcpyAsync(h, acc, sizeof h, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess && st == TALOS_OK) st = chunked ? batch_finish(c, 0, nullptr) : finish_step(c);
     cudaFree(acc);
     if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "perplexity: %s", cudaGetErrorString(e));
     TRY(st);
