@@ -213,8 +213,9 @@ talos_status talos_prefill(talos_ctx* ctx, const uint32_t* tokens, size_t n, siz
  * logits_out + i * vocab_size (host). Each sequence computes what
  * Model::forward (src/model/llama.rs:85-183) computes for it alone; this is the
  * batched decode of the multi-prompt workload, which the reference runs as
- * separate token-by-token loops (src/main.rs:88-113). No reference counterpart
- * as an entry point.
+ * separate token-by-token loops (src/main.rs:88-113). talos_cap_context and
+ * talos_ctx_set_kv_dtype release the slots (reserve them again afterwards). No
+ * reference counterpart as an entry point.
  */
 #define TALOS_MAX_BATCH 4
 talos_status talos_ctx_set_batch(talos_ctx* ctx, int max_seqs);

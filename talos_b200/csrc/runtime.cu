@@ -528,7 +528,12 @@ static bool expected_shape(const talos_ctx* c, const std::string& name, size_t* 
 
 static size_t kv_elem(const talos_ctx* c) { return c->kv_f16 ? sizeof(__half) : sizeof(float); }
 
+static talos_status batch_free(talos_ctx* c);
+
+// (Re)allocates the cache for c->kv_ctx positions. The batched step's buffers
+// are sized by the cache, so they are released too (talos_ctx_set_batch again).
 static talos_status alloc_kv(talos_ctx* c) {
+    if (c->bmem) TRY(batch_free(c));
     if (c->kcache) cudaFree(c->kcache);
     if (c->vcache) cudaFree(c->vcache);
     if (c->rope_cs) cudaFree(c->rope_cs);

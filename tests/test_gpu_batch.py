@@ -118,3 +118,15 @@ def test_prefill_in_batched_steps(n, pos0):
         assert np.max(np.abs(g - c)) <= 1e-3
         t, pos = oracle.argmax(c), pos + 1
     gpu.close()
+
+
+def test_cap_context_releases_batch_slots():
+    m = Model.load_bytes(tiny_model(gguf.Q4_0))
+    m.ctx.set_batch(2)
+    m.ctx.forward_batch([1, 2], [0, 0])
+    m.cap_context(64)
+    with pytest.raises(TalosError, match="INVALID_ARG"):
+        m.ctx.forward_batch([1, 2], [1, 1])
+    m.ctx.set_batch(2)
+    assert m.ctx.forward_batch([1, 2], [0, 0]).shape == (2, 4096)
+    m.close()
