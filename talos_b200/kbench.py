@@ -25,6 +25,14 @@ Batched decode on the same model:
 
 times K talos_forward_batch steps of N sequences (each at its own position,
 host logits out, wall clock per call) and reports the aggregate tokens/s.
+
+The Llama-3-70B shape (BASELINE config 5's model, all Q4_0, seed 3) on one GPU:
+
+    python -m talos_b200.kbench --llama70b [--model-dir DIR]
+
+writes the 39.7 GB GGUF file to DIR (default /dev/shm; about 95 s), loads it,
+times a 32-token prefill, the per-token decode (device greedy loop, best of
+3 x 48 tokens) and 12 batched steps of 4 sequences, then deletes the file.
 """
 from __future__ import annotations
 
@@ -54,7 +62,11 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--step-kernel", default="auto", choices=["auto", "fused", "layered"])
     ap.add_argument("--batch", type=int, default=0)
+    ap.add_argument("--llama70b", action="store_true")
+    ap.add_argument("--model-dir", default="/dev/shm")
     a = ap.parse_args(argv)
+    if a.llama70b:
+        return llama70b_bench(a)
     if a.batch:
         return batch_bench(a)
     if a.step:
@@ -158,6 +170,56 @@ def batch_bench(a) -> int:
            "ms_per_step": dt / a.steps * 1e3, "tok_s": a.batch * a.steps / dt}
     print(json.dumps(out), flush=True)
     m.close()
+    return 0
+
+
+def llama70b_bench(a) -> int:
+    import shutil
+    import time
+
+    from talos_b200 import Model, build, gguf, synth
+
+    build.build()
+    if shutil.disk_usage(a.model_dir).free < 42e9:
+        print(json.dumps({"kernel": "decode_70b", "skipped": f"under 42 GB free in {a.model_dir}"}))
+        return 0
+    path = os.path.join(a.model_dir, "talos_kbench_llama70b_q4_0.gguf")
+    shape = synth.with_ctx(synth.LLAMA3_70B, 1024)
+    t = time.time()
+    synth.write_llama(path, shape, 3, wtype=gguf.Q4_0)
+    gen = time.time() - t
+    try:
+        t = time.time()
+        m = Model.load(path, device=a.device, max_ctx=1024)
+        load = time.time() - t
+        prompt = synth.token_ids(3, 32, shape.vocab)
+        t = time.perf_counter()
+        last = m.prefill(prompt, 0)
+        pf = time.perf_counter() - t
+        tok = int(np.argmax(last))
+        m.generate_greedy(tok, 32, 4)
+        best = 1e9
+        for _ in range(3):
+            t = time.perf_counter()
+            m.generate_greedy(tok, 36, 48)
+            best = min(best, (time.perf_counter() - t) / 48)
+        algo = 39_099_994_624  # weight bytes per token (all Q4_0 matrices + norms + one embedding row)
+        m.ctx.set_batch(4)
+        toks, pos = [1, 2, 3, 4], [100, 200, 300, 400]
+        for i in range(2):
+            m.ctx.forward_batch(toks, [p + i for p in pos])
+        t = time.perf_counter()
+        for i in range(12):
+            lg = m.ctx.forward_batch(toks, [p + 2 + i for p in pos])
+            toks = [int(np.argmax(r)) for r in lg]
+        bt = (time.perf_counter() - t) / 12
+        m.close()
+    finally:
+        os.remove(path)
+    out = {"kernel": "decode_70b", "step_kernel": "fused", "model_gen_s": gen, "load_s": load,
+           "prefill_32_ms": pf * 1e3, "decode_ms_per_token": best * 1e3, "decode_tok_s": 1 / best,
+           "algo_gbs": algo / best / 1e9, "batch4_ms_per_step": bt * 1e3, "batch4_tok_s": 4 / bt}
+    print(json.dumps(out), flush=True)
     return 0
 
 
