@@ -1903,8 +1903,9 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
                     find_seg(m, t, si, lt);
                     for (int c = 0; c < nchunk; ++c, ++pc) {
                         // Past the first a.prefetch chunks, wait until the consumers have
-                        // staged this phase's input: its loads then meet no queue of
-                        // weight copies in this SM's memory path at the phase start.
+                        // staged this phase's input. The host passes the ring size, so
+                        // the whole ring fills across the phase boundary (measured best);
+                        // a smaller value keeps the staging loads ahead of weight copies.
                         if (pc == a.prefetch && !smem_wait_geq_sleep(&sh.staged, p)) {
                             ok = false;
                             break;
