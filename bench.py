@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Decode benchmark for the Talos B200 path.
+"""Decode benchmark for the Talos B200 path (the Mistral-7B-shape Q4_0 model).
 
 Workload: Mistral-7B-shaped Llama (d 4096, 32 layers, 32/8 heads, ff 14336,
 vocab 32000, RoPE theta 1e6), random N(0, 0.02) weights from seed 1, Q4_0 with

@@ -1,6 +1,6 @@
 """Kernel microbenchmarks.
 
-Matvec:
+Matvec microbenchmark:
 
     python -m talos_b200.kbench [--type q4_0|q8_0|q6_k|f32] [--rows R] [--cols C]
                                 [--copies N] [--reps K] [--warmup W]
@@ -26,7 +26,7 @@ Batched decode on the same model:
 times K talos_forward_batch steps of N sequences (each at its own position,
 host logits out, wall clock per call) and reports the aggregate tokens/s.
 
-The Llama-3-70B shape (BASELINE config 5's model, all Q4_0, seed 3) on one GPU:
+The Llama-3-70B shape (the 70B benchmark model: all Q4_0, seed 3) on one GPU:
 
     python -m talos_b200.kbench --llama70b [--model-dir DIR]
 

@@ -102,7 +102,8 @@ class Shape:
         return self.n_head_kv * self.head_dim
 
 
-# BASELINE configurations (shape only; dtypes are chosen per model).
+# Benchmark model shapes (dtypes are chosen per model): the tiny Llama, the
+# Mistral-7B shape and the Llama-3-70B shape.
 TINY = Shape(n_embd=288, n_layer=6, n_head=6, n_head_kv=2, n_ff=768, vocab=4096, ctx=256)
 MISTRAL_7B = Shape(n_embd=4096, n_layer=32, n_head=32, n_head_kv=8, n_ff=14336, vocab=32000, ctx=4096,
                    rope_base=1e6)

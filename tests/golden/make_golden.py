@@ -10,7 +10,7 @@ fixed numbers and the CPU suite notices any drift of the oracle or of the
 synthetic-input generator (each fixture stores the sha256 of its input bytes).
 
 Fixtures (all inputs are regenerated from seeds, only outputs are stored):
-  tiny_{f32,q8_0,q4_0}.npz   BASELINE configs 1/2: tiny Llama seed 42, 16-token
+  tiny_{f32,q8_0,q4_0}.npz   the tiny Llama benchmark models, seed 42, 16-token
                              prompt (seed 42), 64 greedy tokens, logits after the
                              prompt and after the last greedy step.
   matvec4096_{q4_0,q8_0}.npz config 3: 4096x4096 N(0,0.02) seed 7, x N(0,1);

@@ -1,5 +1,5 @@
 """Shared builders for the parity tests: the reference's self-contained synthetic
-models (tests/gqa.rs, tests/forward_gpu.rs) and the BASELINE shapes."""
+models (tests/gqa.rs, tests/forward_gpu.rs) and the benchmark shapes."""
 from __future__ import annotations
 
 import numpy as np
@@ -109,7 +109,7 @@ def forward_gpu_model(seed: int = 0) -> bytes:
 
 
 def tiny_model(wtype: int) -> bytes:
-    """BASELINE config 1/2: tiny Llama, N(0, 0.02) seed 42; every 2-D weight in wtype."""
+    """The tiny Llama benchmark model: N(0, 0.02) seed 42; every 2-D weight in wtype."""
     return synth.llama_bytes(synth.TINY, 42, wtype=wtype)
 
 

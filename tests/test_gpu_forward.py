@@ -1,6 +1,6 @@
 """Whole decode steps on the GPU against the oracle's CPU forward.
 
-Bars (BASELINE north star): greedy tokens identical; logits within 1e-4 max-abs
+Bars: greedy tokens identical; logits within 1e-4 max-abs
 for F32 weights and 1e-3 max-abs for quantized weights; a re-run is bit-identical
 (tests/forward_gpu.rs:183-190). The step tests run both ways a step can be
 launched: the per-token kernel ("fused") and the layered kernel graph.
@@ -102,13 +102,13 @@ def greedy_parity(data, n_prompt, n_gen, tol, seed=42, sk="auto"):
     return max_err, min_gap
 
 
-def test_tiny_f32_greedy_parity(sk):
+def test_tiny_f32_greedy_parity(sk):  # the tiny F32 benchmark model
     err, gap = greedy_parity(tiny_model(gguf.F32), 16, 64, 1e-4, sk=sk)
     print(f"tiny F32: max abs err {err:.2e}, min top-2 gap {gap:.2e}")
 
 
 @pytest.mark.parametrize("wtype", [gguf.Q4_0, gguf.Q8_0])
-def test_tiny_quant_greedy_parity(wtype, sk):
+def test_tiny_quant_greedy_parity(wtype, sk):  # the tiny quantized benchmark models
     err, gap = greedy_parity(tiny_model(wtype), 16, 64, 1e-3, sk=sk)
     print(f"tiny {gguf.TYPE_NAMES[wtype]}: max abs err {err:.2e}, min top-2 gap {gap:.2e}")
 
@@ -205,7 +205,7 @@ def test_reupload_replaces_weights(second):
 @pytest.mark.slow
 @pytest.mark.parametrize("step_kernel", ["fused", "layered"])
 def test_mistral_7b_shape_parity(tmp_path, step_kernel):
-    """BASELINE config 4 at full size: Q4_0 + Q6_K output; a short prompt and
+    """The Mistral-7B-shape benchmark model at full size: Q4_0 + Q6_K output; a short prompt and
     greedy steps against the oracle (the CPU forward reads 4 GB per token)."""
     path = str(tmp_path / "m7b.gguf")
     synth.write_llama(path, synth.with_ctx(synth.MISTRAL_7B, 64), 1, wtype=gguf.Q4_0, out_type=gguf.Q6_K)

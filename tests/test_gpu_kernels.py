@@ -89,7 +89,7 @@ def test_matvec_q6_k(rows, cols):
 
 @pytest.mark.parametrize("gtype", [gguf.Q4_0, gguf.Q8_0])
 def test_matvec_4096_microbench_shape(gtype):
-    # W N(0, 0.02) seed 7, x N(0, 1), 4096 x 4096.
+    # The 4096 x 4096 microbenchmark case: W N(0, 0.02) seed 7, x N(0, 1).
     raw = synth.tensor(7, "bench.w", 4096, 4096, gtype)
     x = synth.normal(7, "bench.x", 4096, 1.0)
     gpu = model.matvec(gtype, raw, x, 4096, 4096)
