@@ -339,7 +339,17 @@ class Model:
         return self.ctx.perplexity(tokens)[0]
 
     def prefill(self, tokens, pos0: int = 0):
+        """src/main.rs:88-95 in one call: the logits after the last prompt token."""
         return self.ctx.prefill(tokens, pos0)
+
+    def set_batch(self, max_seqs: int):
+        """Cache slots for up to 4 sequences decoded together (0 frees them)."""
+        self.ctx.set_batch(max_seqs)
+
+    def forward_batch(self, tokens, positions) -> np.ndarray:
+        """One step for sequences 0 .. n-1: token i at positions[i] in slot i;
+        [n, vocab_size] logits (each row what forward_gpu gives that sequence alone)."""
+        return self.ctx.forward_batch(tokens, positions)
 
 
 # ----------------------------------------------------------------- kernel entry points
