@@ -49,6 +49,10 @@ import numpy as np  # noqa: E402
 W_BYTES_7B = 6979321856 * 18 // 32 + 131072000 * 210 // 256 + 65 * 4096 * 4 + 4096 // 32 * 18
 KV_BYTES_PER_POS = 2 * 32 * 1024 * 4  # K and V rows read per cached position (f32)
 GATEUP_BYTES = 2 * 14336 * 4096 * 18 // 32 + 4096 * 4 * 2 + 14336 * 4  # weights + x + norm + out
+# DRAM bytes (read + write) of one k_token launch on the 7B shape, from the ncu
+# capture summarised in profiles/k_token_m7b.md (a 2-layer capture scaled to 32
+# layers: the output projection once plus 32 x the per-layer bytes).
+K_TOKEN_TRAFFIC = 4_140_000_000
 PROMPT_LEN = 128
 MODEL_SEED = 1
 PROMPT_SEED = 1
@@ -155,87 +159,60 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
-def profiled_traffic(summary: str):
-    """DRAM bytes per launch of the dominant kernel from its committed ncu summary
-    (the `traffic_bytes_per_launch:` line of profiles/<summary>)."""
-    p = os.path.join(ROOT, "profiles", summary)
-    try:
-        for line in open(p):
-            if line.startswith("traffic_bytes_per_launch:"):
-                return int(line.split(":")[1].strip())
-    except OSError:
-        pass
-    return None
-
-
-def cpu_decode_sample(path: str, budget_s: float, max_tokens: int):
-    """Time the oracle's CPU forward (all host threads) on decode tokens of the
-    same model; returns (tok/s, tokens, threads, seconds)."""
+def cpu_decode(path: str, warmup: int, steps: int, budget_s: float):
+    """The reference's decode loop (src/main.rs:88-113) through the oracle's CPU
+    forward on all host threads: the 128-token prompt fed token by token
+    (untimed), `warmup` greedy steps (untimed), then up to `steps` timed greedy
+    steps, stopping early once `budget_s` seconds have passed. The timed steps sit
+    at the positions the GPU arm times (PROMPT_LEN + warmup onwards). Returns
+    (tok/s, steps timed, threads, seconds, first timed position)."""
     import oracle
+    from talos_b200 import synth
 
     oracle.build()
     threads = max(1, len(os.sched_getaffinity(0)))
     oracle.set_threads(threads)
     m = oracle.Model(path=path)
-    from talos_b200 import synth
-
-    toks = synth.token_ids(PROMPT_SEED, max_tokens, m.cfg.vocab_size)
-    m.forward(toks[0], 0)  # warm the page cache / thread pool (untimed)
-    m.reset()
-    n, t0 = 0, time.perf_counter()
-    while n < max_tokens:
-        m.forward(toks[n], n)
+    prompt = synth.token_ids(PROMPT_SEED, PROMPT_LEN, m.cfg.vocab_size)
+    lg = None
+    for i, t in enumerate(prompt):
+        lg = m.forward(t, i)
+    tok, pos = argmax_last(lg), PROMPT_LEN
+    for _ in range(warmup):
+        tok = argmax_last(m.forward(tok, pos))
+        pos += 1
+    pos0, n, t0 = pos, 0, time.perf_counter()
+    while n < steps:
+        tok = argmax_last(m.forward(tok, pos))
+        pos += 1
         n += 1
         if time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
     m.close()
-    return n / dt, n, threads, dt
+    return n / dt, n, threads, dt, pos0
 
 
 def run_reference(args):
     """--impl reference: the CPU restatement of the reference's forward on this
-    host's cores, each step one decode token of the same workload."""
+    host's cores, on the GPU arm's workload: the same 128-token prompt (fed
+    untimed), the same warm-up steps, then timed greedy decode steps at the same
+    positions."""
     rank = env_int("RANK", 0)
     if rank != 0:
         return 0
-    from talos_b200 import synth
-
     ensure_model(model_path())
-    import oracle
-
-    oracle.build()
-    threads = max(1, len(os.sched_getaffinity(0)))
-    oracle.set_threads(threads)
-    m = oracle.Model(path=model_path())
-    toks = synth.token_ids(PROMPT_SEED, PROMPT_LEN, m.cfg.vocab_size)
-    # A bounded workload sample: the prompt is not replayed; decode steps start at
-    # position 0 (the CPU cost of a token is dominated by its 4.03 GB of weights).
     budget = float(os.environ.get("TALOS_REF_BUDGET_S", "150"))
-    warm = min(args.warmup, 1)
-    pos = 0
-    for i in range(warm):
-        m.forward(toks[i], pos)
-        pos += 1
-    n, t0 = 0, time.perf_counter()
-    tok = toks[warm % len(toks)]
-    while n < args.steps:
-        lg = m.forward(tok, pos)
-        tok = argmax_last(lg)
-        pos += 1
-        n += 1
-        if time.perf_counter() - t0 > budget:
-            break
-    dt = time.perf_counter() - t0
-    v = n / dt
-    sample = (f"{n} greedy decode tokens (positions {warm}..{warm + n - 1}) of the 7B-shape Q4_0/Q6_K model, "
-              f"{threads} threads; steps capped at {budget:.0f} s of CPU time")
+    v, n, threads, dt, pos0 = cpu_decode(model_path(), args.warmup, args.steps, budget)
+    sample = (f"128-token prompt fed untimed, {args.warmup} untimed greedy steps, then {n} timed greedy decode "
+              f"tokens (positions {pos0}..{pos0 + n - 1}) of the 7B-shape Q4_0/Q6_K model, {threads} threads; "
+              f"timed steps capped at {budget:.0f} s of CPU time")
     line = {
         "metric": "decode tok/s (batch 1, 7B-shape Q4_0)", "value": v, "unit": "tok/s", "impl": "reference",
-        "n_gpus": args.gpus, "steps": n, "steps_requested": args.steps, "warmup": warm,
+        "n_gpus": args.gpus, "steps": n, "steps_requested": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000 * dt / max(n, 1), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "q4_0 weights, f32 activations/KV", "data": "synthetic",
-        "config": bench_config(args.gpus, PROMPT_LEN + warm + n),
+        "config": bench_config(args.gpus, PROMPT_LEN + args.warmup + args.steps),
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -364,23 +341,24 @@ def main():
         dom_bytes = W_BYTES_7B + KV_BYTES_PER_POS * (prof_pos + 1)
         dom_ms = step_ms
         dom_name = "k_token (whole decode step: 32 layers + output, one launch)"
-        traffic = profiled_traffic("k_token_m7b.md")
+        traffic = K_TOKEN_TRAFFIC
         launches = 2  # k_token + the greedy-advance kernel
     else:
         dom_bytes = GATEUP_BYTES
         dom_ms = tot_ms["gateup"] / max(tot_n["gateup"], 1)
         dom_name = "gateup (RMSNorm + gate/up Q4_0 matvec + SwiGLU)"
-        traffic = profiled_traffic("gateup_q4_0_m7b.md")
+        traffic = None  # no ncu capture of the layered graph's gate/up kernel
         launches = sum(tot_n.values()) // n_prof + 1  # + the greedy-advance kernel
     achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
 
     # ---------------- CPU baseline (rank 0 at N=1 only)
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        v, n, thr, dt = cpu_decode_sample(path, budget_s=20.0, max_tokens=12)
+        v, n, thr, dt, p0 = cpu_decode(path, W, min(K, 12), budget_s=20.0)
         cpu = {"value": v, "unit": "tok/s", "cores": thr, "kind": "port",
-               "sample": f"{n} decode tokens (positions 0..{n - 1}) of the same 7B-shape model through the "
-                         f"oracle's CPU forward, {dt:.1f} s"}
+               "sample": f"128-token prompt and {W} greedy steps untimed, then {n} timed greedy decode tokens "
+                         f"(positions {p0}..{p0 + n - 1}, the GPU arm's first timed positions) of the same "
+                         f"7B-shape model through the oracle's CPU forward, {dt:.1f} s"}
 
     tok_bytes = W_BYTES_7B + KV_BYTES_PER_POS * kv_avg_pos
     ms_step = ms / K

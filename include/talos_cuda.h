@@ -4,8 +4,8 @@
  * This library replaces the Apple-Metal twin of Talos's CPU forward pass
  * (Tsuskov/talos, Rust). Each entry point names the reference interface it
  * stands in for. The Rust side binds these symbols from a `cuda` cargo feature
- * that mirrors the existing `metal` feature (Cargo.toml:28-31); the binding
- * a maintainer adds is shown in INTEGRATION.md.
+ * that mirrors the existing `metal` feature (Cargo.toml:28-31), with one
+ * `extern "C"` declaration per entry point below.
  *
  * Conventions
  *  - Every call returns a talos_status; talos_last_error() gives the message of
@@ -282,6 +282,16 @@ talos_status talos_profile_phases(talos_ctx* ctx, uint32_t token, size_t pos, ui
 talos_status talos_dequant(int ggml_type, const void* bytes, size_t n_elems, float* out);
 
 /*
+ * Greedy choice over n logits (host) on the current CUDA device:
+ * sample::argmax (src/sample.rs:7-14), the maximum under f32::total_cmp
+ * (-NaN < -inf < ... < -0.0 < +0.0 < ... < +inf < +NaN) and the LAST maximal
+ * index on ties. The decode step's own argmax (talos_generate_greedy, the
+ * logits epilogue) uses the same key. n must be 1 .. 2^32-1 (the reference
+ * panics on empty logits).
+ */
+talos_status talos_argmax(const float* logits, size_t n, uint32_t* index_out);
+
+/*
  * One fused dequant-matvec y = W x on device `device`, with W uploaded for this
  * call only. math::metal::matvec_f32 / matvec_quant
  * (src/math/metal/mod.rs:195-225). x: cols floats, y: rows floats (host).
@@ -328,8 +338,10 @@ talos_status talos_matvec_dev(const talos_weight* w, const float* x_dev, float* 
  * address (cudaGetSymbolAddress); make it before any stream capture. Calls
  * share the scratch: two calls in flight at once (other streams, other
  * threads) race, so serialise them. Results agree with talos_matvec_dev to
- * rounding (another summation order) and are identical call to call. No
- * reference counterpart.
+ * rounding (another summation order) and are identical call to call. Every
+ * device wait is bounded (2 s): a 16-row tile any of whose K slices gave up
+ * waiting for its weight copy comes out as 16 NaN rows (the call itself still
+ * returns TALOS_OK, since it does not synchronise). No reference counterpart.
  */
 talos_status talos_matvec_dev_noalloc(const talos_weight* w, const float* x_dev, float* y_dev, void* stream);
 

@@ -58,6 +58,7 @@ SIGNATURES = {
     "talos_profile_step": (_i, [_vp, _u32, _sz, _vp, _vp]),
     "talos_profile_phases": (_i, [_vp, _u32, _sz, _vp, _sz, C.POINTER(_i), C.POINTER(_i)]),
     "talos_dequant": (_i, [_i, _vp, _sz, _vp]),
+    "talos_argmax": (_i, [_vp, _sz, C.POINTER(C.c_uint32)]),
     "talos_matvec": (_i, [_i, _i, _vp, _sz, _sz, _sz, _vp, _vp]),
     "talos_matvec_resident": (_i, [_vp, C.c_char_p, _i, _vp, _sz, _sz, _sz, _vp, _vp]),
     "talos_weight_create": (_i, [_i, _i, _vp, _sz, _sz, _sz, C.POINTER(_vp)]),

@@ -117,6 +117,14 @@ __device__ __forceinline__ uint32_t total_order_key(float f) {
     return (uint32_t)b ^ 0x80000000u;
 }
 
+// Argmax key of value v at index i: (total-order key << 32) | i. The largest key
+// is the maximum under f32::total_cmp and, among equal values, the LAST index,
+// which is what sample::argmax's max_by keeps (src/sample.rs:7-14). Keys combine
+// with max / atomicMax in any order.
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t i) {
+    return ((unsigned long long)total_order_key(v) << 32) | i;
+}
+
 __device__ __forceinline__ float ld_half_bytes(const uint8_t* p) {
     return __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
 }

@@ -381,6 +381,32 @@ cudaError_t launch_token_nll(const float* logits, int n, uint32_t target, double
     return cudaGetLastError();
 }
 
+// sample::argmax (src/sample.rs:7-14) over n values: the largest argmax_key, the
+// same key the logits epilogues of the decode step reduce.
+__global__ void k_argmax(const float* v, size_t n, unsigned long long* key) {
+    unsigned long long best = 0ull;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const unsigned long long k = argmax_key(v[i], (uint32_t)i);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long oth = __shfl_xor_sync(0xffffffffu, best, o);
+        best = oth > best ? oth : best;
+    }
+    if ((threadIdx.x & 31) == 0) atomicMax(key, best);
+}
+
+cudaError_t launch_argmax(const float* v, size_t n, unsigned long long* key, cudaStream_t s) {
+    size_t blocks = (n + 255) / 256;
+    if (blocks > 1184) blocks = 1184;
+    if (blocks == 0) blocks = 1;
+    cudaError_t e = cudaMemsetAsync(key, 0, sizeof(unsigned long long), s);
+    if (e != cudaSuccess) return e;
+    k_argmax<<<(unsigned)blocks, 256, 0, s>>>(v, n, key);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_greedy_advance(StepParams* step, uint32_t* gen, int cap, cudaStream_t s, bool pdl) {
     return launch_ex(k_greedy_advance, dim3(1), dim3(1), 0, s, pdl, 1, step, gen, cap);
 }

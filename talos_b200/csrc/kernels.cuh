@@ -167,6 +167,9 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, flo
 // acc[0] += the negative log-likelihood logits[0..n) give `target` (f64 log-sum-exp),
 // acc[1] += 1 (src/eval.rs:18-23).
 cudaError_t launch_token_nll(const float* logits, int n, uint32_t target, double* acc, cudaStream_t s);
+// *key = the largest argmax_key of v[0..n) (sample::argmax, src/sample.rs:7-14);
+// the index is its low 32 bits.
+cudaError_t launch_argmax(const float* v, size_t n, unsigned long long* key, cudaStream_t s);
 // Greedy feedback: token = argmax, append it to gen[], pos += 1.
 cudaError_t launch_greedy_advance(StepParams* step, uint32_t* gen, int gen_cap, cudaStream_t s, bool pdl);
 

@@ -652,7 +652,7 @@ __device__ __forceinline__ void apply_epilogue(const MatvecArgs& a, const Seg& s
                 const int row = 16 * lt + lane;
                 if (row < sg.out_rows) {
                     sg.out[row] = a.epi == EPI_ADD ? __fadd_rn(pre.xres, res[lane]) : res[lane];
-                    key = ((unsigned long long)total_order_key(res[lane]) << 32) | (unsigned)row;
+                    key = argmax_key(res[lane], (uint32_t)row);
                 }
             }
             if (a.epi == EPI_LOGITS) {  // running argmax (src/sample.rs:7-14)
@@ -1856,7 +1856,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
                     if (lane < 16 && row < sg.out_rows) {
                         const int g = a.vocab_off + row;
                         for (int r = 0; r < a.tp; ++r) a.plogits[r][g] = res[lane];
-                        key = ((unsigned long long)total_order_key(res[lane]) << 32) | (unsigned)g;
+                        key = argmax_key(res[lane], (uint32_t)g);
                     }
 #pragma unroll
                     for (int o = 8; o > 0; o >>= 1) {
@@ -2108,7 +2108,10 @@ __global__ void __launch_bounds__(MV_CONSUMERS, 1)
     if (tid < 16) {
         float v = 0.f;
         for (int q = 0; q < MV_CWARPS; ++q) v += red[q * 16 + tid];
-        part[((size_t)tile * nslice + slice) * 16 + tid] = v;
+        // a slice whose copy wait expired covers only part of its chunks: its
+        // partials are NaN, so the tile's rows come out NaN whichever slice the
+        // wait expired in (the CTA that adds the slices sees only its own flag)
+        part[((size_t)tile * nslice + slice) * 16 + tid] = sok ? v : __int_as_float(0x7fc00000);
     }
     __threadfence();
     __syncthreads();
@@ -2125,7 +2128,7 @@ __global__ void __launch_bounds__(MV_CONSUMERS, 1)
     float v = 0.f;
     for (int q = 0; q < nslice; ++q) v += __ldcg(part + ((size_t)tile * nslice + q) * 16 + tid);
     const int row = 16 * tile + tid;
-    if (row < w.rows) y[row] = sok ? v : __int_as_float(0x7fc00000);  // NaN rows: a copy timed out
+    if (row < w.rows) y[row] = sok ? v : __int_as_float(0x7fc00000);  // NaN rows: some slice's copy timed out
 }
 
 size_t noalloc_smem_bytes(int type, int K) {

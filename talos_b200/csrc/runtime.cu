@@ -401,6 +401,7 @@ struct talos_ctx {
     void* arena = nullptr;
     size_t arena_bytes = 0;
     float *x = nullptr, *q = nullptr, *att = nullptr, *ff = nullptr, *logits = nullptr, *hidden = nullptr;
+    double* nll_acc = nullptr;  // talos_perplexity: [NLL sum, positions scored]
     StepParams* step = nullptr;
     uint32_t* gen = nullptr;
     // KV + RoPE table
@@ -580,7 +581,7 @@ static talos_status alloc_arena(talos_ctx* c) {
     };
     size_t o_x = take(E * 4), o_q = take(E * 4 + 64), o_att = take(E * 4), o_ff = take(F * 4),
            o_log = take(V * 4), o_hid = take(E * 4), o_step = take(sizeof(StepParams)), o_xb0 = take(E * 4),
-           o_xb1 = take(E * 4);
+           o_xb1 = take(E * 4), o_nll = take(2 * sizeof(double));
     CK(cudaMalloc(&c->arena, off));
     CK(cudaMemsetAsync(c->arena, 0, off, c->stream));
     c->arena_bytes = off;
@@ -594,6 +595,7 @@ static talos_status alloc_arena(talos_ctx* c) {
     c->step = (StepParams*)(b + o_step);
     c->xbuf[0] = (float*)(b + o_xb0);
     c->xbuf[1] = (float*)(b + o_xb1);
+    c->nll_acc = (double*)(b + o_nll);
     CK(cudaMallocHost(&c->h_out, (V > E ? V : E) * sizeof(float)));
     CK(cudaMallocHost(&c->h_step, sizeof(StepParams)));
     CK(cudaStreamSynchronize(c->stream));
@@ -1939,8 +1941,7 @@ extern "C" talos_status talos_perplexity(talos_ctx* c, const uint32_t* tokens, s
     bool chunked = false;
     TRY(chunked_ready(c, &chunked));
     if (!chunked) TRY(ensure_graph(c, GM_LOGITS));
-    double* acc = nullptr;  // [nll sum, scored] on the device
-    CK(cudaMalloc(&acc, 2 * sizeof(double)));
+    double* acc = c->nll_acc;  // [nll sum, scored] on the device, cleared on the stream
     talos_status st = TALOS_OK;
     cudaError_t e = cudaMemsetAsync(acc, 0, 2 * sizeof(double), c->stream);
     const int V = (int)c->cfg.vocab_size;
@@ -1974,7 +1975,6 @@ extern "C" talos_status talos_perplexity(talos_ctx* c, const uint32_t* tokens, s
     double h[2] = {0.0, 0.0};
     if (e == cudaSuccess && st == TALOS_OK) e = cudaMemcpyAsync(h, acc, sizeof h, cudaMemcpyDeviceToHost, c->stream);
     if (e == cudaSuccess && st == TALOS_OK) st = chunked ? batch_finish(c, 0, nullptr) : finish_step(c);
-    cudaFree(acc);
     if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "perplexity: %s", cudaGetErrorString(e));
     TRY(st);
     *ppl_out = (float)exp(h[0] / h[1]);
@@ -2080,6 +2080,28 @@ extern "C" talos_status talos_dequant(int type, const void* bytes, size_t n, flo
     cudaFree(d_raw);
     if (d_out) cudaFree(d_out);
     if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "dequant: %s", cudaGetErrorString(e));
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_argmax(const float* logits, size_t n, uint32_t* index_out) {
+    if (!logits || !index_out) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    if (n == 0) return set_err(TALOS_ERR_INVALID_ARG, "argmax of no logits");
+    if (n > 0xffffffffull) return set_err(TALOS_ERR_INVALID_ARG, "%zu logits: indices are 32-bit", n);
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    TRY(device_setup(dev));
+    float* d_v = nullptr;
+    unsigned long long* d_key = nullptr;
+    CK(cudaMalloc(&d_v, n * 4));
+    cudaError_t e = cudaMalloc(&d_key, sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemcpy(d_v, logits, n * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = launch_argmax(d_v, n, d_key, 0);
+    unsigned long long key = 0ull;
+    if (e == cudaSuccess) e = cudaMemcpy(&key, d_key, sizeof key, cudaMemcpyDeviceToHost);
+    cudaFree(d_v);
+    if (d_key) cudaFree(d_key);
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "argmax: %s", cudaGetErrorString(e));
+    *index_out = (uint32_t)(key & 0xffffffffull);
     return TALOS_OK;
 }
 

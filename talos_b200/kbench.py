@@ -47,6 +47,12 @@ TYPES = {"f32": 0, "q4_0": 2, "q8_0": 8, "q6_k": 14}
 ALGO_BYTES_PER_ELEM = {0: 4.0, 2: 18 / 32, 8: 34 / 32, 14: 210 / 256}
 
 
+def argmax_last(v) -> int:
+    """sample::argmax (src/sample.rs:7-14): the last maximal element on ties."""
+    v = np.asarray(v)
+    return int(v.size - 1 - np.argmax(v[::-1]))
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--type", default="q4_0", choices=sorted(TYPES))
@@ -126,7 +132,7 @@ def step_bench(a) -> int:
     del data
     prompt = synth.token_ids(1, 16, shape.vocab)
     last = m.prefill(prompt, 0)
-    tok = int(np.argmax(last))
+    tok = argmax_last(last)
     m.generate_greedy(tok, 16, 2)
     stream = torch.cuda.ExternalStream(m.ctx.stream(), device=torch.device("cuda", a.device))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -164,7 +170,7 @@ def batch_bench(a) -> int:
     t0 = time.perf_counter()
     for i in range(a.steps):
         lg = m.ctx.forward_batch(toks, [p + 3 + i for p in pos])
-        toks = [int(np.argmax(r)) for r in lg]
+        toks = [argmax_last(r) for r in lg]
     dt = time.perf_counter() - t0
     out = {"kernel": "decode_batch", "batch": a.batch, "layers": a.layers, "steps": a.steps,
            "ms_per_step": dt / a.steps * 1e3, "tok_s": a.batch * a.steps / dt}
@@ -196,7 +202,7 @@ def llama70b_bench(a) -> int:
         t = time.perf_counter()
         last = m.prefill(prompt, 0)
         pf = time.perf_counter() - t
-        tok = int(np.argmax(last))
+        tok = argmax_last(last)
         m.generate_greedy(tok, 32, 4)
         best = 1e9
         for _ in range(3):
@@ -211,7 +217,7 @@ def llama70b_bench(a) -> int:
         t = time.perf_counter()
         for i in range(12):
             lg = m.ctx.forward_batch(toks, [p + 2 + i for p in pos])
-            toks = [int(np.argmax(r)) for r in lg]
+            toks = [argmax_last(r) for r in lg]
         bt = (time.perf_counter() - t) / 12
         m.close()
     finally:

@@ -362,6 +362,15 @@ def dequant(gtype: int, raw, n_elems: int) -> np.ndarray:
     return out
 
 
+def argmax(logits) -> int:
+    """talos_argmax: sample::argmax (src/sample.rs:7-14) on the GPU, total order,
+    last maximal index on ties."""
+    v = np.ascontiguousarray(logits, np.float32)
+    out = C.c_uint32()
+    _lib.check(_lib.load().talos_argmax(_ptr(v), v.size, C.byref(out)))
+    return int(out.value)
+
+
 def matvec(gtype: int, raw, x, rows: int, cols: int, device: int = 0) -> np.ndarray:
     """talos_matvec: one fused dequant-matvec (math::metal::matvec_quant twin)."""
     buf = np.ascontiguousarray(np.frombuffer(raw, np.uint8) if not isinstance(raw, np.ndarray) else raw.view(np.uint8))

@@ -44,7 +44,7 @@ def _rank(rank, world, data, toks, n_gen, q_id, q_out):
             uid = q_id.get(timeout=120)
         m = Model.load_bytes(data, device=rank, tp_size=world, tp_rank=rank, nccl_id=uid)
         logits = [m.forward_gpu(int(t), pos) for pos, t in enumerate(toks)]
-        first = int(np.argmax(logits[-1]))  # ties are not expected on random logits
+        first = oracle.argmax(logits[-1])  # sample::argmax: the last maximum on ties
         gen = m.generate_greedy(first, len(toks), n_gen) if n_gen else np.zeros(0, np.uint32)
         q_out.put((rank, np.stack(logits), [int(t) for t in gen], None))
         m.close()

@@ -4,11 +4,15 @@ also runs it after every other test; it passes alone as well.
 
 Checks: two calls in a row give identical results (the per-tile arrival
 counters are back at zero after each call) that agree with talos_matvec_dev,
-the existing entry point, to rounding; weights over the scratch's row limit are
+the existing entry point, to rounding, and with the CPU oracle's
+quant::matvec / matmul::matvec (src/math/quant.rs:18-51, src/math/matmul.rs:34-47)
+within the reference's GPU tolerance |gpu - cpu| <= 1e-3 * max(|cpu|, 1)
+(src/math/metal/mod.rs:527-531); weights over the scratch's row limit are
 refused."""
 import numpy as np
 import pytest
 
+import oracle
 from talos_b200 import Weight, synth
 from talos_b200._lib import TalosError
 
@@ -34,6 +38,12 @@ def test_noalloc_matches_matvec_dev_twice(gtype, rows, cols):
     assert np.array_equal(b, c), "second call differs from the first"
     assert np.all(np.isfinite(b))
     assert np.max(np.abs(b - a)) <= 1e-3
+    if gtype == 0:
+        cpu = oracle.matvec_f32(raw.view(np.float32), x, rows, cols)
+    else:
+        cpu = oracle.matvec_quant(raw, gtype, x, rows, cols)
+    err = np.abs(b - cpu) / np.maximum(np.abs(cpu), 1.0)
+    assert err.max() <= 1e-3, f"max rel err vs oracle {err.max():.3e}"
 
 
 def test_noalloc_refuses_rows_over_the_scratch():
