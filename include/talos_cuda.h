@@ -195,8 +195,9 @@ talos_status talos_generate_greedy(talos_ctx* ctx, uint32_t token, size_t pos, s
  * Feed `n` prompt tokens at positions pos0 .. pos0+n-1 (the prefill loop of
  * src/main.rs:88-95) and write the logits after the last one to `last_logits`
  * (host, may be NULL). On one GPU with an f32 cache and Q4_0 / Q8_0 / Q6_K
- * matrices the prompt goes through the batched step, 4 consecutive positions
- * per weight pass; otherwise one token per step.
+ * matrices the prompt goes through the batched step, up to 128 consecutive
+ * positions per weight pass on the tensor cores (each position attends to the
+ * ones before it, as token-by-token feeding does); otherwise one token per step.
  */
 talos_status talos_prefill(talos_ctx* ctx, const uint32_t* tokens, size_t n, size_t pos0,
                            float* last_logits);
@@ -204,8 +205,9 @@ talos_status talos_prefill(talos_ctx* ctx, const uint32_t* tokens, size_t n, siz
 /*
  * Batched decode: up to TALOS_MAX_BATCH independent sequences per step, each
  * with its own KV cache slot and position; every weight is read once per step
- * for all of them. talos_ctx_set_batch reserves `max_seqs` cache slots (0
- * frees them; reserving empties them) for the context's model, which must have
+ * for all of them (a tensor-core GEMM). talos_ctx_set_batch reserves
+ * `max_seqs` cache slots of the context's current context length each (0 frees
+ * them; reserving empties them) for the context's model, which must have
  * Q4_0 / Q8_0 / Q6_K matrices and head_dim <= 128 (TALOS_ERR_UNSUPPORTED
  * otherwise, and under tensor parallelism). talos_forward_batch runs one step
  * for sequences 0 .. n-1 (n <= max_seqs): sequence i feeds tokens[i] at
@@ -217,7 +219,7 @@ talos_status talos_prefill(talos_ctx* ctx, const uint32_t* tokens, size_t n, siz
  * talos_ctx_set_kv_dtype release the slots (reserve them again afterwards). No
  * reference counterpart as an entry point.
  */
-#define TALOS_MAX_BATCH 4
+#define TALOS_MAX_BATCH 64
 talos_status talos_ctx_set_batch(talos_ctx* ctx, int max_seqs);
 talos_status talos_forward_batch(talos_ctx* ctx, const uint32_t* tokens, const size_t* pos, int n,
                                  float* logits_out);
@@ -227,8 +229,8 @@ talos_status talos_forward_batch(talos_ctx* ctx, const uint32_t* tokens, const s
  * (src/eval.rs:35-52). The tokens are scored in chunks of the context length,
  * each from an empty KV cache; at each position the negative log-likelihood of
  * the next token (token_nll, src/eval.rs:18-23: log-sum-exp in f64) is added on
- * the GPU, so no logits leave the device (4 positions per weight pass where
- * talos_prefill takes its batched steps). Writes exp(mean NLL) to *ppl_out and,
+ * the GPU, so no logits leave the device (up to 128 positions per weight
+ * pass where talos_prefill takes its batched steps). Writes exp(mean NLL) to *ppl_out and,
  * if not NULL, the NLL sum and the number of scored positions. Leaves the KV
  * cache holding the last chunk.
  */

@@ -17,8 +17,8 @@ OUT = os.path.join(PKG, "_lib")
 CUDA_LIB = os.path.join(OUT, "libtalos_cuda.so")
 SYNTH_LIB = os.path.join(OUT, "libtalos_synth.so")
 
-CU_SOURCES = ["kernels.cu", "matvec.cu", "runtime.cu"]
-CU_DEPS = CU_SOURCES + ["common.cuh", "kernels.cuh"]
+CU_SOURCES = ["kernels.cu", "matvec.cu", "gemm.cu", "runtime.cu"]
+CU_DEPS = CU_SOURCES + ["common.cuh", "kernels.cuh", "ptx.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

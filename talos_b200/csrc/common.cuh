@@ -16,7 +16,8 @@ enum GType : int { GT_F32 = 0, GT_Q4_0 = 2, GT_Q8_0 = 8, GT_Q6_K = 14 };
 // (nibbles + f16 block scales); Q8_0 1024, 8704 B; Q6_K 1024, 8768 B (6-bit
 // quants widened to bytes, sub-block scales, f16 super-block scales); F32 256,
 // 8192 B. Rows pad to a multiple of 16 and columns to CK with entries that add
-// nothing (quant at the zero point, scale 0). p1 .. p3 are unused (null).
+// nothing (quant at the zero point, scale 0). p1 (quant types): one f32, the
+// largest |value| the blocks dequantize to (k_wbound). p2, p3 are unused (null).
 struct PackedW {
     int type;
     int rows, cols;   // logical shape [rows, cols]

@@ -1,0 +1,784 @@
+// gemm.cu -- the tensor-core (tcgen05) GEMM of the prefill and batched-decode
+// steps on B200 (sm_100a).
+//
+// Y[t][r] = sum_k dequant(W)[r][k] * X[t][k] for up to 128 token columns per
+// tile: the prompt positions of a prefill chunk, or the independent sequences
+// of a batched decode step. The arithmetic of every (r, t) element is what
+// quant::matvec (Tsuskov/talos src/math/quant.rs:18-51) computes for that row
+// and input, to f32 rounding.
+//
+// Exactness. The tensor cores multiply f16 (kind::f16) into f32 accumulators.
+//  * Weights: a Q4_0 / Q8_0 value (q - z) * d has at most 4 + 11 / 8 + 11
+//    significant bits, so it is EXACTLY A_hi + A_lo with A_hi = f16(v) and
+//    A_lo = v - A_hi (computed with one f16 multiply and one f16 FMA, both exact
+//    here). The tensor's values are first scaled by a power of two 2^eA that
+//    keeps them inside f16's normal range (the bound comes from the tensor's
+//    largest block scale, recorded when it was packed); the epilogue multiplies
+//    by 2^-eA. Q6_K's (d * sc) * q (src/gguf/dtype.rs:112-115) has up to 25
+//    bits: it is formed in f32 like the reference and split into hi + lo
+//    (22 bits).
+//  * Activations: each token's input row is scaled by a power of two 2^-e_t
+//    into [2^14, 2^15) at its largest element and split into f16 x_hi + x_lo
+//    (~22 bits); the epilogue multiplies by 2^e_t. No input overflows f16 and
+//    small inputs keep their relative precision.
+//  * Per K step of 16: D[:, 0:2N] += A_hi x [x_hi | x_lo] and
+//    D[:, 0:N] += A_lo x x_hi (the A_lo x_lo term is below f32 rounding); the
+//    result is D[:, t] + D[:, N + t].
+//
+// Structure: one CTA per SM (persistent over work units = 128-row tile x token
+// tile x K slice), warp-specialised:
+//  * warps 0-3: epilogue. Warp q reads TMEM lanes 32q .. 32q+31 (its tile rows)
+//    with tcgen05.ld, combines, scales and applies the step's epilogue (store,
+//    residual add, SwiGLU, RoPE + KV-cache append); with split-K the partial
+//    tile goes to a workspace and the unit that completes the tile adds the
+//    slices in slice order (deterministic). The four warps never wait for one
+//    another.
+//  * warp 4: weight producer. 1-D bulk copies of the packed group-chunks
+//    (k_pack_*: 8 rows x CK) of the tile's 16 row groups, 128 inputs per raw
+//    slot, into a ring of raw slots.
+//  * warp 5: activation producer. Tiled TMA (cp.async.bulk.tensor.3d, no
+//    multicast) of the formatted [x_hi; x_lo] planes into the B stage, in the
+//    canonical no-swizzle K-major layout of tcgen05 (8 x 16-byte core matrices).
+//  * warp 6: allocates TMEM (two accumulators of 2N f32 columns), one thread
+//    issues tcgen05.mma.cta_group::1.kind::f16 (M 128, N 2N / N, K 16) and
+//    tcgen05.commit to the stage's "empty" and the accumulator's "full" barrier.
+//  * warps 7-14: dequantizers. Raw slot -> A_hi / A_lo stage tiles (f16, the
+//    same canonical layout), fence.proxy.async, arrive.
+// Every mbarrier wait is bounded (2 s); on expiry the CTA records an error bit
+// in BatchParams::error and every role leaves its loop; TMEM is freed at exit.
+#include <cuda.h>
+#include <math.h>
+
+#include "kernels.cuh"
+#include "ptx.cuh"
+
+namespace talos {
+
+constexpr int GM_BM = 128;   // weight rows per tile = TMEM lanes
+constexpr int GM_BK = 64;    // K per A/B stage
+constexpr int GM_RK = 128;   // K per raw weight slot (two stages)
+constexpr int GM_NS = 2;     // A/B stages
+constexpr int GM_NDQ = 8;    // dequantizer warps
+constexpr int GM_WP = 4, GM_XP = 5, GM_MMA = 6, GM_DQ0 = 7;
+constexpr int GM_THREADS = (GM_DQ0 + GM_NDQ) * 32;
+constexpr int GM_SMEM = 220 * 1024;
+constexpr int GM_MAXRAW = 8;
+
+// Bytes per row group of one raw slot (128 inputs): lane records, then scales.
+//  Q4_0: quad q of the group-chunk (512 B) + its f16 scales [8 rows][4] (64 B)
+//  Q8_0: quad q (1024 B) + scales [8 rows][4] (64 B)
+//  Q6_K: step-quads 2m, 2m+1 (1024 B) + the chunk's sc [8][64] and d [8][4] (576 B)
+template <int TYPE>
+struct GmFmt;
+template <>
+struct GmFmt<GT_Q4_0> {
+    static constexpr int LREC = 512, SC = 64;
+};
+template <>
+struct GmFmt<GT_Q8_0> {
+    static constexpr int LREC = 1024, SC = 64;
+};
+template <>
+struct GmFmt<GT_Q6_K> {
+    static constexpr int LREC = 1024, SC = 576;
+};
+
+template <int TYPE, int NT>
+struct GmCfg {
+    static constexpr int GRP = GmFmt<TYPE>::LREC + GmFmt<TYPE>::SC;
+    static constexpr int RAW = 16 * GRP;
+    static constexpr int A_BYTES = 2 * GM_BM * GM_BK * 2;  // A_hi + A_lo
+    static constexpr int B_BYTES = 2 * NT * GM_BK * 2;     // [x_hi; x_lo]
+    static constexpr int BAR_BYTES = 1024;
+    static constexpr int FIXED = GM_NS * (A_BYTES + B_BYTES) + BAR_BYTES;
+    static constexpr int NRAW_FIT = (GM_SMEM - FIXED) / RAW;
+    static constexpr int NRAW = NRAW_FIT > GM_MAXRAW ? GM_MAXRAW : NRAW_FIT;
+    static constexpr int SMEM = FIXED + NRAW * RAW;
+    static constexpr int TCOLS = 4 * NT;  // two accumulators of 2N columns
+    static_assert(NRAW >= 2, "raw ring too small");
+};
+
+// ---------------------------------------------------------------- PTX
+
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major, no-swizzle shared-memory matrix descriptor (tcgen05): 8-row x 16-byte
+// core matrices; LBO = byte distance between core matrices along K, SBO = along
+// M / N; version 1 (bits 46-47) for sm_100.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+// Instruction descriptor, kind::f16: f32 accumulate, f16 A and B, both K-major, M 128.
+__host__ __device__ constexpr uint32_t umma_idesc(int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(GM_BM >> 4) << 24);
+}
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+            "r"(smem_u32(dst)),
+        "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ---------------------------------------------------------------- work units
+
+struct GmUnit {
+    int si, lt;  // segment, tile within it
+    int tt, ks;  // token tile, K slice
+    int r0, r1;  // raw slots [r0, r1) of the slice
+    int tile;    // output tile index (row tile x token tile) for the split-K counters
+};
+__device__ __forceinline__ GmUnit gm_unit(const GemmArgs& a, int u, int ntt) {
+    GmUnit w;
+    w.ks = u % a.S;
+    int rest = u / a.S;
+    w.tt = rest % ntt;
+    int rt = rest / ntt;
+    w.tile = rt * ntt + w.tt;
+    w.si = 0;
+    while (w.si + 1 < a.nseg && rt >= a.seg[w.si].ntiles) rt -= a.seg[w.si++].ntiles;
+    w.lt = rt;
+    const int R = a.KP / GM_RK;
+    w.r0 = (int)((long)w.ks * R / a.S);
+    w.r1 = (int)((long)(w.ks + 1) * R / a.S);
+    return w;
+}
+
+// Row group gi (0..15) of a tile: matrix and group index. A SwiGLU pair tile is
+// 64 gate rows and the same 64 up rows, groups interleaved (even: gate, odd: up).
+__device__ __forceinline__ const PackedW* gm_group(const GemmSeg& sg, int lt, int gi, int& g) {
+    if (sg.pair) {
+        g = lt * 8 + (gi >> 1);
+        return (gi & 1) ? &sg.B : &sg.A;
+    }
+    g = lt * 16 + gi;
+    return &sg.A;
+}
+
+// Byte offsets, inside group g's data, of the lane records and scales of raw slot rs.
+template <int TYPE>
+__device__ __forceinline__ void gm_src(const PackedW& w, int g, int rs, const uint8_t*& lrec, const uint8_t*& sc) {
+    const int k0 = rs * GM_RK;
+    if (TYPE == GT_Q4_0) {
+        const uint8_t* gc = (const uint8_t*)w.p0 + ((size_t)g * w.nk + k0 / 2048) * (16 * 512 + 16 * 64);
+        const int q = (k0 % 2048) / 128;
+        lrec = gc + q * 512;
+        sc = gc + 16 * 512 + q * 64;
+    } else if (TYPE == GT_Q8_0) {
+        const uint8_t* gc = (const uint8_t*)w.p0 + ((size_t)g * w.nk + k0 / 1024) * (8 * 1024 + 8 * 64);
+        const int q = (k0 % 1024) / 128;
+        lrec = gc + q * 1024;
+        sc = gc + 8 * 1024 + q * 64;
+    } else {
+        const uint8_t* gc = (const uint8_t*)w.p0 + ((size_t)g * w.nk + k0 / 1024) * (16 * 512 + 8 * 64 + 8 * 4 * 2);
+        const int m = (k0 % 1024) / 128;
+        lrec = gc + 2 * m * 512;
+        sc = gc + 16 * 512;
+    }
+}
+
+// The segment's scale exponent eA: its values * 2^eA stay below 2^14 (the bound
+// is recorded at pack time: the largest |value| the format can give, k_wbound;
+// a SwiGLU pair takes the larger of its two matrices' bounds).
+__device__ __forceinline__ int gm_wexp(const GemmSeg& sg) {
+    float b = sg.A.p1 ? *(const float*)sg.A.p1 : 0.f;
+    if (sg.pair && sg.B.p1) b = fmaxf(b, *(const float*)sg.B.p1);
+    if (!(b > 0.f) || !isfinite(b)) return 0;
+    int ex;
+    frexpf(b, &ex);  // b in [2^(ex-1), 2^ex)
+    int e = 14 - ex;
+    return e > 60 ? 60 : (e < -60 ? -60 : e);
+}
+
+// ---------------------------------------------------------------- dequantizers
+//
+// Thread (lr, t) = (lane / 4, lane % 4) of a group task holds, per 32-element
+// block (16 for Q6_K), the k pairs {2t, 2t+1}, {2t+8, 2t+9}, {16+2t, 17+2t},
+// {24+2t, 25+2t} (the packed lane records); each pair is one 4-byte f16x2 word
+// of a core-matrix row: A[kg][row][2t .. 2t+1], kg = the pair's 8-k group.
+
+__device__ __forceinline__ void gm_put(uint8_t* A, int kg, int row, int t, __half2 v) {
+    uint32_t u = *reinterpret_cast<uint32_t*>(&v);
+    *(uint32_t*)(A + kg * (GM_BM * 16) + row * 16 + t * 4) = u;
+}
+__device__ __forceinline__ void gm_split_store(uint8_t* Ahi, uint8_t* Alo, int kg, int row, int t, __half2 q,
+                                               __half2 d) {
+    const __half2 hi = __hmul2(q, d);
+    const __half2 lo = __hfma2(q, d, __hneg2(hi));  // exact remainder (see the file comment)
+    gm_put(Ahi, kg, row, t, hi);
+    gm_put(Alo, kg, row, t, lo);
+}
+__device__ __forceinline__ void gm_split_store_f32(uint8_t* Ahi, uint8_t* Alo, int kg, int row, int t, float v0,
+                                                   float v1) {
+    const __half2 hi = __floats2half2_rn(v0, v1);
+    const float2 hf = __half22float2(hi);
+    const __half2 lo = __floats2half2_rn(v0 - hf.x, v1 - hf.y);
+    gm_put(Ahi, kg, row, t, hi);
+    gm_put(Alo, kg, row, t, lo);
+}
+// Q8_0 bytes (two int8 in byte positions sel) -> f16x2 exactly: 1024 + (q + 128) - 1152.
+__device__ __forceinline__ __half2 q8_pair(uint32_t w, uint32_t sel) {
+    const uint32_t b = __byte_perm(w ^ 0x80808080u, 0x64646464u, sel);
+    __half2 h = *reinterpret_cast<const __half2*>(&b);
+    return __hsub2(h, __half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480)));  // 1152
+}
+
+// One group task of one stage (half h of the raw slot): raw group data -> A rows
+// 8 gi .. 8 gi + 7 of this stage's A_hi / A_lo (Q4_0, Q8_0; Q6_K: gm_dequant_q6).
+template <int TYPE>
+__device__ __forceinline__ void gm_dequant(const uint8_t* grp, uint8_t* Ahi, uint8_t* Alo, int gi, int h, int lane,
+                                           float wsc) {
+    const int lr = lane >> 2, t = lane & 3, row = gi * 8 + lr;
+    if (TYPE == GT_Q4_0) {
+        const uint4 rec = *(const uint4*)(grp + lane * 16);
+        const uint32_t sc2 = *(const uint32_t*)(grp + 512 + lr * 8 + h * 4);
+        const uint32_t wv[2] = {h ? rec.z : rec.x, h ? rec.w : rec.y};
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+            const float d = __half2float(__ushort_as_half((unsigned short)(sc2 >> (16 * jj)))) * wsc;
+            const __half2 dd = __float2half2_rn(d);
+            const uint32_t w = wv[jj];
+            uint32_t q;
+            q = q4_lo_f16x2(w);
+            gm_split_store(Ahi, Alo, 4 * jj + 0, row, t, *reinterpret_cast<__half2*>(&q), dd);
+            q = q4_hi_f16x2(w);
+            gm_split_store(Ahi, Alo, 4 * jj + 1, row, t, *reinterpret_cast<__half2*>(&q), dd);
+            q = q4_lo_f16x2(w >> 8);
+            gm_split_store(Ahi, Alo, 4 * jj + 2, row, t, *reinterpret_cast<__half2*>(&q), dd);
+            q = q4_hi_f16x2(w >> 8);
+            gm_split_store(Ahi, Alo, 4 * jj + 3, row, t, *reinterpret_cast<__half2*>(&q), dd);
+        }
+    } else if (TYPE == GT_Q8_0) {
+        const uint4 rec = *(const uint4*)(grp + lane * 32 + h * 16);
+        const uint32_t sc2 = *(const uint32_t*)(grp + 1024 + lr * 8 + h * 4);
+        const uint32_t wv[4] = {rec.x, rec.y, rec.z, rec.w};
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+            const float d = __half2float(__ushort_as_half((unsigned short)(sc2 >> (16 * jj)))) * wsc;
+            const __half2 dd = __float2half2_rn(d);
+            // bytes of block jj: {2t, 2t+1, 2t+8, 2t+9} then {16+2t, 17+2t, 24+2t, 25+2t}
+            gm_split_store(Ahi, Alo, 4 * jj + 0, row, t, q8_pair(wv[2 * jj], 0x4140), dd);
+            gm_split_store(Ahi, Alo, 4 * jj + 1, row, t, q8_pair(wv[2 * jj], 0x4342), dd);
+            gm_split_store(Ahi, Alo, 4 * jj + 2, row, t, q8_pair(wv[2 * jj + 1], 0x4140), dd);
+            gm_split_store(Ahi, Alo, 4 * jj + 3, row, t, q8_pair(wv[2 * jj + 1], 0x4342), dd);
+        }
+    }
+}
+
+// Q6_K needs the sub-block position inside its 1024-input chunk for the scales.
+__device__ __forceinline__ void gm_dequant_q6(const uint8_t* grp, uint8_t* Ahi, uint8_t* Alo, int gi, int h,
+                                              int lane, float wsc, int step0) {
+    const int lr = lane >> 2, t = lane & 3, row = gi * 8 + lr;
+    const uint4 rec = *(const uint4*)(grp + h * 512 + lane * 16);
+    const uint32_t wv[4] = {rec.x, rec.y, rec.z, rec.w};
+    const int8_t* scp = (const int8_t*)(grp + 1024) + lr * 64;
+    const uint16_t* dp = (const uint16_t*)(grp + 1024 + 512) + lr * 4;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const int step = step0 + h * 4 + s;  // sub-block index in the chunk, 0..63
+        const float d = __half2float(__ushort_as_half(dp[step >> 4]));
+        const float dsc = __fmul_rn(d, (float)scp[step]);
+        const uint32_t w = wv[s];
+        const float v0 = __fmul_rn(dsc, (float)((int)(w & 0xFF) - 32)) * wsc;
+        const float v1 = __fmul_rn(dsc, (float)((int)((w >> 8) & 0xFF) - 32)) * wsc;
+        const float v2 = __fmul_rn(dsc, (float)((int)((w >> 16) & 0xFF) - 32)) * wsc;
+        const float v3 = __fmul_rn(dsc, (float)((int)(w >> 24) - 32)) * wsc;
+        gm_split_store_f32(Ahi, Alo, 2 * s, row, t, v0, v1);      // k 2t, 2t+1 of the sub-block
+        gm_split_store_f32(Ahi, Alo, 2 * s + 1, row, t, v2, v3);  // k 2t+8, 2t+9
+    }
+}
+
+// ---------------------------------------------------------------- epilogue
+
+__device__ __forceinline__ void gm_apply(const GemmArgs& a, const GemmSeg& sg, int lt, int r, int t, int ntok, float v,
+                                         const uint32_t* pos) {
+    const int lane = threadIdx.x & 31;
+    const bool live = t < ntok;
+    if (sg.epi == EPI_B_SWIGLU) {  // src/math/ops.rs:33-37: gate lanes r % 16 < 8, up on lane + 8
+        const float up = __shfl_down_sync(0xffffffffu, v, 8);
+        const int row = lt * 64 + (r >> 4) * 8 + (r & 7);
+        if (live && (r & 8) == 0 && row < sg.rows) sg.y[(size_t)t * sg.ldy + row] = __fmul_rn(silu_ref(v), up);
+        return;
+    }
+    const int row = lt * GM_BM + r;
+    if (sg.epi >= EPI_B_ROPE) {
+        // pairs (2i, 2i+1) on lanes l, l ^ 1 (src/math/ops.rs:48-61); then the cache
+        // append of src/kv_cache.rs:21-26 at the token's slot and position
+        const float pv = __shfl_xor_sync(0xffffffffu, v, 1);
+        (void)lane;
+        if (!live || row >= sg.rows) return;
+        const uint32_t p = pos[t];
+        float o = v;
+        if (sg.epi != EPI_B_VCACHE) {
+            const float2 c = a.rope_cs[(size_t)p * (a.hd >> 1) + ((row % a.hd) >> 1)];
+            o = (row & 1) ? __fadd_rn(__fmul_rn(pv, c.y), __fmul_rn(v, c.x))
+                          : __fsub_rn(__fmul_rn(v, c.x), __fmul_rn(pv, c.y));
+        }
+        float* dst = sg.epi == EPI_B_ROPE ? sg.y + (size_t)t * sg.ldy
+                                          : (sg.epi == EPI_B_KCACHE ? a.kc : a.vc) + (size_t)t * a.seq_stride +
+                                                (size_t)p * a.kv_dim;
+        dst[row] = o;
+        return;
+    }
+    if (!live || row >= sg.rows) return;
+    float* y = sg.y + (size_t)t * sg.ldy + row;
+    *y = sg.epi == EPI_B_ADD ? __fadd_rn(*y, v) : v;
+}
+
+// ---------------------------------------------------------------- the kernel
+
+template <int TYPE, int NT>
+__global__ void __launch_bounds__(GM_THREADS, 1)
+    k_gemm(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ GemmArgs a) {
+    using C = GmCfg<TYPE, NT>;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t* sA = smem;                                   // [NS][hi 16 KB | lo 16 KB]
+    uint8_t* sB = smem + GM_NS * C::A_BYTES;              // [NS][kg 8][2 NT][16 B]
+    uint8_t* sR = sB + GM_NS * C::B_BYTES;                // [NRAW][16 groups][GRP]
+    uint64_t* bars = (uint64_t*)(sR + C::NRAW * C::RAW);  // barriers
+    uint64_t* raw_full = bars;
+    uint64_t* raw_empty = raw_full + C::NRAW;
+    uint64_t* a_full = raw_empty + C::NRAW;
+    uint64_t* b_full = a_full + GM_NS;
+    uint64_t* st_empty = b_full + GM_NS;
+    uint64_t* acc_full = st_empty + GM_NS;   // [2]
+    uint64_t* acc_empty = acc_full + 2;      // [2]
+    uint64_t* done = acc_empty + 2;          // the MMA thread's final commit
+    uint32_t* tmem_slot = (uint32_t*)(done + 1);
+    int* s_flag = (int*)(tmem_slot + 1);     // [0]: some role gave up on a wait
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    const int ntok = a.bp->n;
+    const int ntt = (ntok + NT - 1) / NT;
+    const int nunits = a.nrt * ntt * a.S;
+
+    if (tid == 0) {
+        for (int i = 0; i < C::NRAW; ++i) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], GM_NDQ);
+        }
+        for (int i = 0; i < GM_NS; ++i) {
+            mbar_init(&a_full[i], GM_NDQ);
+            mbar_init(&b_full[i], 1);
+            mbar_init(&st_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 4);
+        }
+        mbar_init(done, 1);
+        s_flag[0] = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == GM_MMA) {  // TMEM: two accumulators of 2 NT f32 columns
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"((uint32_t)C::TCOLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    auto fail = [&]() {
+        *(volatile int*)&s_flag[0] = 1;
+        atomicOr((unsigned*)&a.bp->error, 2u);
+    };
+    auto stop = [&]() { return *(volatile int*)&s_flag[0] != 0; };
+
+    if (warp == GM_WP) {
+        // ---------------- weight producer
+        if (lane == 0) {
+            uint32_t ri = 0;
+            for (int u = blockIdx.x; u < nunits && !stop(); u += gridDim.x) {
+                const GmUnit U = gm_unit(a, u, ntt);
+                const GemmSeg& sg = a.seg[U.si];
+                for (int rs = U.r0; rs < U.r1; ++rs, ++ri) {
+                    const int slot = ri % C::NRAW;
+                    if (!mbar_wait(&raw_empty[slot], ((ri / C::NRAW) & 1) ^ 1)) {
+                        fail();
+                        break;
+                    }
+                    uint32_t bytes = 0;
+                    for (int gi = 0; gi < 16; ++gi) {
+                        int g;
+                        const PackedW* w = gm_group(sg, U.lt, gi, g);
+                        if (g < w->rows_pad / 8) bytes += C::GRP;
+                    }
+                    mbar_expect_tx(&raw_full[slot], bytes);
+                    uint8_t* dst = sR + slot * C::RAW;
+                    for (int gi = 0; gi < 16; ++gi) {
+                        int g;
+                        const PackedW* w = gm_group(sg, U.lt, gi, g);
+                        if (g >= w->rows_pad / 8) continue;
+                        const uint8_t *lr, *sc;
+                        gm_src<TYPE>(*w, g, rs, lr, sc);
+                        bulk_g2s(dst + gi * C::GRP, lr, GmFmt<TYPE>::LREC, &raw_full[slot]);
+                        bulk_g2s(dst + gi * C::GRP + GmFmt<TYPE>::LREC, sc, GmFmt<TYPE>::SC, &raw_full[slot]);
+                    }
+                }
+                if (stop()) break;
+            }
+            // copies in flight land before the CTA exits
+            const uint32_t first = ri > (uint32_t)C::NRAW ? ri - C::NRAW : 0;
+            for (uint32_t j = first; j < ri; ++j) mbar_wait(&raw_full[j % C::NRAW], (j / C::NRAW) & 1);
+        }
+    } else if (warp == GM_XP) {
+        // ---------------- activation producer: TMA tiles of the [x_hi; x_lo] planes
+        if (lane == 0) {
+            uint32_t si = 0;
+            for (int u = blockIdx.x; u < nunits && !stop(); u += gridDim.x) {
+                const GmUnit U = gm_unit(a, u, ntt);
+                for (int rs = U.r0; rs < U.r1 && !stop(); ++rs)
+                    for (int h = 0; h < 2; ++h, ++si) {
+                        const int s = si % GM_NS;
+                        if (!mbar_wait(&st_empty[s], ((si / GM_NS) & 1) ^ 1)) {
+                            fail();
+                            break;
+                        }
+                        mbar_expect_tx(&b_full[s], C::B_BYTES);
+                        uint8_t* dst = sB + s * C::B_BYTES;
+                        const int k0 = rs * GM_RK + h * GM_BK;
+#pragma unroll 1
+                        for (int i = 0; i < GM_BK / 8; ++i)
+                            tma_load_3d(dst + i * (2 * NT * 16), &tmx, k0 + 8 * i, U.tt * NT, 0, &b_full[s]);
+                    }
+            }
+            const uint32_t first = si > (uint32_t)GM_NS ? si - GM_NS : 0;
+            for (uint32_t j = first; j < si; ++j) mbar_wait(&b_full[j % GM_NS], (j / GM_NS) & 1);
+        }
+    } else if (warp == GM_MMA) {
+        // ---------------- MMA issuer
+        if (lane == 0) {
+            uint32_t si = 0, nu = 0;
+            const uint32_t lbo_a = GM_BM * 16, lbo_b = 2 * NT * 16, sbo = 128;
+            for (int u = blockIdx.x; u < nunits && !stop(); u += gridDim.x, ++nu) {
+                const GmUnit U = gm_unit(a, u, ntt);
+                const int ab = nu & 1;
+                if (!mbar_wait(&acc_empty[ab], ((nu >> 1) & 1) ^ 1)) {
+                    fail();
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + ab * (2 * NT);
+                bool first = true;
+                bool ok = true;
+                for (int rs = U.r0; rs < U.r1 && ok; ++rs)
+                    for (int h = 0; h < 2; ++h, ++si) {
+                        const int s = si % GM_NS;
+                        const uint32_t par = (si / GM_NS) & 1;
+                        if (!mbar_wait(&a_full[s], par) || !mbar_wait(&b_full[s], par)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t ah = smem_u32(sA + s * C::A_BYTES), al = ah + GM_BM * GM_BK * 2;
+                        const uint32_t bb = smem_u32(sB + s * C::B_BYTES);
+#pragma unroll
+                        for (int kk = 0; kk < GM_BK / 16; ++kk) {
+                            const uint64_t bd = umma_desc(bb + kk * 2 * lbo_b, lbo_b, sbo);
+                            umma_f16(d, umma_desc(ah + kk * 2 * lbo_a, lbo_a, sbo), bd, umma_idesc(2 * NT),
+                                     (first && kk == 0) ? 0u : 1u);
+                            umma_f16(d, umma_desc(al + kk * 2 * lbo_a, lbo_a, sbo), bd, umma_idesc(NT), 1u);
+                        }
+                        first = false;
+                        umma_commit(&st_empty[s]);  // the stage's A and B are free once these MMAs finish
+                    }
+                if (!ok) {
+                    fail();
+                    break;
+                }
+                umma_commit(&acc_full[ab]);
+            }
+            // every MMA issued has finished before TMEM is freed
+            umma_commit(done);
+            mbar_wait(done, 0);
+        }
+        __syncwarp();
+    } else if (warp >= GM_DQ0) {
+        // ---------------- dequantizers: warp dw takes row groups dw and dw + 8
+        const int dw = warp - GM_DQ0;
+        uint32_t ri = 0, si = 0;
+        int cur_si = -1;
+        float wsc = 1.f;
+        for (int u = blockIdx.x; u < nunits && !stop(); u += gridDim.x) {
+            const GmUnit U = gm_unit(a, u, ntt);
+            const GemmSeg& sg = a.seg[U.si];
+            if (U.si != cur_si) {
+                cur_si = U.si;
+                wsc = ldexpf(1.f, gm_wexp(sg));
+            }
+            bool ok = true;
+            for (int rs = U.r0; rs < U.r1 && ok; ++rs, ++ri) {
+                const int slot = ri % C::NRAW;
+                // every wait's outcome is made warp-uniform (the lanes leave together)
+                if (!__all_sync(0xffffffffu, mbar_wait(&raw_full[slot], (ri / C::NRAW) & 1))) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* raw = sR + slot * C::RAW;
+                for (int h = 0; h < 2; ++h, ++si) {
+                    const int s = si % GM_NS;
+                    if (!__all_sync(0xffffffffu, mbar_wait(&st_empty[s], ((si / GM_NS) & 1) ^ 1))) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* Ahi = sA + s * C::A_BYTES;
+                    uint8_t* Alo = Ahi + GM_BM * GM_BK * 2;
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const int gi = dw + 8 * j;
+                        if (TYPE == GT_Q6_K)
+                            gm_dequant_q6(raw + gi * C::GRP, Ahi, Alo, gi, h, lane, wsc, ((rs * GM_RK) % 1024) / 16);
+                        else
+                            gm_dequant<TYPE>(raw + gi * C::GRP, Ahi, Alo, gi, h, lane, wsc);
+                    }
+                    fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core's reads
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a_full[s]);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&raw_empty[slot]);
+            }
+            if (!ok) {
+                if (lane == 0) fail();
+                break;
+            }
+        }
+    } else {
+        // ---------------- epilogue: warp q owns TMEM lanes / tile rows 32q .. 32q+31.
+        // The four warps never wait for each other: with split-K each warp has its
+        // own arrival counter per output tile (cnt[tile * 4 + q]).
+        const int q = warp, r = q * 32 + lane;
+        uint32_t nu = 0;
+        for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++nu) {
+            const GmUnit U = gm_unit(a, u, ntt);
+            const GemmSeg& sg = a.seg[U.si];
+            const int ab = nu & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[ab], (nu >> 1) & 1))) {
+                if (lane == 0) fail();
+                break;
+            }
+            tc_fence_after();
+            const float wsc = ldexpf(1.f, -gm_wexp(sg));
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * (2 * NT);
+            const int t0 = U.tt * NT;
+            float* part = a.S > 1 ? a.ws + ((size_t)(U.tile * a.S + U.ks) * NT) * GM_BM : nullptr;
+#pragma unroll 1
+            for (int c = 0; c < NT; c += 16) {
+                float vh[16], vl[16];
+                tmem_ld16(tbase + c, vh);
+                tmem_ld16(tbase + NT + c, vl);
+                tmem_wait_ld();
+                if (part) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) part[(size_t)(c + j) * GM_BM + r] = vh[j] + vl[j];
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int t = t0 + c + j;
+                        const float v = (vh[j] + vl[j]) * (wsc * (t < ntok ? a.xs[t] : 0.f));
+                        gm_apply(a, sg, U.lt, r, t, ntok, v, a.bp->pos);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[ab]);
+            if (!part) continue;
+            // split-K: the unit that completes the tile's rows adds the slices in
+            // slice order (the same order every run)
+            __threadfence();
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) {
+                unsigned* cp = &a.cnt[U.tile * 4 + q];
+                last = atomicAdd(cp, 1u) == (unsigned)(a.S - 1);
+                if (last) *cp = 0u;  // every slice has arrived: ready for the next launch
+            }
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (!last) continue;
+            __threadfence();
+            const float* base = a.ws + ((size_t)U.tile * a.S * NT) * GM_BM;
+#pragma unroll 1
+            for (int c = 0; c < NT; ++c) {
+                float v = 0.f;
+                for (int s = 0; s < a.S; ++s) v += __ldcg(base + ((size_t)s * NT + c) * GM_BM + r);
+                const int t = t0 + c;
+                v *= wsc * (t < ntok ? a.xs[t] : 0.f);
+                gm_apply(a, sg, U.lt, r, t, ntok, v, a.bp->pos);
+            }
+        }
+    }
+    // ---------------- teardown: every role is out of its loop
+    tc_fence_before();
+    __syncthreads();
+    if (warp == GM_MMA) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TCOLS));
+    }
+}
+
+// ---------------------------------------------------------------- activation format
+
+// One CTA per token column t (prefill position or sequence) of the first
+// `gridDim.x` columns of the [2][Tp][ldp] planes: the input row
+// x[t] (RMSNorm with norm_w first when set: src/math/ops.rs:5-12, (x * s) * w),
+// scaled by 2^-e_t so its largest |value| lies in [2^14, 2^15), split into
+// f16 hi / lo planes [2][Tp][ldp] (zeros past K and for t >= n); xs[t] = 2^e_t.
+__global__ void __launch_bounds__(1024) k_xfmt_g(const float* x, int ldx, int K, int KP, int ldp, int Tp,
+                                                 const float* norm_w, float eps, const BatchParams* bp, __half* planes,
+                                                 float* xs) {
+    __shared__ float red[32];
+    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __half* hi = planes + (size_t)t * ldp;
+    __half* lo = planes + ((size_t)Tp + t) * ldp;
+    if (t >= bp->n) {
+        for (int k = tid; k < KP; k += blockDim.x) hi[k] = lo[k] = __float2half_rn(0.f);
+        if (tid == 0) xs[t] = 0.f;
+        return;
+    }
+    const float* xr = x + (size_t)t * ldx;
+    auto block_reduce = [&](float v, bool is_max) -> float {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float w = __shfl_xor_sync(0xffffffffu, v, o);
+            v = is_max ? fmaxf(v, w) : v + w;
+        }
+        __syncthreads();
+        if (lane == 0) red[warp] = v;
+        __syncthreads();
+        float tot = is_max ? 0.f : 0.f;
+        const int nw = blockDim.x >> 5;
+        for (int i = 0; i < nw; ++i) tot = is_max ? fmaxf(tot, red[i]) : tot + red[i];
+        return tot;
+    };
+    float s = 1.f;
+    if (norm_w) {
+        float ss = 0.f;
+        for (int k = tid; k < K; k += blockDim.x) ss = fmaf(xr[k], xr[k], ss);
+        const float tot = block_reduce(ss, false);
+        s = 1.0f / sqrtf(tot / (float)K + eps);
+    }
+    auto val = [&](int k) -> float { return norm_w ? __fmul_rn(__fmul_rn(xr[k], s), norm_w[k]) : xr[k]; };
+    float m = 0.f;
+    for (int k = tid; k < K; k += blockDim.x) m = fmaxf(m, fabsf(val(k)));
+    m = block_reduce(m, true);
+    int e = 0;
+    if (m > 0.f && isfinite(m)) {
+        int ex;
+        frexpf(m, &ex);  // m in [2^(ex-1), 2^ex)
+        e = ex - 15;
+    }
+    const float down = ldexpf(1.f, -e);
+    if (tid == 0) xs[t] = ldexpf(1.f, e);
+    for (int k = tid; k < KP; k += blockDim.x) {
+        const float v = k < K ? val(k) * down : 0.f;
+        const __half h = __float2half_rn(v);
+        hi[k] = h;
+        lo[k] = __float2half_rn(v - __half2float(h));
+    }
+}
+
+// ---------------------------------------------------------------- host side
+
+template <int TYPE, int NT>
+static cudaError_t gemm_attr() {
+    return cudaFuncSetAttribute(k_gemm<TYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, GmCfg<TYPE, NT>::SMEM);
+}
+
+cudaError_t gemm_configure() {
+    cudaError_t e;
+#define TALOS_GM_ATTR(T)                                   \
+    if ((e = gemm_attr<T, 32>()) != cudaSuccess) return e; \
+    if ((e = gemm_attr<T, 64>()) != cudaSuccess) return e; \
+    if ((e = gemm_attr<T, 128>()) != cudaSuccess) return e;
+    TALOS_GM_ATTR(GT_Q4_0)
+    TALOS_GM_ATTR(GT_Q8_0)
+    TALOS_GM_ATTR(GT_Q6_K)
+#undef TALOS_GM_ATTR
+    return cudaSuccess;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+cudaError_t gemm_tensor_map(void* planes, int ldp, int Tp, int nt, void* map_out) {
+    static EncodeTiledFn enc = nullptr;
+    if (!enc) {
+        cudaDriverEntryPointQueryResult q;
+        void* fn = nullptr;
+        cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
+        if (e != cudaSuccess) return e;
+        if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+        enc = (EncodeTiledFn)fn;
+    }
+    // dims: k (ldp halves, contiguous), token t (Tp), plane (2: hi, lo); box 8 x nt x 2
+    const cuuint64_t dims[3] = {(cuuint64_t)ldp, (cuuint64_t)Tp, 2};
+    const cuuint64_t strides[2] = {(cuuint64_t)ldp * 2, (cuuint64_t)Tp * ldp * 2};
+    const cuuint32_t box[3] = {8, (cuuint32_t)nt, 2};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc((CUtensorMap*)map_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, planes, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+size_t gemm_map_bytes() { return sizeof(CUtensorMap); }
+
+template <int TYPE, int NT>
+static cudaError_t gemm_go(const void* map, const GemmArgs& a, int grid, cudaStream_t s) {
+    k_gemm<TYPE, NT><<<grid, GM_THREADS, GmCfg<TYPE, NT>::SMEM, s>>>(*(const CUtensorMap*)map, a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gemm(const void* map, const GemmArgs& a, int type, int nt, int grid, cudaStream_t s) {
+    if (a.KP % GM_RK || a.nseg < 1 || a.nseg > 3 || a.S < 1 || grid < 1) return cudaErrorInvalidValue;
+#define TALOS_GM_GO(T)                                      \
+    if (type == T) {                                        \
+        if (nt == 32) return gemm_go<T, 32>(map, a, grid, s);   \
+        if (nt == 64) return gemm_go<T, 64>(map, a, grid, s);   \
+        if (nt == 128) return gemm_go<T, 128>(map, a, grid, s); \
+    }
+    TALOS_GM_GO(GT_Q4_0)
+    TALOS_GM_GO(GT_Q8_0)
+    TALOS_GM_GO(GT_Q6_K)
+#undef TALOS_GM_GO
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_xfmt_g(const float* x, int ldx, int K, int KP, int ldp, int Tp, int ncols, const float* norm_w,
+                          float eps, const BatchParams* bp, void* planes, float* xs, cudaStream_t s) {
+    if (KP > ldp || KP < K || ncols < 1 || ncols > Tp) return cudaErrorInvalidValue;
+    k_xfmt_g<<<ncols, 1024, 0, s>>>(x, ldx, K, KP, ldp, Tp, norm_w, eps, bp, (__half*)planes, xs);
+    return cudaGetLastError();
+}
+
+}  // namespace talos

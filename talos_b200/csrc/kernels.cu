@@ -530,20 +530,5 @@ cudaError_t launch_attention_b(const float* q, int ldq, const float* kc, const f
     return cudaGetLastError();
 }
 
-__global__ void k_swiglu_b(const float* g, const float* u, float* h, int ld, int n_ff, const BatchParams* bp) {
-    const int s = blockIdx.y;
-    if (s >= bp->n) return;
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n_ff) {
-        const size_t o = (size_t)s * ld + i;
-        h[o] = __fmul_rn(silu_ref(g[o]), u[o]);
-    }
-}
-
-cudaError_t launch_swiglu_b(const float* g, const float* u, float* h, int ld, int n_ff, const BatchParams* bp,
-                            cudaStream_t s) {
-    k_swiglu_b<<<dim3((n_ff + 255) / 256, MB_SEQ), 256, 0, s>>>(g, u, h, ld, n_ff, bp);
-    return cudaGetLastError();
-}
 
 }  // namespace talos

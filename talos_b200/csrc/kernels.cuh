@@ -73,61 +73,67 @@ size_t noalloc_smem_bytes(int type, int K);
 cudaError_t launch_matvec_noalloc(const PackedW& w, const float* x, float* y, int nslice, float* part,
                                   unsigned* cnt, cudaStream_t s);
 
-// ---------------------------------------------------------------- batched decode
+// ---------------------------------------------------------------- batched steps
 //
-// Up to MB_SEQ sequences per weight pass: the MMA's 8 B columns hold four
-// sequences' f16 hi / lo activation parts. Activations are formatted once per
-// matvec input (k_xfmt_b) into per-block B fragments and block sums, which the
-// batched matvec streams through its ring together with the weights.
+// A batched step runs up to MB_SEQ token columns through every weight at once:
+// the independent sequences of a batched decode step, or consecutive prompt
+// positions of one sequence (prefill). Its matrix products are the tcgen05 GEMM
+// of gemm.cu: k_xfmt_g formats each matrix input (RMSNorm, per-column power-of-
+// two scale, f16 hi / lo planes), k_gemm multiplies the packed weights into it.
 
-constexpr int MB_SEQ = 4;
+constexpr int MB_SEQ = 128;
 
 struct BatchParams {
-    int n;                     // active sequences (1 .. MB_SEQ)
+    int n;                     // active token columns (1 .. MB_SEQ)
     uint32_t token[MB_SEQ];
     uint32_t pos[MB_SEQ];
-    uint32_t error;            // device-side error bits (2: a bounded wait expired)
+    uint32_t error;            // device-side error bits (1: token out of range, 2: a bounded wait expired)
 };
-
-// Formatted activation of [MB_SEQ][K] inputs for weights of `type`: fragments
-// (KP/32 blocks x 32 lanes x 16 bytes) and block sums ([KP/32] or, Q6_K,
-// [KP/16] x MB_SEQ floats). KP = K rounded up to the type's chunk.
-size_t xfmt_frag_bytes(int type, int K);
-size_t xfmt_sum_bytes(int type, int K);
-// x: [n][ldx] f32; norm_w: optional RMSNorm weight (eps); sequences n .. MB_SEQ-1 get zeros.
-cudaError_t launch_xfmt_b(int type, const float* x, int ldx, int K, const float* norm_w, float eps,
-                          const BatchParams* bp, void* frag, float* sums, cudaStream_t s);
 
 // Batched epilogues: store / add rows; SwiGLU of paired gate (A) / up (B) rows;
 // RoPE of q rows (stored to y); RoPE of k rows and v rows, appended to the
-// sequence's cache row at its position.
+// column's cache slot at its position.
 enum { EPI_B_STORE = 0, EPI_B_ADD = 1, EPI_B_SWIGLU = 2, EPI_B_ROPE = 3, EPI_B_KCACHE = 4, EPI_B_VCACHE = 5 };
-struct BatchSeg {
-    PackedW A, B;  // B: the up matrix of a SwiGLU pair (tile = 8 rows of A + the same 8 of B)
+
+// One weight of a GEMM launch. Tiles are 128 rows of A; a SwiGLU pair tile is
+// 64 gate rows of A and the same 64 up rows of B.
+struct GemmSeg {
+    PackedW A, B;
     int pair;
     int ntiles;
-    float* y;      // [MB_SEQ][ldy]
+    float* y;      // [MB_SEQ][ldy] outputs (EPI_B_KCACHE / VCACHE: unused)
     int ldy;
-    int rows;      // logical output rows
+    int rows;      // logical output rows (pair: ff rows)
     int epi;
 };
-struct BatchMvArgs {
-    BatchSeg seg[3];  // same type and input; tiles numbered across segments
+struct GemmArgs {
+    GemmSeg seg[3];  // same type and input; row tiles numbered across segments
     int nseg;
-    int ntiles;
-    int K;
-    const void* frag;  // formatted activation (launch_xfmt_b for the type)
-    const float* sums;
-    const float2* rope_cs;  // RoPE (cos, sin) [ctx][hd/2]
-    int hd;
-    int kv_dim;
-    float* kc;  // this layer's caches: sequence s's rows at kc + s * seq_stride
+    int nrt;         // row tiles over all segments
+    int S;           // K slices per output tile (split-K; 1 = none)
+    int K, KP;       // input length; KP = K rounded up to 128
+    const float* xs;       // per-column scale 2^e_t of the formatted input (k_xfmt_g)
+    const float2* rope_cs; // RoPE (cos, sin) [ctx][hd/2]
+    int hd, kv_dim;
+    float* kc;             // this layer's caches: column t's rows at kc + t * seq_stride
     float* vc;
     size_t seq_stride;
-    const BatchParams* bp;  // active sequence count, positions, error bits
+    const BatchParams* bp;
+    float* ws;             // split-K partial tiles [tiles][S][NT][128]
+    unsigned* cnt;         // split-K arrival counters [tiles][4], zero between launches
 };
-cudaError_t launch_matvec_b(const BatchMvArgs& a, int max_ctas, cudaStream_t s);
-cudaError_t matvec_b_configure();
+// Format columns 0 .. ncols-1 of `x` ([n][ldx] f32; columns n .. ncols-1
+// become zeros) for a GEMM whose weights have K inputs: f16 hi / lo planes
+// [2][Tp][ldp] and xs[] (ncols <= Tp).
+cudaError_t launch_xfmt_g(const float* x, int ldx, int K, int KP, int ldp, int Tp, int ncols, const float* norm_w,
+                          float eps, const BatchParams* bp, void* planes, float* xs, cudaStream_t s);
+// The tensor map (CUtensorMap, gemm_map_bytes() bytes) the GEMM's activation
+// producer reads `planes` through with token tiles of nt columns.
+cudaError_t gemm_tensor_map(void* planes, int ldp, int Tp, int nt, void* map_out);
+size_t gemm_map_bytes();
+// nt: token columns per tile (32, 64 or 128); grid: CTAs (one per SM at most).
+cudaError_t launch_gemm(const void* map, const GemmArgs& a, int type, int nt, int grid, cudaStream_t s);
+cudaError_t gemm_configure();
 
 // x[s] = dequant(token_embd row of token[s]) (src/model/weights.rs:57-62)
 cudaError_t launch_embed_b(const uint8_t* embd_raw, int type, int cols, int vocab, const BatchParams* bp, float* x,
@@ -136,9 +142,6 @@ cudaError_t launch_embed_b(const uint8_t* embd_raw, int type, int cols, int voca
 cudaError_t launch_attention_b(const float* q, int ldq, const float* kc, const float* vc, size_t seq_stride,
                                int kv_dim, int n_head, int n_kv, int hd, float* out, int ldo, const BatchParams* bp,
                                cudaStream_t s);
-// h[s][i] = silu(g[s][i]) * u[s][i] (src/math/ops.rs:28-37)
-cudaError_t launch_swiglu_b(const float* g, const float* u, float* h, int ld, int n_ff, const BatchParams* bp,
-                            cudaStream_t s);
 
 // ---------------------------------------------------------------- attention
 

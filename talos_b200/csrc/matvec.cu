@@ -28,6 +28,7 @@
 #include <math.h>
 
 #include "kernels.cuh"
+#include "ptx.cuh"
 
 namespace talos {
 
@@ -98,6 +99,7 @@ bool pack_sizes(int type, int rows, int cols, PackSizes* o) {
     o->rows_pad = ceil_div_h(rows, 16) * 16;
     o->nk = ceil_div_h(cols, ck);  // chunks per row group
     o->b0 = (size_t)(o->rows_pad / 8) * o->nk * fmt_gcb(type);
+    o->b1 = type == GT_F32 ? 0 : 16;  // the value bound k_wbound records
     return true;
 }
 
@@ -254,6 +256,29 @@ __global__ void k_pack_f32(const uint8_t* raw, PackedW w) {
     }
 }
 
+// The largest |value| a quant tensor's blocks can dequantize to, recorded at p1
+// (f32) for the tensor-core GEMM's power-of-two prescale: max |d| x 8 (Q4_0:
+// |nibble - 8| <= 8), x 128 (Q8_0), and max |d * sc| x 32 (Q6_K: |q - 32| <= 32).
+// Non-negative f32 values order like their bit patterns, so atomicMax on the
+// bits takes the maximum.
+__global__ void k_wbound(const uint8_t* raw, int type, size_t nblocks, float* out) {
+    float m = 0.f;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < nblocks; i += (size_t)gridDim.x * blockDim.x) {
+        if (type == GT_Q4_0) {
+            m = fmaxf(m, fabsf(ld_half_bytes(raw + i * 18)) * 8.f);
+        } else if (type == GT_Q8_0) {
+            m = fmaxf(m, fabsf(ld_half_bytes(raw + i * 34)) * 128.f);
+        } else {
+            const uint8_t* b = raw + i * 210;
+            int sm = 0;
+            for (int j = 0; j < 16; ++j) sm = max(sm, abs((int)(int8_t)b[192 + j]));
+            m = fmaxf(m, fabsf(ld_half_bytes(b + 208)) * (float)sm * 32.f);
+        }
+    }
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) atomicMax((unsigned*)out, __float_as_uint(m));
+}
+
 cudaError_t launch_pack(const uint8_t* raw, const PackedW& w, cudaStream_t s) {
     const int T = 256;
     const unsigned G = 148 * 16;
@@ -264,65 +289,46 @@ cudaError_t launch_pack(const uint8_t* raw, const PackedW& w, cudaStream_t s) {
         case GT_Q6_K: k_pack_q6_k<<<G, 64, 0, s>>>(raw, w); break;
         default: return cudaErrorInvalidValue;
     }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || w.type == GT_F32 || !w.p1) return e;
+    if ((e = cudaMemsetAsync((void*)w.p1, 0, sizeof(float), s)) != cudaSuccess) return e;
+    const size_t nb = (size_t)w.rows * (w.cols / gguf_block_elems(w.type));
+    k_wbound<<<148 * 4, 256, 0, s>>>(raw, w.type, nb, (float*)w.p1);
     return cudaGetLastError();
 }
 
-// ----------------------------------------------------------------------------
-// PTX helpers: mbarrier, 1-D bulk copy, programmatic dependent launch
-// ----------------------------------------------------------------------------
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-// Bounded wait: false once 2 s have passed without the phase completing (only on
-// a broken pipeline); the caller records an error and leaves its loop.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
-    for (;;) {
-        for (int i = 0; i < 64; ++i)
-            if (mbar_try_wait(bar, parity)) return true;
-        if (globaltimer_ns() - t0 > 2000000000ull) return false;
-    }
-}
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// PTX helpers (mbarrier, 1-D bulk copy, programmatic dependent launch): ptx.cuh
 
 constexpr int MV_CONSUMERS = 512;              // 16 consumer warps
 constexpr int MV_CWARPS = MV_CONSUMERS / 32;
 constexpr int MV_THREADS = MV_CONSUMERS + 64;  // + 1 producer warp + 1 epilogue warp
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+// consumer_sync that also ORs a flag over the 512 consumer threads.
+__device__ __forceinline__ bool consumer_sync_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, 512, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
+}
+
+// f16 range of the staged activation. Its f16 hi part overflows from 65,520 on,
+// so an input with an element of magnitude 2^15 or more is staged again scaled
+// by 2^-16 (exact for f32), as often as needed (at most kStageRetries times),
+// and the tile's row sums are multiplied back by the same power of two. Inputs
+// in range take one pass; the check rides on the staging's last barrier.
+constexpr float kStageBig = 32768.f;
+constexpr float kStageDown = 1.52587890625e-05f;  // 2^-16
+constexpr int kStageRetries = 6;
+__device__ __forceinline__ bool big4(float4 v) {
+    return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))) >= kStageBig;
+}
+__device__ __forceinline__ float4 scale4(float4 v, float s) { return make_float4(v.x * s, v.y * s, v.z * s, v.w * s); }
 
 // D = A(16x16 f16) * B(16x8 f16), f32 accumulate from zero / from d. Not
 // volatile: the MMAs of independent blocks may be scheduled around each other.
@@ -767,7 +773,8 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const __grid_constant_
         if (a.norm_w) v = __fmul_rn(__fmul_rn(v, scale), a.norm_w[e]);
         return v;
     };
-    {
+    float sdown = 1.f, sup = 1.f;  // f16 range scale of the staged input (kStageBig)
+    for (int tries = 0;; ++tries) {
         // One coalesced pass, one 32-element block per warp iteration: lane l holds
         // element 32j + l, writes its f16 hi / lo halves into the B-fragment slots
         // and the warp sums the block for the zero-point term (per 16 for Q6_K
@@ -776,13 +783,15 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const __grid_constant_
         half* xh = (half*)stage_x;
         const int s16 = lane >> 4, r16 = lane & 15;
         const int m = 2 * s16 + (r16 >> 3), t = (r16 & 7) >> 1, hp = r16 & 1;
+        bool big = false;
 #pragma unroll 4
-        for (int j = warp; j < KP / 32; j += MV_CWARPS) {
-            const float v = xin(32 * j + lane);
+        for (int j = warp; j < KP / 32; j += MV_CONSUMERS / 32) {
+            const float v = xin(32 * j + lane) * sdown;
             if (TYPE == GT_F32) {
                 stage_x[32 * j + lane] = v;
                 continue;
             }
+            big |= fabsf(v) >= kStageBig;
             // Q4_0 high-nibble positions (k 2t+8, 2t+9) meet A = 16 u 2^-24: pre-divide by 16
             const float vv = (TYPE == GT_Q4_0 && (r16 >> 3)) ? v * 0.0625f : v;
             const half hi = __float2half_rn(vv);
@@ -799,8 +808,10 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const __grid_constant_
                 if (lane == 0) xs16[j] = s;
             }
         }
+        if (!consumer_sync_or(big) || TYPE == GT_F32 || tries == kStageRetries) break;
+        sdown *= kStageDown;
+        sup *= 1.f / kStageDown;
     }
-    consumer_sync();
     pdl_launch();
 
     const int lane = tid & 31, warp = tid >> 5;
@@ -846,8 +857,8 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const __grid_constant_
             const float v = warp_sum(acc.pA);
             if (lane < 16) pb[warp * 16 + lane] = (lane == warp) ? v : 0.f;
         } else if ((lane & 3) == 0) {
-            pb[warp * 16 + (lane >> 2)] = fmaf(acc.pA, kTwo24, -Zero<TYPE>::z * acc.qA);
-            pb[warp * 16 + 8 + (lane >> 2)] = fmaf(acc.pB, kTwo24, -Zero<TYPE>::z * acc.qB);
+            pb[warp * 16 + (lane >> 2)] = fmaf(acc.pA, kTwo24, -Zero<TYPE>::z * acc.qA) * sup;
+            pb[warp * 16 + 8 + (lane >> 2)] = fmaf(acc.pB, kTwo24, -Zero<TYPE>::z * acc.qB) * sup;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&tdone[b]);
@@ -1070,6 +1081,7 @@ struct TkShared {
     int stop;     // consumer thread 0's snapshot of err at a phase start, read after the sync
     int started;  // last phase the consumers entered (epilogue warp follows it)
     int staged;   // last phase whose input the consumers have staged (producer follows it)
+    float sup;    // the staged input's f16 range factor (kStageBig), applied to the row sums
 };
 
 // Profiling stamps (TokenArgs::stamps): [phase][cta][4] = phase entered,
@@ -1203,9 +1215,12 @@ __device__ __forceinline__ void tk_sums(float* xs16, int e0, float4 v, int lane)
 // Input sources, one instantiation each (only the code a phase uses is fetched:
 // staging runs once per phase and is latency-bound, instruction fetch included).
 enum : int { SRC_PLAIN = 0, SRC_EMBED = 1, SRC_XSUM = 2, SRC_ATT = 3 };
+// The staging pass of tk_stage_src at f16 range scale `sdown` (1 in range,
+// then 2^-16 steps, kStageBig); true when an element of the scaled input is
+// still out of range. Ends at the consumers' barrier (which ORs the flag).
 template <int TYPE, int SRC>
-__device__ __noinline__ bool tk_stage_src(const TokenArgs& a, const TokenPhase& P, uint32_t tok, uint32_t pos,
-                                          float* U, float* red, int p, TkShared* sh, unsigned long long target) {
+__device__ __forceinline__ bool tk_stage_body(const TokenArgs& a, const TokenPhase& P, uint32_t tok, uint32_t pos,
+                                              float* U, float* red, float sdown) {
     const MatvecArgs& m = P.mv;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = m.K, KP = ((K + Fmt<TYPE>::CK - 1) / Fmt<TYPE>::CK) * Fmt<TYPE>::CK, nrun = KP / 128;
@@ -1260,8 +1275,7 @@ __device__ __noinline__ bool tk_stage_src(const TokenArgs& a, const TokenPhase& 
     // normed phases: the norm weights were copied to wpre before the barrier
     // (tk_prefetch) when K is a multiple of 4
     const float* wpre = (m.norm_w && !(K & 3)) ? U + KP + KP / 16 : nullptr;
-    if (wpre) cp_async_commit_wait();
-    if (!tk_gate(a, p, sh, target)) return false;
+    bool big = false;
     if constexpr (SRC == SRC_ATT) {
         // the attention output, merged from the softmax partials of each head's
         // splits (src/math/ops.rs:15-25 normalisation, applied to the merged sums):
@@ -1306,6 +1320,8 @@ __device__ __noinline__ bool tk_stage_src(const TokenArgs& a, const TokenPhase& 
                     }
                 }
             }
+            v = scale4(v, sdown);
+            big |= big4(v);
             tk_put4<TYPE>(U, e0, v);
             tk_sums<TYPE>(xs16, e0, v, lane);
         }
@@ -1337,10 +1353,12 @@ __device__ __noinline__ bool tk_stage_src(const TokenArgs& a, const TokenPhase& 
         for (int i = 0; i < TK_NORM_REGS / 4; ++i) {
             const int r = warp + MV_CWARPS * i, e0 = 128 * r + 4 * lane;
             if (r < nrun) {
-                const float4 v = make_float4(__fmul_rn(__fmul_rn(xv[i].x, sc), wv[i].x),
-                                             __fmul_rn(__fmul_rn(xv[i].y, sc), wv[i].y),
-                                             __fmul_rn(__fmul_rn(xv[i].z, sc), wv[i].z),
-                                             __fmul_rn(__fmul_rn(xv[i].w, sc), wv[i].w));
+                const float4 v = scale4(make_float4(__fmul_rn(__fmul_rn(xv[i].x, sc), wv[i].x),
+                                                    __fmul_rn(__fmul_rn(xv[i].y, sc), wv[i].y),
+                                                    __fmul_rn(__fmul_rn(xv[i].z, sc), wv[i].z),
+                                                    __fmul_rn(__fmul_rn(xv[i].w, sc), wv[i].w)),
+                                        sdown);
+                big |= big4(v);
                 tk_put4<TYPE>(U, e0, v);
                 tk_sums<TYPE>(xs16, e0, v, lane);
             }
@@ -1357,13 +1375,33 @@ __device__ __noinline__ bool tk_stage_src(const TokenArgs& a, const TokenPhase& 
             for (int i = 0; i < TK_ROUND; ++i) {
                 const int r = r0 + warp + MV_CWARPS * i;
                 if (r < nrun) {
-                    tk_put4<TYPE>(U, 128 * r + 4 * lane, xv[i]);
-                    tk_sums<TYPE>(xs16, 128 * r + 4 * lane, xv[i], lane);
+                    const float4 v = scale4(xv[i], sdown);
+                    big |= big4(v);
+                    tk_put4<TYPE>(U, 128 * r + 4 * lane, v);
+                    tk_sums<TYPE>(xs16, 128 * r + 4 * lane, v, lane);
                 }
             }
         }
     }
-    consumer_sync();
+    return consumer_sync_or(big);
+}
+
+template <int TYPE, int SRC>
+__device__ __noinline__ bool tk_stage_src(const TokenArgs& a, const TokenPhase& P, uint32_t tok, uint32_t pos,
+                                          float* U, float* red, int p, TkShared* sh, unsigned long long target) {
+    const MatvecArgs& m = P.mv;
+    const int K = m.K, KP = ((K + Fmt<TYPE>::CK - 1) / Fmt<TYPE>::CK) * Fmt<TYPE>::CK;
+    // normed phases: the norm weights were copied to wpre before the barrier
+    // (tk_prefetch) when K is a multiple of 4
+    if (m.norm_w && !(K & 3)) cp_async_commit_wait();
+    (void)KP;
+    if (!tk_gate(a, p, sh, target)) return false;
+    float sup = 1.f;
+    if (tk_stage_body<TYPE, SRC>(a, P, tok, pos, U, red, 1.f) && TYPE != GT_F32) {
+        sup = 1.f / kStageDown;
+        if (tk_stage_body<TYPE, SRC>(a, P, tok, pos, U, red, kStageDown)) atomicOr(&a.step->error, 8u);
+    }
+    if (threadIdx.x == 0) sh->sup = sup;  // read after the consumers' next barrier
     return true;
 }
 
@@ -1839,6 +1877,9 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
                 for (int w = 0; w < MV_CWARPS / 2; ++w) v += pb[(8 * h + w) * 16 + r];
                 const float other = __shfl_xor_sync(0xffffffffu, v, 16);
                 v = h == 0 ? v + other : other + v;
+                // the staged input's f16 range factor (1 unless it was rescaled);
+                // the consumers set it before their first tile's partials
+                v *= *(volatile float*)&sh.sup;
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tfree[b]);
                 if (lane < 16) res[lane] = v;
@@ -2056,17 +2097,25 @@ __global__ void __launch_bounds__(MV_CONSUMERS, 1)
         sok = 1;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    // stage x (all of it: consume_* index the staged input by absolute chunk)
-    for (int r = warp; r < KP / 128; r += MV_CWARPS) {
-        const int e0 = 128 * r + 4 * lane;
-        float t4[4];
+    // stage x (all of it: consume_* index the staged input by absolute chunk),
+    // again scaled by 2^-16 while an element is out of f16 range (kStageBig)
+    float sdown = 1.f, sup = 1.f;
+    for (int tries = 0;; ++tries) {
+        bool big = false;
+        for (int r = warp; r < KP / 128; r += MV_CWARPS) {
+            const int e0 = 128 * r + 4 * lane;
+            float t4[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) t4[i] = e0 + i < K ? x[e0 + i] : 0.f;
-        const float4 v = make_float4(t4[0], t4[1], t4[2], t4[3]);
-        tk_put4<TYPE>(U, e0, v);
-        tk_sums<TYPE>(xs16, e0, v, lane);
+            for (int i = 0; i < 4; ++i) t4[i] = e0 + i < K ? x[e0 + i] : 0.f;
+            const float4 v = scale4(make_float4(t4[0], t4[1], t4[2], t4[3]), sdown);
+            big |= big4(v);
+            tk_put4<TYPE>(U, e0, v);
+            tk_sums<TYPE>(xs16, e0, v, lane);
+        }
+        if (!__syncthreads_or(big) || TYPE == GT_F32 || tries == kStageRetries) break;
+        sdown *= kStageDown;
+        sup *= 1.f / kStageDown;
     }
-    __syncthreads();
     Acc acc = {0.f, 0.f, 0.f, 0.f};
     bool ok = true;
     int issued = 0;  // thread 0: chunks copied
@@ -2101,8 +2150,8 @@ __global__ void __launch_bounds__(MV_CONSUMERS, 1)
         const float v = warp_sum(acc.pA);
         if (lane < 16) red[warp * 16 + lane] = (lane == warp) ? v : 0.f;
     } else if ((lane & 3) == 0) {
-        red[warp * 16 + (lane >> 2)] = fmaf(acc.pA, kTwo24, -Zero<TYPE>::z * acc.qA);
-        red[warp * 16 + 8 + (lane >> 2)] = fmaf(acc.pB, kTwo24, -Zero<TYPE>::z * acc.qB);
+        red[warp * 16 + (lane >> 2)] = fmaf(acc.pA, kTwo24, -Zero<TYPE>::z * acc.qA) * sup;
+        red[warp * 16 + 8 + (lane >> 2)] = fmaf(acc.pB, kTwo24, -Zero<TYPE>::z * acc.qB) * sup;
     }
     __syncthreads();
     if (tid < 16) {
@@ -2231,407 +2280,5 @@ cudaError_t launch_token(const TokenArgs& a, int grid, cudaStream_t s, bool coop
     return cudaLaunchKernelEx(&cfg, k_token, a);
 }
 
-
-// ============================================================================
-// Batched decode (up to MB_SEQ sequences per weight pass)
-// ============================================================================
-//
-// The same weight fragments and MMAs as k_matvec, but the B operand's eight
-// columns are four sequences' (hi, lo) activation parts instead of one
-// sequence's: lane 8s + 4h + t of a block's fragment record holds sequence s,
-// part h (0 hi, 1 lo), k pair t. The MMA's D fragment then gives lane l the
-// row value of sequence l % 4, so the per-lane math of the single-sequence
-// consumers is unchanged; only where the B fragment and the block sums come
-// from differs. The activation cannot be staged whole (4 x K floats), so each
-// ring stage carries, after the tile's two group-chunks, the chunk of
-// formatted activation they meet (fragments + block sums, one bulk copy each).
-
-template <int TYPE>
-struct FmtB {
-    static constexpr int NSUM = TYPE == GT_Q6_K ? Fmt<TYPE>::CK / 16 : Fmt<TYPE>::CK / 32;  // sums per chunk, per seq
-    static constexpr int XFB = Fmt<TYPE>::CK / 32 * 512;  // fragment bytes per chunk
-    static constexpr int XSB = NSUM * MB_SEQ * 4;         // sum bytes per chunk
-    static constexpr int WB = 2 * Fmt<TYPE>::GCB;
-    static constexpr int STAGE = WB + XFB + XSB;
-    static constexpr int NST = 4;
-};
-
-static int ck_host(int type) { return fmt_ck(type); }
-
-size_t xfmt_frag_bytes(int type, int K) {
-    const int ck = ck_host(type);
-    if (!ck || type == GT_F32) return 0;
-    const size_t kp = (size_t)ceil_div_h(K, ck) * ck;
-    return kp / 32 * 512;
-}
-size_t xfmt_sum_bytes(int type, int K) {
-    const int ck = ck_host(type);
-    if (!ck || type == GT_F32) return 0;
-    const size_t kp = (size_t)ceil_div_h(K, ck) * ck;
-    return (type == GT_Q6_K ? kp / 16 : kp / 32) * MB_SEQ * 4;
-}
-
-// One CTA per (8 blocks, sequence): RMSNorm scale of the sequence (summed over
-// all of K by every CTA of that sequence, in one fixed order), then lane l of
-// warp w formats element 32 j + l of block j = 8 bx + w, like k_matvec's staging.
-template <int TYPE>
-__global__ void __launch_bounds__(256) k_xfmt_b(const float* x, int ldx, int K, int KP, const float* norm_w, float eps,
-                                                const BatchParams* bp, half* frag, float* sums) {
-    const int s = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const bool live = s < bp->n;
-    const float* xs = x + (size_t)s * ldx;
-    __shared__ float red[8];
-    float scale = 1.f;
-    if (norm_w && live) {  // src/math/ops.rs:5-12
-        float ss = 0.f;
-        for (int k = tid; k < K; k += 256) {
-            const float v = xs[k];
-            ss = fmaf(v, v, ss);
-        }
-        ss = warp_sum(ss);
-        if (lane == 0) red[warp] = ss;
-        __syncthreads();
-        float tot = 0.f;
-#pragma unroll
-        for (int w = 0; w < 8; ++w) tot += red[w];
-        scale = 1.0f / sqrtf(tot / (float)K + eps);
-    }
-    const int j = blockIdx.x * 8 + warp;
-    if (32 * j >= KP) return;
-    const int e = 32 * j + lane;
-    float v = 0.f;
-    if (live && e < K) {
-        v = xs[e];
-        if (norm_w) v = __fmul_rn(__fmul_rn(v, scale), norm_w[e]);
-    }
-    const int s16 = lane >> 4, r16 = lane & 15;
-    const int m = 2 * s16 + (r16 >> 3), t = (r16 & 7) >> 1, hp = r16 & 1;
-    const float vv = (TYPE == GT_Q4_0 && (r16 >> 3)) ? v * 0.0625f : v;
-    const half hi = __float2half_rn(vv);
-    const half lo = __float2half_rn(vv - __half2float(hi));
-    frag[((j * 32 + 8 * s + t) * 4 + m) * 2 + hp] = hi;
-    frag[((j * 32 + 8 * s + 4 + t) * 4 + m) * 2 + hp] = lo;
-    float sm = v;
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
-    if (TYPE == GT_Q6_K) {
-        if (r16 == 0) sums[(2 * j + s16) * MB_SEQ + s] = sm;
-    } else {
-        sm += __shfl_xor_sync(0xffffffffu, sm, 16);
-        if (lane == 0) sums[j * MB_SEQ + s] = sm;
-    }
-}
-
-cudaError_t launch_xfmt_b(int type, const float* x, int ldx, int K, const float* norm_w, float eps,
-                          const BatchParams* bp, void* frag, float* sums, cudaStream_t s) {
-    const int ck = ck_host(type);
-    if (!ck || type == GT_F32) return cudaErrorInvalidValue;
-    const int KP = ceil_div_h(K, ck) * ck;
-    const dim3 grid(ceil_div_h(KP / 32, 8), MB_SEQ);
-    switch (type) {
-        case GT_Q4_0: k_xfmt_b<GT_Q4_0><<<grid, 256, 0, s>>>(x, ldx, K, KP, norm_w, eps, bp, (half*)frag, sums); break;
-        case GT_Q8_0: k_xfmt_b<GT_Q8_0><<<grid, 256, 0, s>>>(x, ldx, K, KP, norm_w, eps, bp, (half*)frag, sums); break;
-        case GT_Q6_K: k_xfmt_b<GT_Q6_K><<<grid, 256, 0, s>>>(x, ldx, K, KP, norm_w, eps, bp, (half*)frag, sums); break;
-        default: return cudaErrorInvalidValue;
-    }
-    return cudaGetLastError();
-}
-
-// Batched consumers: one stage (group-chunks A, B; activation chunk xf / xs) ->
-// per-lane partial sums of row (lane / 4) (+8 for B) of sequence lane % 4.
-__device__ __forceinline__ void consume_q4_0_b(const uint8_t* sA, const uint8_t* sB, const uint4* xf, const float* xs,
-                                               Acc& acc) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sq = lane & 3;
-    constexpr int QPC = Fmt<GT_Q4_0>::CK / 128;
-    const uint4 wa = *(const uint4*)(sA + (warp * 32 + lane) * 16);
-    const uint4 wb = *(const uint4*)(sB + (warp * 32 + lane) * 16);
-    const uint2 ca = *(const uint2*)(sA + QPC * 512 + (warp * 8 + (lane >> 2)) * 8);
-    const uint2 cb = *(const uint2*)(sB + QPC * 512 + (warp * 8 + (lane >> 2)) * 8);
-    const float2 a01 = __half22float2(*reinterpret_cast<const half2*>(&ca.x));
-    const float2 a23 = __half22float2(*reinterpret_cast<const half2*>(&ca.y));
-    const float2 b01 = __half22float2(*reinterpret_cast<const half2*>(&cb.x));
-    const float2 b23 = __half22float2(*reinterpret_cast<const half2*>(&cb.y));
-    const float dA[4] = {a01.x, a01.y, a23.x, a23.y};
-    const float dB[4] = {b01.x, b01.y, b23.x, b23.y};
-    const uint32_t xa[4] = {wa.x, wa.y, wa.z, wa.w};
-    const uint32_t xb[4] = {wb.x, wb.y, wb.z, wb.w};
-    const int blk0 = warp * 4;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const uint4 bx = xf[(blk0 + j) * 32 + lane];
-        const float S = xs[(blk0 + j) * MB_SEQ + sq];
-        float d[4];
-        mma_z(d, xa[j] & 0x000F000Fu, xb[j] & 0x000F000Fu, xa[j] & 0x00F000F0u, xb[j] & 0x00F000F0u, bx.x, bx.y);
-        const uint32_t ya = xa[j] >> 8, yb = xb[j] >> 8;
-        mma_acc(d, ya & 0x000F000Fu, yb & 0x000F000Fu, ya & 0x00F000F0u, yb & 0x00F000F0u, bx.z, bx.w);
-        acc.pA = fmaf(dA[j], d[0], fmaf(dA[j], d[1], acc.pA));
-        acc.pB = fmaf(dB[j], d[2], fmaf(dB[j], d[3], acc.pB));
-        acc.qA = fmaf(dA[j], S, acc.qA);
-        acc.qB = fmaf(dB[j], S, acc.qB);
-    }
-}
-
-__device__ __forceinline__ void consume_q8_0_b(const uint8_t* sA, const uint8_t* sB, const uint4* xf, const float* xs,
-                                               Acc& acc) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sq = lane & 3;
-    const int quad = warp >> 1, half_ = warp & 1;
-    const uint4 wa = *(const uint4*)(sA + (quad * 32 + lane) * 32 + half_ * 16);
-    const uint4 wb = *(const uint4*)(sB + (quad * 32 + lane) * 32 + half_ * 16);
-    const uint32_t ca = *(const uint32_t*)(sA + 8 * 1024 + (quad * 8 + (lane >> 2)) * 8 + half_ * 4);
-    const uint32_t cb = *(const uint32_t*)(sB + 8 * 1024 + (quad * 8 + (lane >> 2)) * 8 + half_ * 4);
-    const float2 fa = __half22float2(*reinterpret_cast<const half2*>(&ca));
-    const float2 fb = __half22float2(*reinterpret_cast<const half2*>(&cb));
-    const float dA[2] = {fa.x, fa.y};
-    const float dB[2] = {fb.x, fb.y};
-    const uint32_t A[4] = {wa.x ^ 0x80808080u, wa.y ^ 0x80808080u, wa.z ^ 0x80808080u, wa.w ^ 0x80808080u};
-    const uint32_t B[4] = {wb.x ^ 0x80808080u, wb.y ^ 0x80808080u, wb.z ^ 0x80808080u, wb.w ^ 0x80808080u};
-    const int blk0 = warp * 2;
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        const uint4 bx = xf[(blk0 + j) * 32 + lane];
-        const float S = xs[(blk0 + j) * MB_SEQ + sq];
-        float d[4];
-        mma_z(d, bytes_sub(A[2 * j], 0x4140), bytes_sub(B[2 * j], 0x4140), bytes_sub(A[2 * j], 0x4342),
-              bytes_sub(B[2 * j], 0x4342), bx.x, bx.y);
-        mma_acc(d, bytes_sub(A[2 * j + 1], 0x4140), bytes_sub(B[2 * j + 1], 0x4140), bytes_sub(A[2 * j + 1], 0x4342),
-                bytes_sub(B[2 * j + 1], 0x4342), bx.z, bx.w);
-        acc.pA = fmaf(dA[j], d[0], fmaf(dA[j], d[1], acc.pA));
-        acc.pB = fmaf(dB[j], d[2], fmaf(dB[j], d[3], acc.pB));
-        acc.qA = fmaf(dA[j], S, acc.qA);
-        acc.qB = fmaf(dB[j], S, acc.qB);
-    }
-}
-
-__device__ __forceinline__ void consume_q6_k_b(const uint8_t* sA, const uint8_t* sB, const uint4* xf, const float* xs,
-                                               Acc& acc) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sq = lane & 3;
-    const int row = lane >> 2;
-    const uint32_t scA = *(const uint32_t*)(sA + 16 * 512 + row * 64 + warp * 4);
-    const uint32_t scB = *(const uint32_t*)(sB + 16 * 512 + row * 64 + warp * 4);
-    const float dA = __half2float(*(const half*)(sA + 16 * 512 + 8 * 64 + (row * 4 + (warp >> 2)) * 2));
-    const float dB = __half2float(*(const half*)(sB + 16 * 512 + 8 * 64 + (row * 4 + (warp >> 2)) * 2));
-    const uint4 wa = *(const uint4*)(sA + (warp * 32 + lane) * 16);
-    const uint4 wb = *(const uint4*)(sB + (warp * 32 + lane) * 16);
-    const uint32_t A[4] = {wa.x, wa.y, wa.z, wa.w};
-    const uint32_t B[4] = {wb.x, wb.y, wb.z, wb.w};
-    const int step0 = warp * 4;
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-        const int blk = (step0 + 2 * p) / 2;
-        const uint4 bx = xf[blk * 32 + lane];
-        const float s0 = xs[(step0 + 2 * p) * MB_SEQ + sq], s1 = xs[(step0 + 2 * p + 1) * MB_SEQ + sq];
-        float d0[4], d1[4];
-        mma_z(d0, bytes_sub(A[2 * p], 0x4140), bytes_sub(B[2 * p], 0x4140), bytes_sub(A[2 * p], 0x4342),
-              bytes_sub(B[2 * p], 0x4342), bx.x, bx.y);
-        mma_z(d1, bytes_sub(A[2 * p + 1], 0x4140), bytes_sub(B[2 * p + 1], 0x4140), bytes_sub(A[2 * p + 1], 0x4342),
-              bytes_sub(B[2 * p + 1], 0x4342), bx.z, bx.w);
-        const float a0 = __fmul_rn(dA, (float)(int8_t)(scA >> (16 * p))),
-                    a1 = __fmul_rn(dA, (float)(int8_t)(scA >> (16 * p + 8)));
-        const float b0 = __fmul_rn(dB, (float)(int8_t)(scB >> (16 * p))),
-                    b1 = __fmul_rn(dB, (float)(int8_t)(scB >> (16 * p + 8)));
-        acc.pA = fmaf(a0, d0[0] + d0[1], acc.pA);
-        acc.pA = fmaf(a1, d1[0] + d1[1], acc.pA);
-        acc.qA = fmaf(a0, s0, fmaf(a1, s1, acc.qA));
-        acc.pB = fmaf(b0, d0[2] + d0[3], acc.pB);
-        acc.pB = fmaf(b1, d1[2] + d1[3], acc.pB);
-        acc.qB = fmaf(b0, s0, fmaf(b1, s1, acc.qB));
-    }
-}
-
-// Roles as k_matvec: producer warp (weights + activation chunk per stage), 16
-// consumer warps, epilogue warp (reduces a tile's 16 x 64 partials in warp
-// order and stores / adds the 16 rows x 4 sequences).
-template <int TYPE>
-__global__ void __launch_bounds__(MV_THREADS, 1) k_matvec_b(const __grid_constant__ BatchMvArgs a) {
-    using F = FmtB<TYPE>;
-    constexpr int NST = F::NST, GCB = Fmt<TYPE>::GCB, CK = Fmt<TYPE>::CK;
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int tid = threadIdx.x;
-    const int nchunk = (a.K + CK - 1) / CK;
-    uint8_t* ring = smem;
-    uint64_t* full = (uint64_t*)(smem + NST * F::STAGE);
-    uint64_t* empty = full + NST;
-    uint64_t* tdone = empty + NST;  // [2]
-    uint64_t* tfree = tdone + 2;    // [2]
-    float* part = (float*)(tfree + 2);  // [2][16 warps][64]
-    __shared__ int s_err;
-    if (tid == 0) {
-        for (int i = 0; i < NST; ++i) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], MV_CWARPS);
-        }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&tdone[i], MV_CWARPS);
-            mbar_init(&tfree[i], 1);
-        }
-        s_err = 0;
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
-    const int lane = tid & 31;
-
-    if (tid >= MV_CONSUMERS + 32) {
-        // ---------------- epilogue warp
-        const int n = a.bp->n, sq = lane & 3, r = lane >> 2;
-        const uint32_t pos = sq < n ? a.bp->pos[sq] : 0u;
-        int it = 0;
-        for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, ++it) {
-            int si = 0, lt = t;
-            while (si + 1 < a.nseg && lt >= a.seg[si].ntiles) lt -= a.seg[si++].ntiles;
-            const BatchSeg& sg = a.seg[si];
-            const int b = it & 1;
-            if (!mbar_wait(&tdone[b], (uint32_t)(it >> 1) & 1)) {
-                s_err = 1;
-                atomicOr((unsigned*)&a.bp->error, 2u);
-                return;
-            }
-            const float* pb = part + b * MV_CWARPS * 64;
-            // v0: row r of sequence sq, v1: row r + 8 (for a pair: gate row r, up row r)
-            float v0 = 0.f, v1 = 0.f;
-#pragma unroll
-            for (int w = 0; w < MV_CWARPS; ++w) {
-                v0 += pb[w * 64 + lane];
-                v1 += pb[w * 64 + 32 + lane];
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tfree[b]);
-            const bool live = sq < n;
-            float* ys = sg.y + (size_t)sq * sg.ldy;
-            if (sg.epi == EPI_B_SWIGLU) {  // src/math/ops.rs:33-37
-                const int row = 8 * lt + r;
-                if (live && row < sg.rows) ys[row] = __fmul_rn(silu_ref(v0), v1);
-            } else if (sg.epi >= EPI_B_ROPE) {
-                // pairs (2i, 2i+1) sit on lanes l and l ^ 4 (src/math/ops.rs:48-61)
-                const float p0 = __shfl_xor_sync(0xffffffffu, v0, 4), p1 = __shfl_xor_sync(0xffffffffu, v1, 4);
-                float* dst = sg.epi == EPI_B_ROPE ? ys
-                             : (sg.epi == EPI_B_KCACHE ? a.kc : a.vc) + (size_t)sq * a.seq_stride + (size_t)pos * a.kv_dim;
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int row = 16 * lt + r + 8 * h;
-                    const float v = h ? v1 : v0, pv = h ? p1 : p0;
-                    float o = v;
-                    if (sg.epi != EPI_B_VCACHE) {
-                        const float2 c = a.rope_cs[(size_t)pos * (a.hd >> 1) + ((row % a.hd) >> 1)];
-                        o = (row & 1) ? __fadd_rn(__fmul_rn(pv, c.y), __fmul_rn(v, c.x))
-                                      : __fsub_rn(__fmul_rn(v, c.x), __fmul_rn(pv, c.y));
-                    }
-                    if (live && row < sg.rows) dst[row] = o;
-                }
-            } else {
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int row = 16 * lt + r + 8 * h;
-                    const float v = h ? v1 : v0;
-                    if (live && row < sg.rows) ys[row] = sg.epi == EPI_B_ADD ? __fadd_rn(ys[row], v) : v;
-                }
-            }
-        }
-        return;
-    }
-    if (tid >= MV_CONSUMERS) {
-        // ---------------- producer warp
-        if (tid == MV_CONSUMERS) {
-            uint32_t it = 0;
-            bool ok = true;
-            for (int t = blockIdx.x; t < a.ntiles && ok; t += gridDim.x) {
-                int si = 0, lt = t;
-                while (si + 1 < a.nseg && lt >= a.seg[si].ntiles) lt -= a.seg[si++].ntiles;
-                const BatchSeg& sg = a.seg[si];
-                const PackedW& WB = sg.pair ? sg.B : sg.A;
-                const uint8_t* ga0 = (const uint8_t*)sg.A.p0 + (size_t)(sg.pair ? lt : 2 * lt) * sg.A.nk * GCB;
-                const uint8_t* gb0 = (const uint8_t*)WB.p0 + (size_t)(sg.pair ? lt : 2 * lt + 1) * WB.nk * GCB;
-                for (int c = 0; c < nchunk; ++c, ++it) {
-                    const int slot = it % NST;
-                    if (!mbar_wait(&empty[slot], ((it / NST) & 1) ^ 1) || *(volatile int*)&s_err) {
-                        ok = false;
-                        break;
-                    }
-                    uint8_t* dst = ring + slot * F::STAGE;
-                    mbar_expect_tx(&full[slot], F::STAGE);
-                    bulk_g2s(dst, ga0 + (size_t)c * GCB, GCB, &full[slot]);
-                    bulk_g2s(dst + GCB, gb0 + (size_t)c * GCB, GCB, &full[slot]);
-                    bulk_g2s(dst + F::WB, (const uint8_t*)a.frag + (size_t)c * F::XFB, F::XFB, &full[slot]);
-                    bulk_g2s(dst + F::WB + F::XFB, (const uint8_t*)a.sums + (size_t)c * F::XSB, F::XSB, &full[slot]);
-                }
-            }
-            const uint32_t first = it > (uint32_t)NST ? it - NST : 0;
-            for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % NST], (j / NST) & 1);
-            if (!ok) {
-                s_err = 1;
-                atomicOr((unsigned*)&a.bp->error, 2u);
-            }
-        }
-        return;
-    }
-
-    // ---------------- consumers
-    const int warp = tid >> 5;
-    uint32_t it = 0;
-    int nt = 0;
-    for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, ++nt) {
-        Acc acc = {0.f, 0.f, 0.f, 0.f};
-        for (int c = 0; c < nchunk; ++c, ++it) {
-            const int slot = it % NST;
-            if (!mbar_wait(&full[slot], (it / NST) & 1)) {
-                s_err = 1;
-                atomicOr((unsigned*)&a.bp->error, 2u);
-                return;
-            }
-            const uint8_t* st = ring + slot * F::STAGE;
-            const uint4* xf = (const uint4*)(st + F::WB);
-            const float* xs = (const float*)(st + F::WB + F::XFB);
-            if (TYPE == GT_Q4_0)
-                consume_q4_0_b(st, st + GCB, xf, xs, acc);
-            else if (TYPE == GT_Q8_0)
-                consume_q8_0_b(st, st + GCB, xf, xs, acc);
-            else
-                consume_q6_k_b(st, st + GCB, xf, xs, acc);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-        }
-        const int b = nt & 1;
-        if (!mbar_wait(&tfree[b], ((uint32_t)(nt >> 1) & 1u) ^ 1u)) {
-            s_err = 1;
-            atomicOr((unsigned*)&a.bp->error, 2u);
-            return;
-        }
-        float* pb = part + b * MV_CWARPS * 64 + warp * 64;
-        // row r (A: lane / 4, B: + 8) of sequence lane % 4 -> index 4 r + s
-        pb[(lane >> 2) * 4 + (lane & 3)] = fmaf(acc.pA, kTwo24, -Zero<TYPE>::z * acc.qA);
-        pb[((lane >> 2) + 8) * 4 + (lane & 3)] = fmaf(acc.pB, kTwo24, -Zero<TYPE>::z * acc.qB);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tdone[b]);
-    }
-}
-
-template <int TYPE>
-static size_t matvec_b_smem() {
-    using F = FmtB<TYPE>;
-    return (size_t)F::NST * F::STAGE + (2 * F::NST + 4) * 8 + 2 * MV_CWARPS * 64 * 4;
-}
-
-cudaError_t matvec_b_configure() {
-    cudaError_t e;
-    if ((e = cudaFuncSetAttribute(k_matvec_b<GT_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)matvec_b_smem<GT_Q4_0>())))
-        return e;
-    if ((e = cudaFuncSetAttribute(k_matvec_b<GT_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)matvec_b_smem<GT_Q8_0>())))
-        return e;
-    return cudaFuncSetAttribute(k_matvec_b<GT_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)matvec_b_smem<GT_Q6_K>());
-}
-
-cudaError_t launch_matvec_b(const BatchMvArgs& a, int max_ctas, cudaStream_t s) {
-    if (a.ntiles <= 0) return cudaSuccess;
-    const int grid = a.ntiles < max_ctas ? a.ntiles : max_ctas;
-    switch (a.seg[0].A.type) {
-        case GT_Q4_0: k_matvec_b<GT_Q4_0><<<grid, MV_THREADS, matvec_b_smem<GT_Q4_0>(), s>>>(a); break;
-        case GT_Q8_0: k_matvec_b<GT_Q8_0><<<grid, MV_THREADS, matvec_b_smem<GT_Q8_0>(), s>>>(a); break;
-        case GT_Q6_K: k_matvec_b<GT_Q6_K><<<grid, MV_THREADS, matvec_b_smem<GT_Q6_K>(), s>>>(a); break;
-        default: return cudaErrorInvalidValue;
-    }
-    return cudaGetLastError();
-}
 
 }  // namespace talos

@@ -344,7 +344,7 @@ static talos_status device_setup(int device) {
         g_cfg_err = matvec_configure();
         if (g_cfg_err == cudaSuccess) g_cfg_err = attention_configure();
         if (g_cfg_err == cudaSuccess) g_cfg_err = token_configure();
-        if (g_cfg_err == cudaSuccess) g_cfg_err = matvec_b_configure();
+        if (g_cfg_err == cudaSuccess) g_cfg_err = gemm_configure();
     });
     if (g_cfg_err != cudaSuccess) return set_err(TALOS_ERR_CUDA, "matvec_configure: %s", cudaGetErrorString(g_cfg_err));
     if (device < 64 && g_sms[device] == 0) {
@@ -440,36 +440,42 @@ struct talos_ctx {
     std::vector<std::pair<cudaEvent_t, int>>* prof = nullptr;
     std::vector<LayerW> layers;
 
-    // batched decode (talos_ctx_set_batch): one allocation for the parameters,
-    // the [MB_SEQ][..] activations, the formatted-input scratch and the caches
-    int bmax = 0;
+    // batched steps (talos_forward_batch, talos_prefill, talos_perplexity): one
+    // allocation for the parameters, the [MB_SEQ][..] activations, the GEMM's
+    // formatted input and split-K workspace, and the sequences' cache slots
+    int bmax = 0;              // sequences with cache slots (talos_ctx_set_batch)
     void* bmem = nullptr;
     size_t bbytes = 0;
     BatchParams* bp = nullptr;
     BatchParams* h_bp = nullptr;  // pinned
     float *bx = nullptr, *bq = nullptr, *batt = nullptr;
-    float *bg = nullptr, *bu = nullptr, *bh = nullptr, *blog = nullptr, *bsums = nullptr;
-    void* bfrag = nullptr;
+    float *bh = nullptr, *blog = nullptr;
+    void* bplanes = nullptr;   // [2][MB_SEQ][bldp] f16: the GEMM input's hi / lo planes
+    float* bxs = nullptr;      // [MB_SEQ] per-column scales of the formatted input
+    int bldp = 0;
+    float* bws = nullptr;      // split-K partial tiles
+    unsigned* bcnt = nullptr;  // split-K arrival counters (zero between launches)
     float *bkc = nullptr, *bvc = nullptr;  // [bmax][n_layer][kv_ctx][kv_dim]
     size_t bseq_stride = 0;                // floats per sequence in bkc / bvc
-    float* h_blog = nullptr;               // pinned [MB_SEQ][V]
-    cudaGraphExec_t bgraph = nullptr;
-    cudaGraphExec_t bgraph_pf = nullptr;  // the same step on the main cache: chunked prefill
+    float* h_blog = nullptr;               // pinned [TALOS_MAX_BATCH][V]
+    alignas(64) uint8_t bmaps[3][128];     // tensor maps of bplanes for 32 / 64 / 128-column tiles
+    cudaGraphExec_t bgraph[3][3] = {};     // [BatchMode][token-tile size]
 
+    void drop_batch_graphs() {
+        for (auto& row : bgraph)
+            for (auto& g : row)
+                if (g) {
+                    cudaGraphExecDestroy(g);
+                    g = nullptr;
+                }
+    }
     void drop_graphs() {
         for (auto& g : graph)
             if (g) {
                 cudaGraphExecDestroy(g);
                 g = nullptr;
             }
-        if (bgraph) {
-            cudaGraphExecDestroy(bgraph);
-            bgraph = nullptr;
-        }
-        if (bgraph_pf) {
-            cudaGraphExecDestroy(bgraph_pf);
-            bgraph_pf = nullptr;
-        }
+        drop_batch_graphs();
         for (auto& p : d_phases)
             if (p) {
                 cudaFree(p);
@@ -1496,14 +1502,19 @@ static talos_status set_step(talos_ctx* c, uint32_t token, size_t pos) {
 }
 
 // Error bits of StepParams::error: 1 = token id out of range, 2 = the weight
-// stream gave up waiting, 4 = a barrier or hand-off wait ran out.
+// stream gave up waiting, 4 = a barrier or hand-off wait ran out, 8 = a matvec
+// input of the per-token kernel stayed beyond the f16 hi / lo split's range
+// after its one 2^-16 rescale (an element of magnitude 2^31 or more).
 static talos_status finish_step(talos_ctx* c) {
     CK(cudaMemcpyAsync(c->h_step, c->step, sizeof(StepParams), cudaMemcpyDeviceToHost, c->stream));
     CK(cudaStreamSynchronize(c->stream));
     const uint32_t err = c->h_step->error;
     if (!err) return TALOS_OK;
     reset_sync(c);
-    if (err & ~1u) return set_err(TALOS_ERR_TIMEOUT, "a bounded device wait ran out (code %u)", err);
+    if (err & 6u) return set_err(TALOS_ERR_TIMEOUT, "a bounded device wait ran out (code %u)", err);
+    if (err & 8u)
+        return set_err(TALOS_ERR_UNSUPPORTED, "an activation of magnitude 2^31 or more (code %u); the layered "
+                       "step kernel (TALOS_STEP_LAYERED) rescales further", err);
     return set_err(TALOS_ERR_OOB, "device bounds check fired (code %u)", err);
 }
 
@@ -1620,22 +1631,32 @@ static talos_status profile_fused(talos_ctx* c, double* kernel_ms, uint32_t* lau
     return TALOS_OK;
 }
 
-// ------------------------------------------------------------------ batched decode
+// ------------------------------------------------------------------ batched steps
 //
-// Up to MB_SEQ independent sequences per step (the batched drivers of the
-// workload: several prompts decoded together). Each weight is read once per
-// step for all of them: the batched matvec puts four sequences in the MMA's B
-// columns. The step is the layered sequence of src/model/llama.rs:96-183 with
-// per-sequence positions and caches, captured once as a CUDA graph that reads
-// the sequence count, tokens and positions from device memory.
+// Up to MB_SEQ token columns per step, every weight read once per step for all
+// of them through the tcgen05 GEMM (gemm.cu). Three uses, one captured CUDA
+// graph per use and token-tile size (32, 64 or 128 columns), each reading the
+// column count, tokens and positions from device memory:
+//  * BM_DECODE (talos_forward_batch): independent sequences, each with its own
+//    cache slot and position, and their logits;
+//  * BM_PREFILL (talos_prefill): consecutive prompt positions of the one
+//    sequence of the main cache (src/main.rs:88-95), no logits;
+//  * BM_SCORE (talos_perplexity): the same with every column's logits.
+// The step is the layered sequence of src/model/llama.rs:96-183 per column:
+// embedding row; per layer GEMM q/k/v (RoPE, cache append), attention, GEMM
+// o-proj (+ residual), GEMM gate/up (SwiGLU), GEMM down (+ residual); then the
+// final norm and the output GEMM. A column at position p attends to positions
+// 0 .. p of its cache, so prompt positions of one step see each other's rows.
+
+enum BatchMode { BM_DECODE = 0, BM_PREFILL = 1, BM_SCORE = 2 };
+static int nt_of(int ntc) { return 32 << ntc; }
+static int ntc_for(int n) { return n <= 32 ? 0 : (n <= 64 ? 1 : 2); }
+constexpr int GM_MAX_WAVES = 5;   // split-K never makes more than 5 units per SM
+constexpr int GM_MAX_CNT = 4096;  // split-K counters (4 per output tile)
 
 static talos_status batch_free(talos_ctx* c) {
     CK(cudaStreamSynchronize(c->stream));
-    for (cudaGraphExec_t* g : {&c->bgraph, &c->bgraph_pf})
-        if (*g) {
-            cudaGraphExecDestroy(*g);
-            *g = nullptr;
-        }
+    c->drop_batch_graphs();
     if (c->bmem) cudaFree(c->bmem);
     c->bmem = nullptr;
     c->bbytes = 0;
@@ -1643,12 +1664,13 @@ static talos_status batch_free(talos_ctx* c) {
     return TALOS_OK;
 }
 
-// The batched step's buffers, with cache slots for max_seqs sequences (0: the
-// activations only, for the chunked prefill on the main cache).
+// The batched steps' buffers, with cache slots for max_seqs sequences (0: the
+// activations only, for prefill and perplexity on the main cache).
 static talos_status batch_alloc(talos_ctx* c, int max_seqs) {
     TRY(batch_free(c));
     const size_t E = c->cfg.n_embd, F = c->cfg.n_ff, V = c->cfg.vocab_size, L = c->cfg.n_layer;
-    const size_t KPmax = ((std::max(E, F) + 2047) / 2048) * 2048;  // largest chunk-rounded input
+    const size_t KPmax = ((std::max(E, F) + 127) / 128) * 128;  // largest GEMM input, rounded to 128
+    const int sms = sm_count_dev(c->device);
     size_t off = 0;
     auto take = [&](size_t bytes) {
         size_t o = off;
@@ -1657,9 +1679,9 @@ static talos_status batch_alloc(talos_ctx* c, int max_seqs) {
     };
     const size_t o_bp = take(sizeof(BatchParams));
     const size_t o_x = take(MB_SEQ * E * 4), o_q = take(MB_SEQ * c->q_rows * 4), o_att = take(MB_SEQ * E * 4),
-                 o_g = take(MB_SEQ * F * 4),
-                 o_u = take(MB_SEQ * F * 4), o_h = take(MB_SEQ * F * 4), o_log = take(MB_SEQ * V * 4);
-    const size_t o_frag = take(KPmax / 32 * 512), o_sums = take(KPmax / 16 * MB_SEQ * 4);
+                 o_h = take(MB_SEQ * F * 4), o_log = take(MB_SEQ * V * 4);
+    const size_t o_pl = take(2 * MB_SEQ * KPmax * 2), o_xs = take(MB_SEQ * 4);
+    const size_t o_ws = take((size_t)GM_MAX_WAVES * sms * 128 * 128 * 4), o_cnt = take(GM_MAX_CNT * 4);
     const size_t seq_stride = L * c->kv_ctx * (size_t)c->kv_dim;
     const size_t o_kc = take((size_t)max_seqs * seq_stride * 4 + 4), o_vc = take((size_t)max_seqs * seq_stride * 4 + 4);
     void* mem = nullptr;
@@ -1670,12 +1692,19 @@ static talos_status batch_alloc(talos_ctx* c, int max_seqs) {
     c->bbytes = off;
     c->bp = (BatchParams*)(b + o_bp);
     c->bx = (float*)(b + o_x), c->bq = (float*)(b + o_q);
-    c->batt = (float*)(b + o_att), c->bg = (float*)(b + o_g), c->bu = (float*)(b + o_u), c->bh = (float*)(b + o_h);
-    c->blog = (float*)(b + o_log), c->bfrag = b + o_frag, c->bsums = (float*)(b + o_sums);
+    c->batt = (float*)(b + o_att), c->bh = (float*)(b + o_h);
+    c->blog = (float*)(b + o_log);
+    c->bplanes = b + o_pl, c->bxs = (float*)(b + o_xs), c->bldp = (int)KPmax;
+    c->bws = (float*)(b + o_ws), c->bcnt = (unsigned*)(b + o_cnt);
     c->bkc = (float*)(b + o_kc), c->bvc = (float*)(b + o_vc);
     c->bseq_stride = seq_stride;
+    if (gemm_map_bytes() > sizeof c->bmaps[0]) return set_err(TALOS_ERR_CUDA, "tensor map larger than its slot");
+    for (int i = 0; i < 3; ++i) {
+        cudaError_t e = gemm_tensor_map(c->bplanes, c->bldp, MB_SEQ, nt_of(i), c->bmaps[i]);
+        if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "tensor map: %s", cudaGetErrorString(e));
+    }
     if (!c->h_bp) CK(cudaMallocHost(&c->h_bp, sizeof(BatchParams)));
-    if (!c->h_blog) CK(cudaMallocHost(&c->h_blog, MB_SEQ * V * 4));
+    if (!c->h_blog) CK(cudaMallocHost(&c->h_blog, (size_t)TALOS_MAX_BATCH * V * 4));
     c->bmax = max_seqs;
     CK(cudaStreamSynchronize(c->stream));
     return TALOS_OK;
@@ -1683,29 +1712,28 @@ static talos_status batch_alloc(talos_ctx* c, int max_seqs) {
 
 extern "C" talos_status talos_ctx_set_batch(talos_ctx* c, int max_seqs) {
     if (!c) return set_err(TALOS_ERR_INVALID_ARG, "NULL ctx");
-    if (max_seqs < 0 || max_seqs > MB_SEQ)
-        return set_err(TALOS_ERR_INVALID_ARG, "batch of %d sequences (at most %d)", max_seqs, MB_SEQ);
+    if (max_seqs < 0 || max_seqs > TALOS_MAX_BATCH)
+        return set_err(TALOS_ERR_INVALID_ARG, "batch of %d sequences (at most %d)", max_seqs, TALOS_MAX_BATCH);
     if (c->tp > 1) return set_err(TALOS_ERR_UNSUPPORTED, "batched decode under tensor parallelism");
     CK(cudaSetDevice(c->device));
     if (max_seqs == 0) return batch_free(c);
     return batch_alloc(c, max_seqs);
 }
 
-// x formatted for the segments' weight type (skipped when the previous matvec
-// read the same input the same way), then every segment's rows for every live
-// sequence in one launch.
-struct BatchFmtCache {
+// The input of the previous GEMM of the step, when formatted the same way (the
+// next GEMM reads it again without a new k_xfmt_g).
+struct GmInput {
     const float* in = nullptr;
     const float* norm = nullptr;
-    int type = -1;
+    int K = 0;
 };
 
-static BatchSeg bseg(const DevTensor* A, const DevTensor* B, float* y, int ldy, int rows, int epi) {
-    BatchSeg g{};
+static GemmSeg gseg(const DevTensor* A, const DevTensor* B, float* y, int ldy, int rows, int epi) {
+    GemmSeg g{};
     g.A = A->w;
     g.pair = B != nullptr;
     if (B) g.B = B->w;
-    g.ntiles = B ? A->w.rows_pad / 8 : A->w.rows_pad / 16;
+    g.ntiles = B ? (rows + 63) / 64 : (A->w.rows + 127) / 128;
     g.y = y;
     g.ldy = ldy;
     g.rows = rows;
@@ -1713,48 +1741,73 @@ static BatchSeg bseg(const DevTensor* A, const DevTensor* B, float* y, int ldy, 
     return g;
 }
 
-static talos_status mv_b(talos_ctx* c, BatchFmtCache& fc, BatchMvArgs a, const float* in, const float* norm) {
-    const int type = a.seg[0].A.type;
-    cudaError_t e = cudaSuccess;
-    if (fc.in != in || fc.norm != norm || fc.type != type) {
-        e = launch_xfmt_b(type, in, a.K, a.K, norm, c->cfg.rms_eps, c->bp, c->bfrag, c->bsums, c->stream);
-        if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched input format: %s", cudaGetErrorString(e));
-        fc = BatchFmtCache{in, norm, type};
+// K slices per output tile: the split that fills the SMs' waves best (a slice
+// costs a partial tile's round trip through L2, so more slices must earn it).
+static int gm_split(int nrt, int R, int sms) {
+    int best = 1;
+    double bscore = -1.0;
+    for (int S = 1; S <= std::min(R, 16); ++S) {
+        const long units = (long)nrt * S;
+        if (S > 1 && (units > (long)GM_MAX_WAVES * sms || nrt * 4 > GM_MAX_CNT)) break;
+        const long waves = (units + sms - 1) / sms;
+        const double score = (double)units / (double)(waves * sms) - 0.02 * (S - 1);
+        if (score > bscore + 1e-9) {
+            bscore = score;
+            best = S;
+        }
     }
-    a.ntiles = 0;
-    for (int i = 0; i < a.nseg; ++i) a.ntiles += a.seg[i].ntiles;
-    a.frag = c->bfrag;
-    a.sums = c->bsums;
+    return best;
+}
+
+// One GEMM of the batched step: format its input unless the previous GEMM read
+// the same one, then every segment's rows for every live column.
+static talos_status gm(talos_ctx* c, GmInput& fi, GemmArgs a, const float* in, const float* norm, int ntc) {
+    const int type = a.seg[0].A.type, nt = nt_of(ntc);
+    const int K = a.K, KP = (K + 127) / 128 * 128;
+    cudaError_t e = cudaSuccess;
+    if (fi.in != in || fi.norm != norm || fi.K != K) {
+        e = launch_xfmt_g(in, K, K, KP, c->bldp, MB_SEQ, nt, norm, c->cfg.rms_eps, c->bp, c->bplanes, c->bxs,
+                          c->stream);
+        if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "GEMM input format: %s", cudaGetErrorString(e));
+        fi = GmInput{in, norm, K};
+    }
+    const int sms = sm_count(c);
+    a.KP = KP;
+    a.nrt = 0;
+    for (int i = 0; i < a.nseg; ++i) a.nrt += a.seg[i].ntiles;
+    a.S = gm_split(a.nrt, KP / 128, sms);
+    a.xs = c->bxs;
     a.bp = c->bp;
-    e = launch_matvec_b(a, sm_count(c), c->stream);
-    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched matvec: %s", cudaGetErrorString(e));
+    a.ws = c->bws;
+    a.cnt = c->bcnt;
+    const int units = a.nrt * a.S;  // one token tile: a step holds at most nt columns
+    e = launch_gemm(c->bmaps[ntc], a, type, nt, std::min(units, sms), c->stream);
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "GEMM launch: %s", cudaGetErrorString(e));
     return TALOS_OK;
 }
 
-// prefill: the slots are consecutive positions of the one sequence of the main
-// cache (f32), so every slot's K/V row lands there and attention sees the rows
-// the other slots of the step appended.
-static talos_status enqueue_batch(talos_ctx* c, bool prefill) {
+static talos_status enqueue_batch(talos_ctx* c, int mode, int ntc) {
     const talos_cfg& cfg = c->cfg;
     const int E = (int)cfg.n_embd, F = (int)cfg.n_ff, V = (int)cfg.vocab_size;
     const DevTensor& embd = c->w["token_embd.weight"];
     cudaError_t e = launch_embed_b((const uint8_t*)embd.mem, embd.type, E, V, c->bp, c->bx, E, c->stream);
     if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched embed: %s", cudaGetErrorString(e));
-    BatchFmtCache fc;
+    GmInput fi;
+    const bool slots = mode == BM_DECODE;
     const size_t kv_layer = c->kv_ctx * (size_t)c->kv_dim;
-    const size_t seq_stride = prefill ? 0 : c->bseq_stride;
+    const size_t seq_stride = slots ? c->bseq_stride : 0;
     for (uint32_t l = 0; l < cfg.n_layer; ++l) {
         const LayerW& L = c->layers[l];
-        float* kc = (prefill ? (float*)c->kcache : c->bkc) + l * kv_layer;
-        float* vc = (prefill ? (float*)c->vcache : c->bvc) + l * kv_layer;
-        // rmsnorm + q/k/v + RoPE + KV append (llama.rs:118-130): one launch when
+        float* kc = (slots ? c->bkc : (float*)c->kcache) + l * kv_layer;
+        float* vc = (slots ? c->bvc : (float*)c->vcache) + l * kv_layer;
+        // rmsnorm + q/k/v + RoPE + KV append (llama.rs:118-130): one GEMM when
         // the three share a type
         {
             const DevTensor* w3[3] = {L.q, L.k, L.v};
             const int epi3[3] = {EPI_B_ROPE, EPI_B_KCACHE, EPI_B_VCACHE};
             const int rows3[3] = {c->q_rows, c->kv_dim, c->kv_dim};
             for (int i = 0; i < 3;) {
-                BatchMvArgs a{};
+                GemmArgs a{};
                 a.K = E;
                 a.rope_cs = c->rope_cs;
                 a.hd = c->hd;
@@ -1763,10 +1816,10 @@ static talos_status enqueue_batch(talos_ctx* c, bool prefill) {
                 a.vc = vc;
                 a.seq_stride = seq_stride;
                 do {
-                    a.seg[a.nseg++] = bseg(w3[i], nullptr, c->bq, c->q_rows, rows3[i], epi3[i]);
+                    a.seg[a.nseg++] = gseg(w3[i], nullptr, c->bq, c->q_rows, rows3[i], epi3[i]);
                     ++i;
                 } while (i < 3 && a.seg[0].A.type == w3[i]->type);
-                TRY(mv_b(c, fc, a, c->bx, (const float*)L.attn_norm->mem));
+                TRY(gm(c, fi, a, c->bx, (const float*)L.attn_norm->mem, ntc));
             }
         }
         // attention (llama.rs:135-155), o-proj + residual (:157-161)
@@ -1774,41 +1827,33 @@ static talos_status enqueue_batch(talos_ctx* c, bool prefill) {
                                (int)cfg.n_head_kv, c->hd, c->batt, E, c->bp, c->stream);
         if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched attention: %s", cudaGetErrorString(e));
         {
-            BatchMvArgs a{};
+            GemmArgs a{};
             a.K = E;
-            a.seg[a.nseg++] = bseg(L.o, nullptr, c->bx, E, E, EPI_B_ADD);
-            TRY(mv_b(c, fc, a, c->batt, nullptr));
+            a.seg[a.nseg++] = gseg(L.o, nullptr, c->bx, E, E, EPI_B_ADD);
+            TRY(gm(c, fi, a, c->batt, nullptr, ntc));
         }
-        // rmsnorm + SwiGLU FFN (gate/up paired when they share a type) + residual (:163-176)
-        const float* fn = (const float*)L.ffn_norm->mem;
-        if (L.gate->type == L.up->type) {
-            BatchMvArgs a{};
+        // rmsnorm + SwiGLU FFN (gate/up paired; they share a type, bind_layers) +
+        // residual (:163-176)
+        {
+            GemmArgs a{};
             a.K = E;
-            a.seg[a.nseg++] = bseg(L.gate, L.up, c->bh, F, F, EPI_B_SWIGLU);
-            TRY(mv_b(c, fc, a, c->bx, fn));
-        } else {
-            BatchMvArgs a{};
-            a.K = E;
-            a.seg[a.nseg++] = bseg(L.gate, nullptr, c->bg, F, F, EPI_B_STORE);
-            TRY(mv_b(c, fc, a, c->bx, fn));
-            a.seg[0] = bseg(L.up, nullptr, c->bu, F, F, EPI_B_STORE);
-            TRY(mv_b(c, fc, a, c->bx, fn));
-            e = launch_swiglu_b(c->bg, c->bu, c->bh, F, F, c->bp, c->stream);
-            if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched swiglu: %s", cudaGetErrorString(e));
+            a.seg[a.nseg++] = gseg(L.gate, L.up, c->bh, F, F, EPI_B_SWIGLU);
+            TRY(gm(c, fi, a, c->bx, (const float*)L.ffn_norm->mem, ntc));
         }
         {
-            BatchMvArgs a{};
+            GemmArgs a{};
             a.K = F;
-            a.seg[a.nseg++] = bseg(L.down, nullptr, c->bx, E, E, EPI_B_ADD);
-            TRY(mv_b(c, fc, a, c->bh, nullptr));
+            a.seg[a.nseg++] = gseg(L.down, nullptr, c->bx, E, E, EPI_B_ADD);
+            TRY(gm(c, fi, a, c->bh, nullptr, ntc));
         }
-        fc = BatchFmtCache{};  // bx changed in place
+        fi = GmInput{};  // bx changed in place
     }
+    if (mode == BM_PREFILL) return TALOS_OK;  // the last column's logits: batch_last_logits
     // final norm + logits (:89, :181)
-    BatchMvArgs a{};
+    GemmArgs a{};
     a.K = E;
-    a.seg[a.nseg++] = bseg(&c->w["output.weight"], nullptr, c->blog, V, V, EPI_B_STORE);
-    TRY(mv_b(c, fc, a, c->bx, (const float*)c->w["output_norm.weight"].mem));
+    a.seg[a.nseg++] = gseg(&c->w["output.weight"], nullptr, c->blog, V, V, EPI_B_STORE);
+    TRY(gm(c, fi, a, c->bx, (const float*)c->w["output_norm.weight"].mem, ntc));
     return TALOS_OK;
 }
 
@@ -1816,9 +1861,9 @@ static talos_status batch_check(talos_ctx* c) {
     auto ok = [](const DevTensor* t) { return t->type == GT_Q4_0 || t->type == GT_Q8_0 || t->type == GT_Q6_K; };
     for (const LayerW& L : c->layers)
         if (!ok(L.q) || !ok(L.k) || !ok(L.v) || !ok(L.o) || !ok(L.gate) || !ok(L.up) || !ok(L.down))
-            return set_err(TALOS_ERR_UNSUPPORTED, "batched decode needs Q4_0 / Q8_0 / Q6_K matrices");
+            return set_err(TALOS_ERR_UNSUPPORTED, "batched steps need Q4_0 / Q8_0 / Q6_K matrices");
     if (!ok(&c->w["output.weight"]))
-        return set_err(TALOS_ERR_UNSUPPORTED, "batched decode needs a Q4_0 / Q8_0 / Q6_K output matrix");
+        return set_err(TALOS_ERR_UNSUPPORTED, "batched steps need a Q4_0 / Q8_0 / Q6_K output matrix");
     if (c->hd > 128 || c->hd % 4) return set_err(TALOS_ERR_UNSUPPORTED, "batched attention needs head_dim <= 128");
     return TALOS_OK;
 }
@@ -1829,11 +1874,12 @@ __global__ void k_set_batch(BatchParams* d, BatchParams v, bool keep_err) {
     *d = v;
 }
 
-static talos_status batch_graph(talos_ctx* c, bool prefill, cudaGraphExec_t* out) {
+static talos_status batch_graph(talos_ctx* c, int mode, int ntc) {
+    cudaGraphExec_t* out = &c->bgraph[mode][ntc];
     if (*out) return TALOS_OK;
     cudaGraph_t g = nullptr;
     CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-    talos_status st = enqueue_batch(c, prefill);
+    talos_status st = enqueue_batch(c, mode, ntc);
     cudaError_t e = cudaStreamEndCapture(c->stream, &g);
     if (st != TALOS_OK) {
         if (g) cudaGraphDestroy(g);
@@ -1847,10 +1893,13 @@ static talos_status batch_graph(talos_ctx* c, bool prefill, cudaGraphExec_t* out
     return TALOS_OK;
 }
 
-// One batched step: parameters set by a kernel (stream-ordered, so the host never
-// rewrites a buffer a pending copy reads), then the graph.
-static talos_status batch_step(talos_ctx* c, cudaGraphExec_t g, const uint32_t* tokens, const size_t* pos, int n,
-                               bool first) {
+// One batched step of n columns: parameters set by a kernel (stream-ordered, so
+// the host never rewrites a buffer a pending copy reads), then the graph of the
+// smallest token tile that holds n.
+static talos_status batch_step(talos_ctx* c, int mode, const uint32_t* tokens, const size_t* pos, int n, bool first) {
+    if (n < 1 || n > MB_SEQ) return set_err(TALOS_ERR_INVALID_ARG, "%d columns in a batched step", n);
+    const int ntc = ntc_for(n);
+    TRY(batch_graph(c, mode, ntc));
     BatchParams v{};
     v.n = n;
     for (int i = 0; i < n; ++i) {
@@ -1859,7 +1908,7 @@ static talos_status batch_step(talos_ctx* c, cudaGraphExec_t g, const uint32_t* 
     }
     k_set_batch<<<1, 1, 0, c->stream>>>(c->bp, v, !first);
     CK(cudaGetLastError());
-    CK(cudaGraphLaunch(g, c->stream));
+    CK(cudaGraphLaunch(c->bgraph[mode][ntc], c->stream));
     return TALOS_OK;
 }
 
@@ -1885,27 +1934,40 @@ extern "C" talos_status talos_forward_batch(talos_ctx* c, const uint32_t* tokens
     for (int i = 0; i < n; ++i) TRY(check_tok_pos(c, tokens[i], pos[i]));
     TRY(bind_if_dirty(c));
     TRY(batch_check(c));
-    TRY(batch_graph(c, false, &c->bgraph));
-    TRY(batch_step(c, c->bgraph, tokens, pos, n, true));
+    TRY(batch_step(c, BM_DECODE, tokens, pos, n, true));
     return batch_finish(c, n, logits_out);
 }
 
-// talos_prefill in steps of MB_SEQ consecutive prompt positions: one weight pass
-// per step instead of one per token. Taken when the batched step runs the model
-// and the main cache is f32 on one GPU; false in *taken otherwise.
-// Whether the batched step can run consecutive positions of the main cache
-// (one GPU, f32 cache, Q4_0 / Q8_0 / Q6_K matrices); if so its graph is ready.
+// Whether the batched steps can run consecutive positions of the main cache
+// (one GPU, f32 cache, Q4_0 / Q8_0 / Q6_K matrices); if so their buffers exist.
 static talos_status chunked_ready(talos_ctx* c, bool* ok) {
     *ok = false;
     if (c->tp > 1 || c->kv_f16) return TALOS_OK;
     TRY(bind_if_dirty(c));
     if (batch_check(c) != TALOS_OK) return TALOS_OK;
     if (!c->bmem) TRY(batch_alloc(c, 0));
-    TRY(batch_graph(c, true, &c->bgraph_pf));
     *ok = true;
     return TALOS_OK;
 }
 
+// logits of one residual-stream row x (device): final norm + output matvec
+// (llama.rs:181, :89) into c->logits.
+static talos_status row_logits(talos_ctx* c, const float* x) {
+    const DevTensor& ow = c->w["output.weight"];
+    MatvecArgs a{};
+    a.K = (int)c->cfg.n_embd;
+    a.x = x;
+    a.norm_w = (const float*)c->w["output_norm.weight"].mem;
+    a.eps = c->cfg.rms_eps;
+    a.epi = EPI_STORE;
+    a.step = c->step;
+    a.seg[a.nseg++] = make_seg(&ow, nullptr, 0, c->logits, (int)c->cfg.vocab_size, 0);
+    return run_mv(c, a, ow.type);
+}
+
+// talos_prefill in steps of up to MB_SEQ consecutive prompt positions: one
+// weight pass per step instead of one per token. Taken when the batched step
+// runs the model and the main cache is f32 on one GPU; false in *taken otherwise.
 static talos_status prefill_chunked(talos_ctx* c, const uint32_t* tokens, size_t n, size_t pos0, float* last_logits,
                                     bool* taken) {
     *taken = false;
@@ -1913,18 +1975,19 @@ static talos_status prefill_chunked(talos_ctx* c, const uint32_t* tokens, size_t
     TRY(chunked_ready(c, taken));
     if (!*taken) return TALOS_OK;
     int last_n = 1;
+    std::vector<size_t> pos(MB_SEQ);
     for (size_t i = 0; i < n; i += MB_SEQ) {
         const int k = (int)std::min<size_t>(MB_SEQ, n - i);
-        size_t pos[MB_SEQ];
         for (int j = 0; j < k; ++j) pos[j] = pos0 + i + j;
-        TRY(batch_step(c, c->bgraph_pf, tokens + i, pos, k, i == 0));
+        TRY(batch_step(c, BM_PREFILL, tokens + i, pos.data(), k, i == 0));
         last_n = k;
     }
-    std::vector<float> all;
-    if (last_logits) all.resize((size_t)last_n * c->cfg.vocab_size);
-    TRY(batch_finish(c, last_n, last_logits ? all.data() : nullptr));
-    if (last_logits)
-        memcpy(last_logits, all.data() + (size_t)(last_n - 1) * c->cfg.vocab_size, c->cfg.vocab_size * 4);
+    if (last_logits) {
+        TRY(row_logits(c, c->bx + (size_t)(last_n - 1) * c->cfg.n_embd));
+        CK(cudaMemcpyAsync(c->h_out, c->logits, c->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, c->stream));
+    }
+    TRY(batch_finish(c, 0, nullptr));
+    if (last_logits) memcpy(last_logits, c->h_out, c->cfg.vocab_size * 4);
     return TALOS_OK;
 }
 
@@ -1937,7 +2000,7 @@ extern "C" talos_status talos_perplexity(talos_ctx* c, const uint32_t* tokens, s
         if (tokens[i] >= c->cfg.vocab_size)
             return set_err(TALOS_ERR_INVALID_ARG, "token %u at %zu out of range (vocab %u)", tokens[i], i,
                            c->cfg.vocab_size);
-    // positions in steps of 4 through the batched step where it runs the model
+    // positions in steps of up to MB_SEQ through the batched step where it runs the model
     bool chunked = false;
     TRY(chunked_ready(c, &chunked));
     if (!chunked) TRY(ensure_graph(c, GM_LOGITS));
@@ -1946,30 +2009,30 @@ extern "C" talos_status talos_perplexity(talos_ctx* c, const uint32_t* tokens, s
     cudaError_t e = cudaMemsetAsync(acc, 0, 2 * sizeof(double), c->stream);
     const int V = (int)c->cfg.vocab_size;
     bool first = true;
+    std::vector<size_t> pos(MB_SEQ);
     // chunks of the context length, each from an empty cache (src/eval.rs:35-52)
     const size_t chunk = c->kv_ctx;
     for (size_t c0 = 0; e == cudaSuccess && st == TALOS_OK && c0 + 1 < n; c0 += chunk) {
         const size_t len = std::min(chunk, n - c0);
         if (len < 2) break;  // a trailing single token predicts nothing
         if (chunked) {
-            // scored positions 0 .. len-2, MB_SEQ per step, NLLs added in position order
+            // scored positions 0 .. len-2, up to MB_SEQ per step, NLLs added in position order
             for (size_t p0 = 0; e == cudaSuccess && st == TALOS_OK && p0 + 1 < len; p0 += MB_SEQ) {
                 const int k = (int)std::min<size_t>(MB_SEQ, len - 1 - p0);
-                size_t pos[MB_SEQ];
                 for (int j = 0; j < k; ++j) pos[j] = p0 + j;
-                st = batch_step(c, c->bgraph_pf, tokens + c0 + p0, pos, k, first);
+                st = batch_step(c, BM_SCORE, tokens + c0 + p0, pos.data(), k, first);
                 first = false;
                 for (int j = 0; j < k && st == TALOS_OK && e == cudaSuccess; ++j)
                     e = launch_token_nll(c->blog + (size_t)j * V, V, tokens[c0 + p0 + j + 1], acc, c->stream);
             }
             continue;
         }
-        for (size_t pos = 0; e == cudaSuccess && pos + 1 < len; ++pos) {
-            k_set_step<<<1, 1, 0, c->stream>>>(c->step, tokens[c0 + pos], (uint32_t)pos);
+        for (size_t pos1 = 0; e == cudaSuccess && pos1 + 1 < len; ++pos1) {
+            k_set_step<<<1, 1, 0, c->stream>>>(c->step, tokens[c0 + pos1], (uint32_t)pos1);
             e = cudaGetLastError();
             if (e == cudaSuccess) e = cudaGraphLaunch(c->graph[GM_LOGITS], c->stream);
             if (e == cudaSuccess)
-                e = launch_token_nll(c->logits, V, tokens[c0 + pos + 1], acc, c->stream);
+                e = launch_token_nll(c->logits, V, tokens[c0 + pos1 + 1], acc, c->stream);
         }
     }
     double h[2] = {0.0, 0.0};

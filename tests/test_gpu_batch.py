@@ -1,7 +1,8 @@
-"""Batched decode (talos_ctx_set_batch / talos_forward_batch): up to 4
-sequences per step, each with its own cache slot and position, against one
-oracle model per sequence. Bars as for one sequence: logits within 1e-3
-max-abs (quantized weights), greedy tokens identical, reruns bit-identical."""
+"""Batched steps on the tensor-core GEMM: batched decode (talos_ctx_set_batch /
+talos_forward_batch, up to 64 sequences per step, each with its own cache slot
+and position) against one oracle model per sequence, and prefill of up to 128
+consecutive prompt positions per step. Bars as for one sequence: logits within
+1e-3 max-abs (quantized weights), greedy tokens identical, reruns bit-identical."""
 import numpy as np
 import pytest
 
@@ -87,7 +88,7 @@ def test_batch_argument_errors():
     with pytest.raises(TalosError, match="INVALID_ARG"):
         m.ctx.forward_batch([4096, 1], [0, 0])  # token == vocab
     with pytest.raises(TalosError, match="INVALID_ARG"):
-        m.ctx.set_batch(5)
+        m.ctx.set_batch(65)
     m.close()
     f = Model.load_bytes(tiny_model(gguf.F32))
     f.ctx.set_batch(1)
@@ -96,10 +97,30 @@ def test_batch_argument_errors():
     f.close()
 
 
-@pytest.mark.parametrize("n,pos0", [(1, 0), (5, 0), (11, 0), (6, 3)])
+def test_batch_32_sequences():
+    """32 sequences at once (the batch size of the 70B-shape benchmark), each
+    joining at its own step with its own prompt length: every sequence's logits
+    and greedy tokens against its own oracle model."""
+    data = tiny_model(gguf.Q4_0)
+    prompts = [prompt(2 + (7 * i) % 9, 4096, 100 + i) for i in range(32)]
+    g, c = run_batch(data, prompts, start=[i % 5 for i in range(32)], steps=14)
+    assert max_err(g, c) <= 1e-3
+
+
+def test_batch_token_tile_sizes():
+    """Step sizes around the 32 / 64-column tile boundaries (graphs per tile size)."""
+    data = tiny_model(gguf.Q8_0)
+    for nseq in (33, 64):
+        prompts = [prompt(3, 4096, 300 + i) for i in range(nseq)]
+        g, c = run_batch(data, prompts, start=[0] * nseq, steps=5)
+        assert max_err(g, c) <= 1e-3
+
+
+@pytest.mark.parametrize("n,pos0", [(1, 0), (5, 0), (11, 0), (6, 3), (128, 0), (150, 5), (249, 0)])
 def test_prefill_in_batched_steps(n, pos0):
-    """talos_prefill runs 4 consecutive prompt positions per weight pass on the
-    main cache: the last logits and the decode steps after it match the oracle."""
+    """talos_prefill runs up to 128 consecutive prompt positions per weight pass
+    on the main cache: the last logits and the decode steps after it match the
+    oracle."""
     data = tiny_model(gguf.Q8_0)
     cpu = oracle.Model(data=data)
     gpu = Model.load_bytes(data)
