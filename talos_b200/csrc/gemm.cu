@@ -57,7 +57,6 @@ namespace talos {
 constexpr int GM_BM = 128;   // weight rows per tile = TMEM lanes
 constexpr int GM_BK = 64;    // K per A/B stage
 constexpr int GM_RK = 128;   // K per raw weight slot (two stages)
-constexpr int GM_NS = 2;     // A/B stages
 constexpr int GM_NDQ = 8;    // dequantizer warps
 constexpr int GM_WP = 4, GM_XP = 5, GM_MMA = 6, GM_DQ0 = 7;
 constexpr int GM_THREADS = (GM_DQ0 + GM_NDQ) * 32;
@@ -83,6 +82,9 @@ struct GmFmt<GT_Q6_K> {
     static constexpr int LREC = 1024, SC = 576;
 };
 
+// Shared memory of one configuration: NS A/B stages (4, 3 or 2: as many as fit
+// beside a ring of at least two raw slots; more stages hide more of the
+// dequantize -> MMA -> release round trip), then as many raw slots as fit (<= 8).
 template <int TYPE, int NT>
 struct GmCfg {
     static constexpr int GRP = GmFmt<TYPE>::LREC + GmFmt<TYPE>::SC;
@@ -90,7 +92,10 @@ struct GmCfg {
     static constexpr int A_BYTES = 2 * GM_BM * GM_BK * 2;  // A_hi + A_lo
     static constexpr int B_BYTES = 2 * NT * GM_BK * 2;     // [x_hi; x_lo]
     static constexpr int BAR_BYTES = 1024;
-    static constexpr int FIXED = GM_NS * (A_BYTES + B_BYTES) + BAR_BYTES;
+    static constexpr int EPI_BYTES = 4 * NT * 8;  // the epilogue warps' column scales and positions
+    static constexpr int fixed(int ns) { return ns * (A_BYTES + B_BYTES) + BAR_BYTES + EPI_BYTES; }
+    static constexpr int NS = fixed(4) + 2 * RAW <= GM_SMEM ? 4 : (fixed(3) + 2 * RAW <= GM_SMEM ? 3 : 2);
+    static constexpr int FIXED = fixed(NS);
     static constexpr int NRAW_FIT = (GM_SMEM - FIXED) / RAW;
     static constexpr int NRAW = NRAW_FIT > GM_MAXRAW ? GM_MAXRAW : NRAW_FIT;
     static constexpr int SMEM = FIXED + NRAW * RAW;
@@ -317,39 +322,69 @@ __device__ __forceinline__ void gm_dequant_q6(const uint8_t* grp, uint8_t* Ahi, 
 
 // ---------------------------------------------------------------- epilogue
 
-__device__ __forceinline__ void gm_apply(const GemmArgs& a, const GemmSeg& sg, int lt, int r, int t, int ntok, float v,
-                                         const uint32_t* pos) {
-    const int lane = threadIdx.x & 31;
-    const bool live = t < ntok;
+// The epilogue of W consecutive token columns t0 .. t0+W-1 of tile row r:
+// v[j] are the raw sums, xs[j] the column scales (2^e_t * 2^-eA, 0 past the
+// live columns), ps[j] the columns' positions. Every global load of the W
+// columns is issued before any is used (one memory round trip per W columns,
+// not one per column). Called by all 32 lanes of an epilogue warp (shuffles).
+template <int W>
+__device__ __forceinline__ void gm_epi(const GemmArgs& a, const GemmSeg& sg, int lt, int r, int t0, int ntok,
+                                       float* v, const float* xs, const uint32_t* ps) {
+#pragma unroll
+    for (int j = 0; j < W; ++j) v[j] *= xs[j];
     if (sg.epi == EPI_B_SWIGLU) {  // src/math/ops.rs:33-37: gate lanes r % 16 < 8, up on lane + 8
-        const float up = __shfl_down_sync(0xffffffffu, v, 8);
+        float up[W];
+#pragma unroll
+        for (int j = 0; j < W; ++j) up[j] = __shfl_down_sync(0xffffffffu, v[j], 8);
         const int row = lt * 64 + (r >> 4) * 8 + (r & 7);
-        if (live && (r & 8) == 0 && row < sg.rows) sg.y[(size_t)t * sg.ldy + row] = __fmul_rn(silu_ref(v), up);
+        if ((r & 8) || row >= sg.rows) return;
+#pragma unroll
+        for (int j = 0; j < W; ++j)
+            if (t0 + j < ntok) sg.y[(size_t)(t0 + j) * sg.ldy + row] = __fmul_rn(silu_ref(v[j]), up[j]);
         return;
     }
     const int row = lt * GM_BM + r;
     if (sg.epi >= EPI_B_ROPE) {
         // pairs (2i, 2i+1) on lanes l, l ^ 1 (src/math/ops.rs:48-61); then the cache
-        // append of src/kv_cache.rs:21-26 at the token's slot and position
-        const float pv = __shfl_xor_sync(0xffffffffu, v, 1);
-        (void)lane;
-        if (!live || row >= sg.rows) return;
-        const uint32_t p = pos[t];
-        float o = v;
+        // append of src/kv_cache.rs:21-26 at the column's slot and position
+        float pv[W];
+#pragma unroll
+        for (int j = 0; j < W; ++j) pv[j] = __shfl_xor_sync(0xffffffffu, v[j], 1);
+        if (row >= sg.rows) return;
+        float2 cs[W];
         if (sg.epi != EPI_B_VCACHE) {
-            const float2 c = a.rope_cs[(size_t)p * (a.hd >> 1) + ((row % a.hd) >> 1)];
-            o = (row & 1) ? __fadd_rn(__fmul_rn(pv, c.y), __fmul_rn(v, c.x))
-                          : __fsub_rn(__fmul_rn(v, c.x), __fmul_rn(pv, c.y));
+            const size_t col = (size_t)((row % a.hd) >> 1);
+#pragma unroll
+            for (int j = 0; j < W; ++j) cs[j] = a.rope_cs[(size_t)ps[j] * (a.hd >> 1) + col];
         }
-        float* dst = sg.epi == EPI_B_ROPE ? sg.y + (size_t)t * sg.ldy
-                                          : (sg.epi == EPI_B_KCACHE ? a.kc : a.vc) + (size_t)t * a.seq_stride +
-                                                (size_t)p * a.kv_dim;
-        dst[row] = o;
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+            const int t = t0 + j;
+            if (t >= ntok) continue;
+            float o = v[j];
+            if (sg.epi != EPI_B_VCACHE)
+                o = (row & 1) ? __fadd_rn(__fmul_rn(pv[j], cs[j].y), __fmul_rn(v[j], cs[j].x))
+                              : __fsub_rn(__fmul_rn(v[j], cs[j].x), __fmul_rn(pv[j], cs[j].y));
+            float* dst = sg.epi == EPI_B_ROPE ? sg.y + (size_t)t * sg.ldy
+                                              : (sg.epi == EPI_B_KCACHE ? a.kc : a.vc) + (size_t)t * a.seq_stride +
+                                                    (size_t)ps[j] * a.kv_dim;
+            dst[row] = o;
+        }
         return;
     }
-    if (!live || row >= sg.rows) return;
-    float* y = sg.y + (size_t)t * sg.ldy + row;
-    *y = sg.epi == EPI_B_ADD ? __fadd_rn(*y, v) : v;
+    if (row >= sg.rows) return;
+    if (sg.epi == EPI_B_ADD) {  // residual (src/model/llama.rs:159-161, 174-176)
+        float old[W];
+#pragma unroll
+        for (int j = 0; j < W; ++j) old[j] = t0 + j < ntok ? sg.y[(size_t)(t0 + j) * sg.ldy + row] : 0.f;
+#pragma unroll
+        for (int j = 0; j < W; ++j)
+            if (t0 + j < ntok) sg.y[(size_t)(t0 + j) * sg.ldy + row] = __fadd_rn(old[j], v[j]);
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < W; ++j)
+        if (t0 + j < ntok) sg.y[(size_t)(t0 + j) * sg.ldy + row] = v[j];
 }
 
 // ---------------------------------------------------------------- the kernel
@@ -360,19 +395,21 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     using C = GmCfg<TYPE, NT>;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* sA = smem;                                   // [NS][hi 16 KB | lo 16 KB]
-    uint8_t* sB = smem + GM_NS * C::A_BYTES;              // [NS][kg 8][2 NT][16 B]
-    uint8_t* sR = sB + GM_NS * C::B_BYTES;                // [NRAW][16 groups][GRP]
+    uint8_t* sB = smem + C::NS * C::A_BYTES;              // [NS][kg 8][2 NT][16 B]
+    uint8_t* sR = sB + C::NS * C::B_BYTES;                // [NRAW][16 groups][GRP]
     uint64_t* bars = (uint64_t*)(sR + C::NRAW * C::RAW);  // barriers
     uint64_t* raw_full = bars;
     uint64_t* raw_empty = raw_full + C::NRAW;
     uint64_t* a_full = raw_empty + C::NRAW;
-    uint64_t* b_full = a_full + GM_NS;
-    uint64_t* st_empty = b_full + GM_NS;
-    uint64_t* acc_full = st_empty + GM_NS;   // [2]
+    uint64_t* b_full = a_full + C::NS;
+    uint64_t* st_empty = b_full + C::NS;
+    uint64_t* acc_full = st_empty + C::NS;   // [2]
     uint64_t* acc_empty = acc_full + 2;      // [2]
     uint64_t* done = acc_empty + 2;          // the MMA thread's final commit
     uint32_t* tmem_slot = (uint32_t*)(done + 1);
     int* s_flag = (int*)(tmem_slot + 1);     // [0]: some role gave up on a wait
+    float* ep_xs = (float*)(sR + C::NRAW * C::RAW + C::BAR_BYTES);  // [4 warps][NT] column scales
+    uint32_t* ep_pos = (uint32_t*)(ep_xs + 4 * NT);                   // [4 warps][NT] column positions
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     const int ntok = a.bp->n;
@@ -384,7 +421,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             mbar_init(&raw_full[i], 1);
             mbar_init(&raw_empty[i], GM_NDQ);
         }
-        for (int i = 0; i < GM_NS; ++i) {
+        for (int i = 0; i < C::NS; ++i) {
             mbar_init(&a_full[i], GM_NDQ);
             mbar_init(&b_full[i], 1);
             mbar_init(&st_empty[i], 1);
@@ -413,65 +450,73 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     auto stop = [&]() { return *(volatile int*)&s_flag[0] != 0; };
 
     if (warp == GM_WP) {
-        // ---------------- weight producer
-        if (lane == 0) {
-            uint32_t ri = 0;
-            for (int u = blockIdx.x; u < nunits && !stop(); u += gridDim.x) {
-                const GmUnit U = gm_unit(a, u, ntt);
-                const GemmSeg& sg = a.seg[U.si];
-                for (int rs = U.r0; rs < U.r1; ++rs, ++ri) {
-                    const int slot = ri % C::NRAW;
-                    if (!mbar_wait(&raw_empty[slot], ((ri / C::NRAW) & 1) ^ 1)) {
-                        fail();
-                        break;
-                    }
-                    uint32_t bytes = 0;
-                    for (int gi = 0; gi < 16; ++gi) {
-                        int g;
-                        const PackedW* w = gm_group(sg, U.lt, gi, g);
-                        if (g < w->rows_pad / 8) bytes += C::GRP;
-                    }
-                    mbar_expect_tx(&raw_full[slot], bytes);
-                    uint8_t* dst = sR + slot * C::RAW;
-                    for (int gi = 0; gi < 16; ++gi) {
-                        int g;
-                        const PackedW* w = gm_group(sg, U.lt, gi, g);
-                        if (g >= w->rows_pad / 8) continue;
-                        const uint8_t *lr, *sc;
-                        gm_src<TYPE>(*w, g, rs, lr, sc);
-                        bulk_g2s(dst + gi * C::GRP, lr, GmFmt<TYPE>::LREC, &raw_full[slot]);
-                        bulk_g2s(dst + gi * C::GRP + GmFmt<TYPE>::LREC, sc, GmFmt<TYPE>::SC, &raw_full[slot]);
-                    }
+        // ---------------- weight producer: lane gi (< 16) copies row group gi's data
+        uint32_t ri = 0;
+        for (int u = blockIdx.x; u < nunits && !stop(); u += gridDim.x) {
+            const GmUnit U = gm_unit(a, u, ntt);
+            const GemmSeg& sg = a.seg[U.si];
+            int g = 0;
+            const PackedW* w = lane < 16 ? gm_group(sg, U.lt, lane, g) : nullptr;
+            const bool valid = w && g < w->rows_pad / 8;
+            const uint32_t bytes = (uint32_t)__popc(__ballot_sync(0xffffffffu, valid)) * C::GRP;
+            bool ok = true;
+            for (int rs = U.r0; rs < U.r1; ++rs, ++ri) {
+                const int slot = ri % C::NRAW;
+                bool w_ok = true;
+                if (lane == 0) {
+                    w_ok = mbar_wait(&raw_empty[slot], ((ri / C::NRAW) & 1) ^ 1);
+                    if (w_ok) mbar_expect_tx(&raw_full[slot], bytes);
                 }
-                if (stop()) break;
+                if (!__shfl_sync(0xffffffffu, (int)w_ok, 0)) {
+                    ok = false;
+                    break;
+                }
+                if (valid) {
+                    const uint8_t *lr, *sc;
+                    gm_src<TYPE>(*w, g, rs, lr, sc);
+                    uint8_t* dst = sR + slot * C::RAW + lane * C::GRP;
+                    bulk_g2s(dst, lr, GmFmt<TYPE>::LREC, &raw_full[slot]);
+                    bulk_g2s(dst + GmFmt<TYPE>::LREC, sc, GmFmt<TYPE>::SC, &raw_full[slot]);
+                }
             }
-            // copies in flight land before the CTA exits
+            if (!ok) {
+                if (lane == 0) fail();
+                break;
+            }
+        }
+        // copies in flight land before the CTA exits
+        if (lane == 0) {
             const uint32_t first = ri > (uint32_t)C::NRAW ? ri - C::NRAW : 0;
             for (uint32_t j = first; j < ri; ++j) mbar_wait(&raw_full[j % C::NRAW], (j / C::NRAW) & 1);
         }
     } else if (warp == GM_XP) {
-        // ---------------- activation producer: TMA tiles of the [x_hi; x_lo] planes
-        if (lane == 0) {
-            uint32_t si = 0;
-            for (int u = blockIdx.x; u < nunits && !stop(); u += gridDim.x) {
-                const GmUnit U = gm_unit(a, u, ntt);
-                for (int rs = U.r0; rs < U.r1 && !stop(); ++rs)
-                    for (int h = 0; h < 2; ++h, ++si) {
-                        const int s = si % GM_NS;
-                        if (!mbar_wait(&st_empty[s], ((si / GM_NS) & 1) ^ 1)) {
-                            fail();
-                            break;
-                        }
-                        mbar_expect_tx(&b_full[s], C::B_BYTES);
-                        uint8_t* dst = sB + s * C::B_BYTES;
-                        const int k0 = rs * GM_RK + h * GM_BK;
-#pragma unroll 1
-                        for (int i = 0; i < GM_BK / 8; ++i)
-                            tma_load_3d(dst + i * (2 * NT * 16), &tmx, k0 + 8 * i, U.tt * NT, 0, &b_full[s]);
+        // ---------------- activation producer: TMA tiles of the [x_hi; x_lo] planes,
+        // lane i (< 8) copies the stage's 8-input group i
+        uint32_t si = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < nunits && ok && !stop(); u += gridDim.x) {
+            const GmUnit U = gm_unit(a, u, ntt);
+            for (int rs = U.r0; rs < U.r1 && ok; ++rs)
+                for (int h = 0; h < 2; ++h, ++si) {
+                    const int s = si % C::NS;
+                    bool w_ok = true;
+                    if (lane == 0) {
+                        w_ok = mbar_wait(&st_empty[s], ((si / C::NS) & 1) ^ 1);
+                        if (w_ok) mbar_expect_tx(&b_full[s], C::B_BYTES);
                     }
-            }
-            const uint32_t first = si > (uint32_t)GM_NS ? si - GM_NS : 0;
-            for (uint32_t j = first; j < si; ++j) mbar_wait(&b_full[j % GM_NS], (j / GM_NS) & 1);
+                    if (!__shfl_sync(0xffffffffu, (int)w_ok, 0)) {
+                        ok = false;
+                        break;
+                    }
+                    if (lane < GM_BK / 8)
+                        tma_load_3d(sB + s * C::B_BYTES + lane * (2 * NT * 16), &tmx, rs * GM_RK + h * GM_BK + 8 * lane,
+                                    U.tt * NT, 0, &b_full[s]);
+                }
+        }
+        if (!ok && lane == 0) fail();
+        if (lane == 0) {
+            const uint32_t first = si > (uint32_t)C::NS ? si - C::NS : 0;
+            for (uint32_t j = first; j < si; ++j) mbar_wait(&b_full[j % C::NS], (j / C::NS) & 1);
         }
     } else if (warp == GM_MMA) {
         // ---------------- MMA issuer
@@ -491,8 +536,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                 bool ok = true;
                 for (int rs = U.r0; rs < U.r1 && ok; ++rs)
                     for (int h = 0; h < 2; ++h, ++si) {
-                        const int s = si % GM_NS;
-                        const uint32_t par = (si / GM_NS) & 1;
+                        const int s = si % C::NS;
+                        const uint32_t par = (si / C::NS) & 1;
                         if (!mbar_wait(&a_full[s], par) || !mbar_wait(&b_full[s], par)) {
                             ok = false;
                             break;
@@ -544,8 +589,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                 }
                 const uint8_t* raw = sR + slot * C::RAW;
                 for (int h = 0; h < 2; ++h, ++si) {
-                    const int s = si % GM_NS;
-                    if (!__all_sync(0xffffffffu, mbar_wait(&st_empty[s], ((si / GM_NS) & 1) ^ 1))) {
+                    const int s = si % C::NS;
+                    if (!__all_sync(0xffffffffu, mbar_wait(&st_empty[s], ((si / C::NS) & 1) ^ 1))) {
                         ok = false;
                         break;
                     }
@@ -576,19 +621,30 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         // The four warps never wait for each other: with split-K each warp has its
         // own arrival counter per output tile (cnt[tile * 4 + q]).
         const int q = warp, r = q * 32 + lane;
+        float* exs = ep_xs + q * NT;
+        uint32_t* eps = ep_pos + q * NT;
         uint32_t nu = 0;
         for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++nu) {
             const GmUnit U = gm_unit(a, u, ntt);
             const GemmSeg& sg = a.seg[U.si];
             const int ab = nu & 1;
+            const int t0 = U.tt * NT;
+            // the unit's column scales (2^e_t of the input, 2^-eA of the weights) and positions
+            {
+                const float wsc = ldexpf(1.f, -gm_wexp(sg));
+                for (int j = lane; j < NT; j += 32) {
+                    const int t = t0 + j;
+                    exs[j] = t < ntok ? a.xs[t] * wsc : 0.f;
+                    eps[j] = t < ntok ? a.bp->pos[t] : 0u;
+                }
+                __syncwarp();
+            }
             if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[ab], (nu >> 1) & 1))) {
                 if (lane == 0) fail();
                 break;
             }
             tc_fence_after();
-            const float wsc = ldexpf(1.f, -gm_wexp(sg));
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * (2 * NT);
-            const int t0 = U.tt * NT;
             float* part = a.S > 1 ? a.ws + ((size_t)(U.tile * a.S + U.ks) * NT) * GM_BM : nullptr;
 #pragma unroll 1
             for (int c = 0; c < NT; c += 16) {
@@ -596,16 +652,14 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                 tmem_ld16(tbase + c, vh);
                 tmem_ld16(tbase + NT + c, vl);
                 tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) vh[j] += vl[j];
                 if (part) {
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) part[(size_t)(c + j) * GM_BM + r] = vh[j] + vl[j];
+                    for (int j = 0; j < 16; ++j) part[(size_t)(c + j) * GM_BM + r] = vh[j];
                 } else {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int t = t0 + c + j;
-                        const float v = (vh[j] + vl[j]) * (wsc * (t < ntok ? a.xs[t] : 0.f));
-                        gm_apply(a, sg, U.lt, r, t, ntok, v, a.bp->pos);
-                    }
+                    gm_epi<8>(a, sg, U.lt, r, t0 + c, ntok, vh, exs + c, eps + c);
+                    gm_epi<8>(a, sg, U.lt, r, t0 + c + 8, ntok, vh + 8, exs + c + 8, eps + c + 8);
                 }
             }
             tc_fence_before();
@@ -627,12 +681,18 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             __threadfence();
             const float* base = a.ws + ((size_t)U.tile * a.S * NT) * GM_BM;
 #pragma unroll 1
-            for (int c = 0; c < NT; ++c) {
-                float v = 0.f;
-                for (int s = 0; s < a.S; ++s) v += __ldcg(base + ((size_t)s * NT + c) * GM_BM + r);
-                const int t = t0 + c;
-                v *= wsc * (t < ntok ? a.xs[t] : 0.f);
-                gm_apply(a, sg, U.lt, r, t, ntok, v, a.bp->pos);
+            for (int c = 0; c < NT; c += 8) {
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = 0.f;
+                for (int s = 0; s < a.S; ++s) {
+                    float w[8];  // the slice's 8 columns, loaded together
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) w[j] = __ldcg(base + ((size_t)s * NT + c + j) * GM_BM + r);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) v[j] += w[j];
+                }
+                gm_epi<8>(a, sg, U.lt, r, t0 + c, ntok, v, exs + c, eps + c);
             }
         }
     }
