@@ -33,17 +33,22 @@
 //    tile goes to a workspace and the unit that completes the tile adds the
 //    slices in slice order (deterministic). The four warps never wait for one
 //    another.
-//  * warp 4: weight producer. 1-D bulk copies of the packed group-chunks
-//    (k_pack_*: 8 rows x CK) of the tile's 16 row groups, 128 inputs per raw
-//    slot, into a ring of raw slots.
-//  * warp 5: activation producer. Tiled TMA (cp.async.bulk.tensor.3d, no
-//    multicast) of the formatted [x_hi; x_lo] planes into the B stage, in the
-//    canonical no-swizzle K-major layout of tcgen05 (8 x 16-byte core matrices).
+//  * warp 4: weight producer. Two tiled TMA copies per raw slot (128 inputs)
+//    of the packed group-chunks (k_pack_*: 8 rows x CK) of the tile's 16 row
+//    groups: their lane records, then their scales, through two tensor maps of
+//    the packed weight (encoded when it was packed; without them, 1-D bulk
+//    copies per row group).
+//  * warp 5: activation producer. One tiled TMA copy per stage
+//    (cp.async.bulk.tensor.3d, no multicast) of the formatted [x_hi; x_lo]
+//    planes into the B stage.
 //  * warp 6: allocates TMEM (two accumulators of 2N f32 columns), one thread
 //    issues tcgen05.mma.cta_group::1.kind::f16 (M 128, N 2N / N, K 16) and
 //    tcgen05.commit to the stage's "empty" and the accumulator's "full" barrier.
-//  * warps 7-14: dequantizers. Raw slot -> A_hi / A_lo stage tiles (f16, the
-//    same canonical layout), fence.proxy.async, arrive.
+//  * warps 7-14: dequantizers. Raw slot -> A_hi / A_lo stage tiles (f16),
+//    fence.proxy.async, arrive.
+// A and B stage tiles are K-major with the 128-byte swizzle of tcgen05 (and of
+// TMA): one 128-byte row per matrix row (64 inputs of f16), its 16-byte chunk c
+// stored at chunk c ^ (row % 8), 8-row atoms 1024 bytes apart.
 // Every mbarrier wait is bounded (2 s); on expiry the CTA records an error bit
 // in BatchParams::error and every role leaves its loop; TMEM is freed at exit.
 #include <cuda.h>
@@ -67,20 +72,32 @@ constexpr int GM_MAXRAW = 8;
 //  Q4_0: quad q of the group-chunk (512 B) + its f16 scales [8 rows][4] (64 B)
 //  Q8_0: quad q (1024 B) + scales [8 rows][4] (64 B)
 //  Q6_K: step-quads 2m, 2m+1 (1024 B) + the chunk's sc [8][64] and d [8][4] (576 B)
+// A raw slot holds the 16 groups' lane records [16][LREC], then their scales
+// [16][SC]. GCB: bytes of one group-chunk; CK: its inputs.
 template <int TYPE>
 struct GmFmt;
 template <>
 struct GmFmt<GT_Q4_0> {
-    static constexpr int LREC = 512, SC = 64;
+    static constexpr int LREC = 512, SC = 64, GCB = 16 * 512 + 16 * 64, CK = 2048;
 };
 template <>
 struct GmFmt<GT_Q8_0> {
-    static constexpr int LREC = 1024, SC = 64;
+    static constexpr int LREC = 1024, SC = 64, GCB = 8 * 1024 + 8 * 64, CK = 1024;
 };
 template <>
 struct GmFmt<GT_Q6_K> {
-    static constexpr int LREC = 1024, SC = 576;
+    static constexpr int LREC = 1024, SC = 576, GCB = 16 * 512 + 8 * 64 + 8 * 4 * 2, CK = 1024;
 };
+// Where raw slot rs's data sits inside a group-chunk (bytes): lane records at
+// lrec_off, scales at sc_off, in chunk rs * 128 / CK.
+template <int TYPE>
+__host__ __device__ constexpr int gm_lrec_off(int rs) {
+    return (rs * 128 % GmFmt<TYPE>::CK) / 128 * GmFmt<TYPE>::LREC;
+}
+template <int TYPE>
+__host__ __device__ constexpr int gm_sc_off(int rs) {
+    return TYPE == GT_Q6_K ? 16 * 512 : (TYPE == GT_Q4_0 ? 16 * 512 : 8 * 1024) + (rs * 128 % GmFmt<TYPE>::CK) / 128 * 64;
+}
 
 // Shared memory of one configuration: NS A/B stages (4, 3 or 2: as many as fit
 // beside a ring of at least two raw slots; more stages hide more of the
@@ -109,12 +126,13 @@ __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.p
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// K-major, no-swizzle shared-memory matrix descriptor (tcgen05): 8-row x 16-byte
-// core matrices; LBO = byte distance between core matrices along K, SBO = along
-// M / N; version 1 (bits 46-47) for sm_100.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+// K-major shared-memory matrix descriptor (tcgen05) with the 128-byte swizzle:
+// start address (16-byte units; a K step of 16 inputs adds 32 bytes), LBO 16
+// bytes (unused by this layout), SBO 1024 bytes between 8-row atoms, version 1
+// (bits 46-47) for sm_100, layout type 2 (bits 61-63) = SWIZZLE_128B.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
 }
 // Instruction descriptor, kind::f16: f32 accumulate, f16 A and B, both K-major, M 128.
 __host__ __device__ constexpr uint32_t umma_idesc(int n) {
@@ -176,45 +194,19 @@ __device__ __forceinline__ GmUnit gm_unit(const GemmArgs& a, int u, int ntt) {
     return w;
 }
 
-// Row group gi (0..15) of a tile: matrix and group index. A SwiGLU pair tile is
-// 64 gate rows and the same 64 up rows, groups interleaved (even: gate, odd: up).
-__device__ __forceinline__ const PackedW* gm_group(const GemmSeg& sg, int lt, int gi, int& g) {
-    if (sg.pair) {
-        g = lt * 8 + (gi >> 1);
-        return (gi & 1) ? &sg.B : &sg.A;
-    }
-    g = lt * 16 + gi;
-    return &sg.A;
-}
-
-// Byte offsets, inside group g's data, of the lane records and scales of raw slot rs.
+// Group g's raw slot rs data in the packed weight: lane records and scales.
 template <int TYPE>
 __device__ __forceinline__ void gm_src(const PackedW& w, int g, int rs, const uint8_t*& lrec, const uint8_t*& sc) {
-    const int k0 = rs * GM_RK;
-    if (TYPE == GT_Q4_0) {
-        const uint8_t* gc = (const uint8_t*)w.p0 + ((size_t)g * w.nk + k0 / 2048) * (16 * 512 + 16 * 64);
-        const int q = (k0 % 2048) / 128;
-        lrec = gc + q * 512;
-        sc = gc + 16 * 512 + q * 64;
-    } else if (TYPE == GT_Q8_0) {
-        const uint8_t* gc = (const uint8_t*)w.p0 + ((size_t)g * w.nk + k0 / 1024) * (8 * 1024 + 8 * 64);
-        const int q = (k0 % 1024) / 128;
-        lrec = gc + q * 1024;
-        sc = gc + 8 * 1024 + q * 64;
-    } else {
-        const uint8_t* gc = (const uint8_t*)w.p0 + ((size_t)g * w.nk + k0 / 1024) * (16 * 512 + 8 * 64 + 8 * 4 * 2);
-        const int m = (k0 % 1024) / 128;
-        lrec = gc + 2 * m * 512;
-        sc = gc + 16 * 512;
-    }
+    const uint8_t* gc =
+        (const uint8_t*)w.p0 + ((size_t)g * w.nk + rs * 128 / GmFmt<TYPE>::CK) * GmFmt<TYPE>::GCB;
+    lrec = gc + gm_lrec_off<TYPE>(rs);
+    sc = gc + gm_sc_off<TYPE>(rs);
 }
 
 // The segment's scale exponent eA: its values * 2^eA stay below 2^14 (the bound
-// is recorded at pack time: the largest |value| the format can give, k_wbound;
-// a SwiGLU pair takes the larger of its two matrices' bounds).
+// is recorded at pack time: the largest |value| the format can give, k_wbound).
 __device__ __forceinline__ int gm_wexp(const GemmSeg& sg) {
-    float b = sg.A.p1 ? *(const float*)sg.A.p1 : 0.f;
-    if (sg.pair && sg.B.p1) b = fmaxf(b, *(const float*)sg.B.p1);
+    const float b = sg.A.p1 ? *(const float*)sg.A.p1 : 0.f;
     if (!(b > 0.f) || !isfinite(b)) return 0;
     int ex;
     frexpf(b, &ex);  // b in [2^(ex-1), 2^ex)
@@ -227,11 +219,13 @@ __device__ __forceinline__ int gm_wexp(const GemmSeg& sg) {
 // Thread (lr, t) = (lane / 4, lane % 4) of a group task holds, per 32-element
 // block (16 for Q6_K), the k pairs {2t, 2t+1}, {2t+8, 2t+9}, {16+2t, 17+2t},
 // {24+2t, 25+2t} (the packed lane records); each pair is one 4-byte f16x2 word
-// of a core-matrix row: A[kg][row][2t .. 2t+1], kg = the pair's 8-k group.
+// of the row's 16-byte chunk kg (the pair's 8-k group): swizzled position
+// row * 128 + (kg ^ row % 8) * 16 + 4 t. A warp's 32 words of one kg fill 32
+// distinct banks.
 
 __device__ __forceinline__ void gm_put(uint8_t* A, int kg, int row, int t, __half2 v) {
     uint32_t u = *reinterpret_cast<uint32_t*>(&v);
-    *(uint32_t*)(A + kg * (GM_BM * 16) + row * 16 + t * 4) = u;
+    *(uint32_t*)(A + row * 128 + ((kg ^ (row & 7)) << 4) + t * 4) = u;
 }
 __device__ __forceinline__ void gm_split_store(uint8_t* Ahi, uint8_t* Alo, int kg, int row, int t, __half2 q,
                                                __half2 d) {
@@ -258,12 +252,12 @@ __device__ __forceinline__ __half2 q8_pair(uint32_t w, uint32_t sel) {
 // One group task of one stage (half h of the raw slot): raw group data -> A rows
 // 8 gi .. 8 gi + 7 of this stage's A_hi / A_lo (Q4_0, Q8_0; Q6_K: gm_dequant_q6).
 template <int TYPE>
-__device__ __forceinline__ void gm_dequant(const uint8_t* grp, uint8_t* Ahi, uint8_t* Alo, int gi, int h, int lane,
-                                           float wsc) {
+__device__ __forceinline__ void gm_dequant(const uint8_t* lrec, const uint8_t* scs, uint8_t* Ahi, uint8_t* Alo, int gi,
+                                           int h, int lane, float wsc) {
     const int lr = lane >> 2, t = lane & 3, row = gi * 8 + lr;
     if (TYPE == GT_Q4_0) {
-        const uint4 rec = *(const uint4*)(grp + lane * 16);
-        const uint32_t sc2 = *(const uint32_t*)(grp + 512 + lr * 8 + h * 4);
+        const uint4 rec = *(const uint4*)(lrec + lane * 16);
+        const uint32_t sc2 = *(const uint32_t*)(scs + lr * 8 + h * 4);
         const uint32_t wv[2] = {h ? rec.z : rec.x, h ? rec.w : rec.y};
 #pragma unroll
         for (int jj = 0; jj < 2; ++jj) {
@@ -281,8 +275,8 @@ __device__ __forceinline__ void gm_dequant(const uint8_t* grp, uint8_t* Ahi, uin
             gm_split_store(Ahi, Alo, 4 * jj + 3, row, t, *reinterpret_cast<__half2*>(&q), dd);
         }
     } else if (TYPE == GT_Q8_0) {
-        const uint4 rec = *(const uint4*)(grp + lane * 32 + h * 16);
-        const uint32_t sc2 = *(const uint32_t*)(grp + 1024 + lr * 8 + h * 4);
+        const uint4 rec = *(const uint4*)(lrec + lane * 32 + h * 16);
+        const uint32_t sc2 = *(const uint32_t*)(scs + lr * 8 + h * 4);
         const uint32_t wv[4] = {rec.x, rec.y, rec.z, rec.w};
 #pragma unroll
         for (int jj = 0; jj < 2; ++jj) {
@@ -298,13 +292,13 @@ __device__ __forceinline__ void gm_dequant(const uint8_t* grp, uint8_t* Ahi, uin
 }
 
 // Q6_K needs the sub-block position inside its 1024-input chunk for the scales.
-__device__ __forceinline__ void gm_dequant_q6(const uint8_t* grp, uint8_t* Ahi, uint8_t* Alo, int gi, int h,
-                                              int lane, float wsc, int step0) {
+__device__ __forceinline__ void gm_dequant_q6(const uint8_t* lrec, const uint8_t* scs, uint8_t* Ahi, uint8_t* Alo,
+                                              int gi, int h, int lane, float wsc, int step0) {
     const int lr = lane >> 2, t = lane & 3, row = gi * 8 + lr;
-    const uint4 rec = *(const uint4*)(grp + h * 512 + lane * 16);
+    const uint4 rec = *(const uint4*)(lrec + h * 512 + lane * 16);
     const uint32_t wv[4] = {rec.x, rec.y, rec.z, rec.w};
-    const int8_t* scp = (const int8_t*)(grp + 1024) + lr * 64;
-    const uint16_t* dp = (const uint16_t*)(grp + 1024 + 512) + lr * 4;
+    const int8_t* scp = (const int8_t*)scs + lr * 64;
+    const uint16_t* dp = (const uint16_t*)(scs + 512) + lr * 4;
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
         const int step = step0 + h * 4 + s;  // sub-block index in the chunk, 0..63
@@ -332,17 +326,6 @@ __device__ __forceinline__ void gm_epi(const GemmArgs& a, const GemmSeg& sg, int
                                        float* v, const float* xs, const uint32_t* ps) {
 #pragma unroll
     for (int j = 0; j < W; ++j) v[j] *= xs[j];
-    if (sg.epi == EPI_B_SWIGLU) {  // src/math/ops.rs:33-37: gate lanes r % 16 < 8, up on lane + 8
-        float up[W];
-#pragma unroll
-        for (int j = 0; j < W; ++j) up[j] = __shfl_down_sync(0xffffffffu, v[j], 8);
-        const int row = lt * 64 + (r >> 4) * 8 + (r & 7);
-        if ((r & 8) || row >= sg.rows) return;
-#pragma unroll
-        for (int j = 0; j < W; ++j)
-            if (t0 + j < ntok) sg.y[(size_t)(t0 + j) * sg.ldy + row] = __fmul_rn(silu_ref(v[j]), up[j]);
-        return;
-    }
     const int row = lt * GM_BM + r;
     if (sg.epi >= EPI_B_ROPE) {
         // pairs (2i, 2i+1) on lanes l, l ^ 1 (src/math/ops.rs:48-61); then the cache
@@ -450,48 +433,57 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     auto stop = [&]() { return *(volatile int*)&s_flag[0] != 0; };
 
     if (warp == GM_WP) {
-        // ---------------- weight producer: lane gi (< 16) copies row group gi's data
+        // ---------------- weight producer: per raw slot, two TMA copies (the 16
+        // groups' lane records, then their scales) through the segment's tensor
+        // maps, or (no maps) lane gi's 1-D bulk copies of row group gi
         uint32_t ri = 0;
-        for (int u = blockIdx.x; u < nunits && !stop(); u += gridDim.x) {
+        bool ok = true;
+        for (int u = blockIdx.x; u < nunits && ok && !stop(); u += gridDim.x) {
             const GmUnit U = gm_unit(a, u, ntt);
             const GemmSeg& sg = a.seg[U.si];
-            int g = 0;
-            const PackedW* w = lane < 16 ? gm_group(sg, U.lt, lane, g) : nullptr;
-            const bool valid = w && g < w->rows_pad / 8;
-            const uint32_t bytes = (uint32_t)__popc(__ballot_sync(0xffffffffu, valid)) * C::GRP;
-            bool ok = true;
+            const int g = U.lt * 16 + lane;
+            const bool valid = lane < 16 && g < sg.A.rows_pad / 8;
+            const uint32_t bytes =
+                sg.wmap ? (uint32_t)C::RAW : (uint32_t)__popc(__ballot_sync(0xffffffffu, valid)) * C::GRP;
             for (int rs = U.r0; rs < U.r1; ++rs, ++ri) {
                 const int slot = ri % C::NRAW;
+                uint8_t* dst = sR + slot * C::RAW;
                 bool w_ok = true;
                 if (lane == 0) {
                     w_ok = mbar_wait(&raw_empty[slot], ((ri / C::NRAW) & 1) ^ 1);
-                    if (w_ok) mbar_expect_tx(&raw_full[slot], bytes);
+                    if (w_ok) {
+                        mbar_expect_tx(&raw_full[slot], bytes);
+                        if (sg.wmap) {  // out-of-range groups of the last tile read as zeros
+                            const int c = rs * GM_RK / GmFmt<TYPE>::CK;
+                            tma_load_3d(dst, (const CUtensorMap*)sg.map_lrec, gm_lrec_off<TYPE>(rs) / 4, c, U.lt * 16,
+                                        &raw_full[slot]);
+                            tma_load_3d(dst + 16 * GmFmt<TYPE>::LREC, (const CUtensorMap*)sg.map_sc,
+                                        gm_sc_off<TYPE>(rs) / 4, c, U.lt * 16, &raw_full[slot]);
+                        }
+                    }
                 }
                 if (!__shfl_sync(0xffffffffu, (int)w_ok, 0)) {
                     ok = false;
                     break;
                 }
-                if (valid) {
+                if (!sg.wmap && valid) {
                     const uint8_t *lr, *sc;
-                    gm_src<TYPE>(*w, g, rs, lr, sc);
-                    uint8_t* dst = sR + slot * C::RAW + lane * C::GRP;
-                    bulk_g2s(dst, lr, GmFmt<TYPE>::LREC, &raw_full[slot]);
-                    bulk_g2s(dst + GmFmt<TYPE>::LREC, sc, GmFmt<TYPE>::SC, &raw_full[slot]);
+                    gm_src<TYPE>(sg.A, g, rs, lr, sc);
+                    bulk_g2s(dst + lane * GmFmt<TYPE>::LREC, lr, GmFmt<TYPE>::LREC, &raw_full[slot]);
+                    bulk_g2s(dst + 16 * GmFmt<TYPE>::LREC + lane * GmFmt<TYPE>::SC, sc, GmFmt<TYPE>::SC,
+                             &raw_full[slot]);
                 }
             }
-            if (!ok) {
-                if (lane == 0) fail();
-                break;
-            }
         }
+        if (!ok && lane == 0) fail();
         // copies in flight land before the CTA exits
         if (lane == 0) {
             const uint32_t first = ri > (uint32_t)C::NRAW ? ri - C::NRAW : 0;
             for (uint32_t j = first; j < ri; ++j) mbar_wait(&raw_full[j % C::NRAW], (j / C::NRAW) & 1);
         }
     } else if (warp == GM_XP) {
-        // ---------------- activation producer: TMA tiles of the [x_hi; x_lo] planes,
-        // lane i (< 8) copies the stage's 8-input group i
+        // ---------------- activation producer: one TMA box per stage, the stage's
+        // 64 inputs of the tile's columns in both planes (128-byte swizzle)
         uint32_t si = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < nunits && ok && !stop(); u += gridDim.x) {
@@ -508,9 +500,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                         ok = false;
                         break;
                     }
-                    if (lane < GM_BK / 8)
-                        tma_load_3d(sB + s * C::B_BYTES + lane * (2 * NT * 16), &tmx, rs * GM_RK + h * GM_BK + 8 * lane,
-                                    U.tt * NT, 0, &b_full[s]);
+                    if (lane == 0) tma_load_3d(sB + s * C::B_BYTES, &tmx, rs * GM_RK + h * GM_BK, U.tt * NT, 0, &b_full[s]);
                 }
         }
         if (!ok && lane == 0) fail();
@@ -522,7 +512,6 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         // ---------------- MMA issuer
         if (lane == 0) {
             uint32_t si = 0, nu = 0;
-            const uint32_t lbo_a = GM_BM * 16, lbo_b = 2 * NT * 16, sbo = 128;
             for (int u = blockIdx.x; u < nunits && !stop(); u += gridDim.x, ++nu) {
                 const GmUnit U = gm_unit(a, u, ntt);
                 const int ab = nu & 1;
@@ -547,10 +536,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                         const uint32_t bb = smem_u32(sB + s * C::B_BYTES);
 #pragma unroll
                         for (int kk = 0; kk < GM_BK / 16; ++kk) {
-                            const uint64_t bd = umma_desc(bb + kk * 2 * lbo_b, lbo_b, sbo);
-                            umma_f16(d, umma_desc(ah + kk * 2 * lbo_a, lbo_a, sbo), bd, umma_idesc(2 * NT),
+                            const uint64_t bd = umma_desc_sw128(bb + kk * 32);
+                            umma_f16(d, umma_desc_sw128(ah + kk * 32), bd, umma_idesc(2 * NT),
                                      (first && kk == 0) ? 0u : 1u);
-                            umma_f16(d, umma_desc(al + kk * 2 * lbo_a, lbo_a, sbo), bd, umma_idesc(NT), 1u);
+                            umma_f16(d, umma_desc_sw128(al + kk * 32), bd, umma_idesc(NT), 1u);
                         }
                         first = false;
                         umma_commit(&st_empty[s]);  // the stage's A and B are free once these MMAs finish
@@ -599,10 +588,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 2; ++j) {
                         const int gi = dw + 8 * j;
+                        const uint8_t* lrec = raw + gi * GmFmt<TYPE>::LREC;
+                        const uint8_t* scs = raw + 16 * GmFmt<TYPE>::LREC + gi * GmFmt<TYPE>::SC;
                         if (TYPE == GT_Q6_K)
-                            gm_dequant_q6(raw + gi * C::GRP, Ahi, Alo, gi, h, lane, wsc, ((rs * GM_RK) % 1024) / 16);
+                            gm_dequant_q6(lrec, scs, Ahi, Alo, gi, h, lane, wsc, ((rs * GM_RK) % 1024) / 16);
                         else
-                            gm_dequant<TYPE>(raw + gi * C::GRP, Ahi, Alo, gi, h, lane, wsc);
+                            gm_dequant<TYPE>(lrec, scs, Ahi, Alo, gi, h, lane, wsc);
                     }
                     fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core's reads
                     __syncwarp();
@@ -790,25 +781,65 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+static EncodeTiledFn g_enc = nullptr;
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link to libcuda).
+static cudaError_t gemm_encoder() {
+    if (g_enc) return cudaSuccess;
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
+    if (e != cudaSuccess) return e;
+    if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+    g_enc = (EncodeTiledFn)fn;
+    return cudaSuccess;
+}
+
 cudaError_t gemm_tensor_map(void* planes, int ldp, int Tp, int nt, void* map_out) {
-    static EncodeTiledFn enc = nullptr;
-    if (!enc) {
-        cudaDriverEntryPointQueryResult q;
-        void* fn = nullptr;
-        cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
-        if (e != cudaSuccess) return e;
-        if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
-        enc = (EncodeTiledFn)fn;
-    }
-    // dims: k (ldp halves, contiguous), token t (Tp), plane (2: hi, lo); box 8 x nt x 2
+    cudaError_t e = gemm_encoder();
+    if (e != cudaSuccess) return e;
+    EncodeTiledFn enc = g_enc;
+    // dims: k (ldp halves, contiguous), token t (Tp), plane (2: hi, lo); box
+    // 64 x nt x 2: one stage's inputs, 128 bytes per (plane, column) row, swizzled
     const cuuint64_t dims[3] = {(cuuint64_t)ldp, (cuuint64_t)Tp, 2};
     const cuuint64_t strides[2] = {(cuuint64_t)ldp * 2, (cuuint64_t)Tp * ldp * 2};
-    const cuuint32_t box[3] = {8, (cuuint32_t)nt, 2};
+    const cuuint32_t box[3] = {GM_BK, (cuuint32_t)nt, 2};
     const cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc((CUtensorMap*)map_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, planes, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// The two tensor maps of a packed quant weight for the GEMM's weight producer:
+// the packed array viewed as u32 [groups][chunks][GCB / 4], boxes of 16 groups x
+// one chunk x (the lane records of one raw slot | its scales).
+template <int TYPE>
+static cudaError_t gemm_weight_maps_t(const PackedW& w, void* lrec_map, void* sc_map) {
+    using F = GmFmt<TYPE>;
+    const cuuint64_t dims[3] = {(cuuint64_t)F::GCB / 4, (cuuint64_t)w.nk, (cuuint64_t)w.rows_pad / 8};
+    const cuuint64_t strides[2] = {(cuuint64_t)F::GCB, (cuuint64_t)F::GCB * w.nk};
+    const cuuint32_t box_l[3] = {(cuuint32_t)F::LREC / 4, 1, 16};
+    const cuuint32_t box_s[3] = {(cuuint32_t)F::SC / 4, 1, 16};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_enc((CUtensorMap*)lrec_map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, (void*)w.p0, dims, strides, box_l,
+                       estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r == CUDA_SUCCESS)
+        r = g_enc((CUtensorMap*)sc_map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, (void*)w.p0, dims, strides, box_s, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t gemm_weight_maps(const PackedW& w, void* lrec_map, void* sc_map) {
+    cudaError_t e = gemm_encoder();
+    if (e != cudaSuccess) return e;
+    switch (w.type) {
+        case GT_Q4_0: return gemm_weight_maps_t<GT_Q4_0>(w, lrec_map, sc_map);
+        case GT_Q8_0: return gemm_weight_maps_t<GT_Q8_0>(w, lrec_map, sc_map);
+        case GT_Q6_K: return gemm_weight_maps_t<GT_Q6_K>(w, lrec_map, sc_map);
+    }
+    return cudaErrorInvalidValue;
 }
 
 size_t gemm_map_bytes() { return sizeof(CUtensorMap); }

@@ -520,6 +520,22 @@ __global__ void __launch_bounds__(ATB_WARPS * 32) k_attention_b(const float* q, 
     }
 }
 
+__global__ void k_swiglu_b(const float* g, const float* u, float* h, int ld, int n_ff, const BatchParams* bp) {
+    const int s = blockIdx.y;
+    if (s >= bp->n) return;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n_ff) {
+        const size_t o = (size_t)s * ld + i;
+        h[o] = __fmul_rn(silu_ref(g[o]), u[o]);
+    }
+}
+
+cudaError_t launch_swiglu_b(const float* g, const float* u, float* h, int ld, int n_ff, const BatchParams* bp,
+                            cudaStream_t s) {
+    k_swiglu_b<<<dim3((n_ff + 255) / 256, MB_SEQ), 256, 0, s>>>(g, u, h, ld, n_ff, bp);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_attention_b(const float* q, int ldq, const float* kc, const float* vc, size_t seq_stride,
                                int kv_dim, int n_head, int n_kv, int hd, float* out, int ldo, const BatchParams* bp,
                                cudaStream_t s) {

@@ -90,20 +90,21 @@ struct BatchParams {
     uint32_t error;            // device-side error bits (1: token out of range, 2: a bounded wait expired)
 };
 
-// Batched epilogues: store / add rows; SwiGLU of paired gate (A) / up (B) rows;
-// RoPE of q rows (stored to y); RoPE of k rows and v rows, appended to the
-// column's cache slot at its position.
+// Batched epilogues: store / add rows; RoPE of q rows (stored to y); RoPE of k
+// rows and v rows, appended to the column's cache slot at its position.
 enum { EPI_B_STORE = 0, EPI_B_ADD = 1, EPI_B_SWIGLU = 2, EPI_B_ROPE = 3, EPI_B_KCACHE = 4, EPI_B_VCACHE = 5 };
 
-// One weight of a GEMM launch. Tiles are 128 rows of A; a SwiGLU pair tile is
-// 64 gate rows of A and the same 64 up rows of B.
+// One weight of a GEMM launch: tiles of 128 rows of A. map_lrec / map_sc are
+// A's two tensor maps (CUtensorMap, gemm_weight_maps) when wmap is set.
 struct GemmSeg {
-    PackedW A, B;
-    int pair;
+    alignas(64) uint8_t map_lrec[128];
+    alignas(64) uint8_t map_sc[128];
+    PackedW A;
+    int wmap;
     int ntiles;
     float* y;      // [MB_SEQ][ldy] outputs (EPI_B_KCACHE / VCACHE: unused)
     int ldy;
-    int rows;      // logical output rows (pair: ff rows)
+    int rows;      // logical output rows
     int epi;
 };
 struct GemmArgs {
@@ -131,6 +132,9 @@ cudaError_t launch_xfmt_g(const float* x, int ldx, int K, int KP, int ldp, int T
 // producer reads `planes` through with token tiles of nt columns.
 cudaError_t gemm_tensor_map(void* planes, int ldp, int Tp, int nt, void* map_out);
 size_t gemm_map_bytes();
+// The two tensor maps (gemm_map_bytes() each) of a packed Q4_0 / Q8_0 / Q6_K
+// weight through which the GEMM copies its lane records and scales.
+cudaError_t gemm_weight_maps(const PackedW& w, void* lrec_map, void* sc_map);
 // nt: token columns per tile (32, 64 or 128); grid: CTAs (one per SM at most).
 cudaError_t launch_gemm(const void* map, const GemmArgs& a, int type, int nt, int grid, cudaStream_t s);
 cudaError_t gemm_configure();
@@ -138,6 +142,9 @@ cudaError_t gemm_configure();
 // x[s] = dequant(token_embd row of token[s]) (src/model/weights.rs:57-62)
 cudaError_t launch_embed_b(const uint8_t* embd_raw, int type, int cols, int vocab, const BatchParams* bp, float* x,
                            int ldx, cudaStream_t s);
+// h[s][i] = silu(g[s][i]) * u[s][i] for the live columns (src/math/ops.rs:28-37)
+cudaError_t launch_swiglu_b(const float* g, const float* u, float* h, int ld, int n_ff, const BatchParams* bp,
+                            cudaStream_t s);
 // GQA attention per (head, sequence) over positions 0 .. pos[s] (src/model/llama.rs:135-155)
 cudaError_t launch_attention_b(const float* q, int ldq, const float* kc, const float* vc, size_t seq_stride,
                                int kv_dim, int n_head, int n_kv, int hd, float* out, int ldo, const BatchParams* bp,

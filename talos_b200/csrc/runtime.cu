@@ -132,6 +132,10 @@ struct DevTensor {
     bool in_arena = false;  // carved from a WeightArena block, not freed alone
     PackedW w{};          // packed matrix view (kind == PACKED)
     enum Kind { PACKED, FLOATS, RAW } kind = PACKED;
+    // the tensor maps through which the batched GEMM copies a packed quant
+    // matrix (gemm_weight_maps); gmap false: it copies row group by row group
+    bool gmap = false;
+    alignas(64) uint8_t gmaps[2][128];
     void release() {
         if (mem && !in_arena) cudaFree(mem);
         mem = nullptr;
@@ -231,6 +235,8 @@ static talos_status pack_from_device(int type, size_t rows, size_t cols, const u
     t->in_arena = arena != nullptr;
     t->w = w;
     t->kind = DevTensor::PACKED;
+    t->gmap = type != GT_F32 && gemm_map_bytes() <= sizeof t->gmaps[0] &&
+              gemm_weight_maps(w, t->gmaps[0], t->gmaps[1]) == cudaSuccess;
     return TALOS_OK;
 }
 
@@ -449,7 +455,7 @@ struct talos_ctx {
     BatchParams* bp = nullptr;
     BatchParams* h_bp = nullptr;  // pinned
     float *bx = nullptr, *bq = nullptr, *batt = nullptr;
-    float *bh = nullptr, *blog = nullptr;
+    float *bg = nullptr, *bu = nullptr, *bh = nullptr, *blog = nullptr;
     void* bplanes = nullptr;   // [2][MB_SEQ][bldp] f16: the GEMM input's hi / lo planes
     float* bxs = nullptr;      // [MB_SEQ] per-column scales of the formatted input
     int bldp = 0;
@@ -1679,7 +1685,8 @@ static talos_status batch_alloc(talos_ctx* c, int max_seqs) {
     };
     const size_t o_bp = take(sizeof(BatchParams));
     const size_t o_x = take(MB_SEQ * E * 4), o_q = take(MB_SEQ * c->q_rows * 4), o_att = take(MB_SEQ * E * 4),
-                 o_h = take(MB_SEQ * F * 4), o_log = take(MB_SEQ * V * 4);
+                 o_g = take(MB_SEQ * F * 4), o_u = take(MB_SEQ * F * 4), o_h = take(MB_SEQ * F * 4),
+                 o_log = take(MB_SEQ * V * 4);
     const size_t o_pl = take(2 * MB_SEQ * KPmax * 2), o_xs = take(MB_SEQ * 4);
     const size_t o_ws = take((size_t)GM_MAX_WAVES * sms * 128 * 128 * 4), o_cnt = take(GM_MAX_CNT * 4);
     const size_t seq_stride = L * c->kv_ctx * (size_t)c->kv_dim;
@@ -1692,7 +1699,7 @@ static talos_status batch_alloc(talos_ctx* c, int max_seqs) {
     c->bbytes = off;
     c->bp = (BatchParams*)(b + o_bp);
     c->bx = (float*)(b + o_x), c->bq = (float*)(b + o_q);
-    c->batt = (float*)(b + o_att), c->bh = (float*)(b + o_h);
+    c->batt = (float*)(b + o_att), c->bg = (float*)(b + o_g), c->bu = (float*)(b + o_u), c->bh = (float*)(b + o_h);
     c->blog = (float*)(b + o_log);
     c->bplanes = b + o_pl, c->bxs = (float*)(b + o_xs), c->bldp = (int)KPmax;
     c->bws = (float*)(b + o_ws), c->bcnt = (unsigned*)(b + o_cnt);
@@ -1728,12 +1735,15 @@ struct GmInput {
     int K = 0;
 };
 
-static GemmSeg gseg(const DevTensor* A, const DevTensor* B, float* y, int ldy, int rows, int epi) {
+static GemmSeg gseg(const DevTensor* A, float* y, int ldy, int rows, int epi) {
     GemmSeg g{};
     g.A = A->w;
-    g.pair = B != nullptr;
-    if (B) g.B = B->w;
-    g.ntiles = B ? (rows + 63) / 64 : (A->w.rows + 127) / 128;
+    g.wmap = A->gmap;
+    if (A->gmap) {
+        memcpy(g.map_lrec, A->gmaps[0], sizeof g.map_lrec);
+        memcpy(g.map_sc, A->gmaps[1], sizeof g.map_sc);
+    }
+    g.ntiles = (A->w.rows + 127) / 128;
     g.y = y;
     g.ldy = ldy;
     g.rows = rows;
@@ -1816,7 +1826,7 @@ static talos_status enqueue_batch(talos_ctx* c, int mode, int ntc) {
                 a.vc = vc;
                 a.seq_stride = seq_stride;
                 do {
-                    a.seg[a.nseg++] = gseg(w3[i], nullptr, c->bq, c->q_rows, rows3[i], epi3[i]);
+                    a.seg[a.nseg++] = gseg(w3[i], c->bq, c->q_rows, rows3[i], epi3[i]);
                     ++i;
                 } while (i < 3 && a.seg[0].A.type == w3[i]->type);
                 TRY(gm(c, fi, a, c->bx, (const float*)L.attn_norm->mem, ntc));
@@ -1829,21 +1839,24 @@ static talos_status enqueue_batch(talos_ctx* c, int mode, int ntc) {
         {
             GemmArgs a{};
             a.K = E;
-            a.seg[a.nseg++] = gseg(L.o, nullptr, c->bx, E, E, EPI_B_ADD);
+            a.seg[a.nseg++] = gseg(L.o, c->bx, E, E, EPI_B_ADD);
             TRY(gm(c, fi, a, c->batt, nullptr, ntc));
         }
-        // rmsnorm + SwiGLU FFN (gate/up paired; they share a type, bind_layers) +
-        // residual (:163-176)
+        // rmsnorm + SwiGLU FFN (gate and up in one GEMM launch; they share a
+        // type, bind_layers) + residual (:163-176)
         {
             GemmArgs a{};
             a.K = E;
-            a.seg[a.nseg++] = gseg(L.gate, L.up, c->bh, F, F, EPI_B_SWIGLU);
+            a.seg[a.nseg++] = gseg(L.gate, c->bg, F, F, EPI_B_STORE);
+            a.seg[a.nseg++] = gseg(L.up, c->bu, F, F, EPI_B_STORE);
             TRY(gm(c, fi, a, c->bx, (const float*)L.ffn_norm->mem, ntc));
+            e = launch_swiglu_b(c->bg, c->bu, c->bh, F, F, c->bp, c->stream);
+            if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched SwiGLU: %s", cudaGetErrorString(e));
         }
         {
             GemmArgs a{};
             a.K = F;
-            a.seg[a.nseg++] = gseg(L.down, nullptr, c->bx, E, E, EPI_B_ADD);
+            a.seg[a.nseg++] = gseg(L.down, c->bx, E, E, EPI_B_ADD);
             TRY(gm(c, fi, a, c->bh, nullptr, ntc));
         }
         fi = GmInput{};  // bx changed in place
@@ -1852,7 +1865,7 @@ static talos_status enqueue_batch(talos_ctx* c, int mode, int ntc) {
     // final norm + logits (:89, :181)
     GemmArgs a{};
     a.K = E;
-    a.seg[a.nseg++] = gseg(&c->w["output.weight"], nullptr, c->blog, V, V, EPI_B_STORE);
+    a.seg[a.nseg++] = gseg(&c->w["output.weight"], c->blog, V, V, EPI_B_STORE);
     TRY(gm(c, fi, a, c->bx, (const float*)c->w["output_norm.weight"].mem, ntc));
     return TALOS_OK;
 }
