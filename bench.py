@@ -193,6 +193,57 @@ def cpu_decode(path: str, warmup: int, steps: int, budget_s: float):
     return n / dt, n, threads, dt, pos0
 
 
+def extra_configs(model, prompt) -> dict:
+    """The other BASELINE configurations, measured on this GPU after the headline
+    run (rank 0 of a one-GPU run only):
+      c1_c2_tiny: the tiny Llama (seed 42) in F32 / Q8_0 / Q4_0, 64 greedy tokens
+          on the device after a 16-token prompt (tok/s; the weights sit in L2);
+      c3_matvec_4096: the 4096 x 4096 Q4_0 / Q8_0 fused dequant-matvec (seed 7,
+          x ~ N(0, 1)), us and algorithmic GB/s with L2 defeated by rotating copies;
+      prefill_128: this model's 128-token prompt through talos_prefill (the
+          tensor-core GEMM path, 128 positions per weight pass), host wall clock;
+      batch32: 32 sequences decoded together through talos_forward_batch (host
+          logits every step), aggregate tok/s."""
+    from talos_b200 import gguf, kbench
+
+    out = {}
+    out["c1_c2_tiny"] = {name: kbench.tiny_decode(t) for name, t in
+                         (("f32", gguf.F32), ("q8_0", gguf.Q8_0), ("q4_0", gguf.Q4_0))}
+    out["c3_matvec_4096"] = {t: {k: v for k, v in kbench.matvec_bench(t, 4096, 4096).items()
+                                 if k in ("us_per_matvec", "gbs", "copies", "algo_bytes")}
+                             for t in ("q4_0", "q8_0")}
+    best = 1e9
+    for _ in range(3):
+        t0 = time.perf_counter()
+        model.prefill(prompt, 0)
+        best = min(best, time.perf_counter() - t0)
+    out["prefill_128"] = {"ms": best * 1e3, "tok_s": len(prompt) / best, "path": "tcgen05 GEMM, 128 positions per step"}
+    nb, vocab = 32, model.cfg.vocab_size
+    model.ctx.set_batch(nb)
+    toks = synth_ids(nb, vocab)
+    # each sequence at its own position: 13 steps from positions spread over 32
+    # below the end of the context the model was loaded with (around the prompt)
+    top = min(PROMPT_LEN + 32, model.cfg.context_length - 14)
+    pos = [top - 32 + (7 * i) % 32 for i in range(nb)]
+    for i in range(3):
+        model.ctx.forward_batch(toks, [p + i for p in pos])
+    steps, t0 = 10, time.perf_counter()
+    for i in range(steps):
+        lg = model.ctx.forward_batch(toks, [p + 3 + i for p in pos])
+        toks = [argmax_last(r) for r in lg]
+    dt = (time.perf_counter() - t0) / steps
+    model.ctx.set_batch(0)
+    out["batch32"] = {"seqs": nb, "ms_per_step": dt * 1e3, "tok_s": nb / dt,
+                      "path": "tcgen05 GEMM, host logits every step"}
+    return out
+
+
+def synth_ids(n: int, vocab: int) -> list[int]:
+    from talos_b200 import synth
+
+    return synth.token_ids(3, n, vocab)
+
+
 def run_reference(args):
     """--impl reference: the CPU restatement of the reference's forward on this
     host's cores, on the GPU arm's workload: the same 128-token prompt (fed
@@ -227,6 +278,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="talos_b200", choices=["talos_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the other BASELINE configurations")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -351,6 +403,9 @@ def main():
         launches = sum(tot_n.values()) // n_prof + 1  # + the greedy-advance kernel
     achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
 
+    # ---------------- the other BASELINE configurations (rank 0 at N=1 only)
+    configs = extra_configs(model, prompt) if world == 1 and not args.no_extra else None
+
     # ---------------- CPU baseline (rank 0 at N=1 only)
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
@@ -379,6 +434,7 @@ def main():
         "gpu_launches": launches * K,
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
+        "configs": configs,
         "setup": {"model_gen_s": gen_s, "load_s": load_s},
     }
     if rank == 0:

@@ -78,40 +78,75 @@ def main(argv=None):
     if a.step:
         return step_bench(a)
 
-    import torch
-
-    from talos_b200 import build, model, synth
+    from talos_b200 import build
 
     build.build()
-    gt = TYPES[a.type]
-    torch.cuda.set_device(a.device)
-    raw = synth.tensor(a.seed, "bench.w", a.rows, a.cols, gt)
-    x = synth.normal(a.seed, "bench.x", a.cols, 1.0)
-    l2 = torch.cuda.get_device_properties(a.device).L2_cache_size
-    copies = a.copies or max(2, int(np.ceil(2 * l2 / raw.nbytes)) + 1)
-    ws = [model.Weight(gt, raw, a.rows, a.cols, a.device) for _ in range(copies)]
-    xd = torch.from_numpy(x).cuda()
-    yd = torch.empty(a.rows, device="cuda")
-    # talos_matvec_bench captures the launches into one CUDA graph and times a
-    # replay with CUDA events, so the host's per-call cost is not measured.
+    print(json.dumps(matvec_bench(a.type, a.rows, a.cols, a.seed, a.reps, a.copies, a.device)), flush=True)
+    return 0
+
+
+def matvec_bench(type_name: str, rows: int, cols: int, seed: int = 7, reps: int = 200, copies: int = 0,
+                 device: int = 0) -> dict:
+    """a seeded N(0, 0.02) [rows, cols] weight of `type_name`
+    and x ~ N(0, 1); `copies` packed copies (enough to exceed twice the L2 when
+    0), cycled through by `reps` graph-captured talos_matvec_dev launches timed
+    with CUDA events. Returns microseconds per matvec and algorithmic GB/s
+    (weight bytes in the GGUF format + x + y)."""
     import ctypes as C
 
-    from talos_b200 import _lib
+    import torch
 
+    from talos_b200 import _lib, model, synth
+
+    gt = TYPES[type_name]
+    torch.cuda.set_device(device)
+    raw = synth.tensor(seed, "bench.w", rows, cols, gt)
+    x = synth.normal(seed, "bench.x", cols, 1.0)
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    copies = copies or max(2, int(np.ceil(2 * l2 / raw.nbytes)) + 1)
+    ws = [model.Weight(gt, raw, rows, cols, device) for _ in range(copies)]
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty(rows, device="cuda")
+    # talos_matvec_bench captures the launches into one CUDA graph and times a
+    # replay with CUDA events, so the host's per-call cost is not measured.
     torch.cuda.synchronize()
     arr = (C.c_void_p * copies)(*[w.h.value for w in ws])
     us_c = C.c_float()
     _lib.check(_lib.load().talos_matvec_bench(arr, copies, C.c_void_p(xd.data_ptr()), C.c_void_p(yd.data_ptr()),
-                                              a.reps, C.byref(us_c)))
+                                              reps, C.byref(us_c)))
     us = float(us_c.value)
-    algo = a.rows * a.cols * ALGO_BYTES_PER_ELEM[gt] + 4 * (a.rows + a.cols)
-    out = {"kernel": f"matvec_{a.type}", "rows": a.rows, "cols": a.cols, "copies": copies,
+    algo = rows * cols * ALGO_BYTES_PER_ELEM[gt] + 4 * (rows + cols)
+    out = {"kernel": f"matvec_{type_name}", "rows": rows, "cols": cols, "copies": copies,
            "l2_bytes": l2, "us_per_matvec": us, "algo_bytes": algo, "gbs": algo / (us * 1e-6) / 1e9,
            "packed_bytes": ws[0].packed_bytes()}
-    print(json.dumps(out), flush=True)
     for w in ws:
         w.close()
-    return 0
+    return out
+
+
+def tiny_decode(wtype: int, device: int = 0) -> dict:
+    """BASELINE configs 1 / 2: the tiny Llama (seed 42) with every 2-D weight in
+    `wtype`, a 16-token prompt, then 64 greedy tokens decoded on the device
+    (talos_generate_greedy), timed with CUDA events. The weights sit in L2
+    (26 MB at most), so the step is latency-bound."""
+    import torch
+
+    from talos_b200 import Model, synth
+
+    m = Model.load_bytes(synth.llama_bytes(synth.TINY, 42, wtype=wtype), device=device)
+    prompt = synth.token_ids(42, 16, synth.TINY.vocab)
+    tok = argmax_last(m.prefill(prompt, 0))
+    m.generate_greedy(tok, 16, 8)  # warm-up (graph capture)
+    stream = torch.cuda.ExternalStream(m.ctx.stream(), device=torch.device("cuda", device))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    m.generate_greedy(tok, 16, 64)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    m.close()
+    return {"tokens": 64, "ms": ms, "tok_s": 64 / (ms / 1e3), "step_kernel": "fused"}
 
 
 def step_bench(a) -> int:
