@@ -93,6 +93,19 @@ talos_status talos_ctx_create_tp(const talos_cfg* cfg, int device, int tp_size, 
                                  const uint8_t* nccl_unique_id, talos_ctx** out);
 talos_status talos_nccl_unique_id(uint8_t out[128]);
 
+/*
+ * Tensor parallel: the ranks of a context wait for each other inside every
+ * step, each wait bounded (2 s). When any rank's step returns
+ * TALOS_ERR_TIMEOUT (a rank that never launched its step, or one that stopped),
+ * the ranks' barrier counters no longer agree: every rank then calls
+ * talos_ctx_tp_resync while no rank has a step in flight (between two host-side
+ * barriers of the caller), which waits for this rank's stream and clears its
+ * counters; the next step on all ranks starts afresh. Until then every batched
+ * step of a rank that saw the failure reports it again. On one GPU it only
+ * clears the per-token kernel's counters. No reference counterpart.
+ */
+talos_status talos_ctx_tp_resync(talos_ctx* ctx);
+
 talos_status talos_ctx_destroy(talos_ctx* ctx);
 
 /*
@@ -194,10 +207,11 @@ talos_status talos_generate_greedy(talos_ctx* ctx, uint32_t token, size_t pos, s
 /*
  * Feed `n` prompt tokens at positions pos0 .. pos0+n-1 (the prefill loop of
  * src/main.rs:88-95) and write the logits after the last one to `last_logits`
- * (host, may be NULL). On one GPU with an f32 cache and Q4_0 / Q8_0 / Q6_K
- * matrices the prompt goes through the batched step, up to 128 consecutive
- * positions per weight pass on the tensor cores (each position attends to the
- * ones before it, as token-by-token feeding does); otherwise one token per step.
+ * (host, may be NULL). With an f32 cache and Q4_0 / Q8_0 / Q6_K matrices the
+ * prompt goes through the batched step, up to 128 consecutive positions per
+ * weight pass on the tensor cores (each position attends to the ones before it,
+ * as token-by-token feeding does); otherwise one token per step. Under tensor
+ * parallelism every rank makes the call with the same arguments.
  */
 talos_status talos_prefill(talos_ctx* ctx, const uint32_t* tokens, size_t n, size_t pos0,
                            float* last_logits);
@@ -209,7 +223,10 @@ talos_status talos_prefill(talos_ctx* ctx, const uint32_t* tokens, size_t n, siz
  * `max_seqs` cache slots of the context's current context length each (0 frees
  * them; reserving empties them) for the context's model, which must have
  * Q4_0 / Q8_0 / Q6_K matrices and head_dim <= 128 (TALOS_ERR_UNSUPPORTED
- * otherwise, and under tensor parallelism). talos_forward_batch runs one step
+ * otherwise). Under tensor parallelism every rank makes each of these calls
+ * with the same arguments (talos_ctx_set_batch maps the ranks' exchange areas;
+ * each step's row-parallel products are summed across ranks inside the step)
+ * and every rank gets all vocab_size logits. talos_forward_batch runs one step
  * for sequences 0 .. n-1 (n <= max_seqs): sequence i feeds tokens[i] at
  * position pos[i] into slot i and gets its vocab_size logits at
  * logits_out + i * vocab_size (host). Each sequence computes what

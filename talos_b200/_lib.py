@@ -38,6 +38,7 @@ SIGNATURES = {
     "talos_ctx_create": (_i, [C.POINTER(Cfg), _i, C.POINTER(_vp)]),
     "talos_ctx_create_tp": (_i, [C.POINTER(Cfg), _i, _i, _i, _vp, C.POINTER(_vp)]),
     "talos_nccl_unique_id": (_i, [_vp]),
+    "talos_ctx_tp_resync": (_i, [_vp]),
     "talos_ctx_destroy": (_i, [_vp]),
     "talos_weight_upload": (_i, [_vp, C.c_char_p, _vp, _sz, _i, _sz, _sz]),
     "talos_ctx_set_step_kernel": (_i, [_vp, _i]),

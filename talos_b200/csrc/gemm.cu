@@ -327,7 +327,7 @@ __device__ __forceinline__ void gm_epi(const GemmArgs& a, const GemmSeg& sg, int
 #pragma unroll
     for (int j = 0; j < W; ++j) v[j] *= xs[j];
     const int row = lt * GM_BM + r;
-    if (sg.epi >= EPI_B_ROPE) {
+    if (sg.epi >= EPI_B_ROPE && sg.epi <= EPI_B_VCACHE) {
         // pairs (2i, 2i+1) on lanes l, l ^ 1 (src/math/ops.rs:48-61); then the cache
         // append of src/kv_cache.rs:21-26 at the column's slot and position
         float pv[W];
@@ -363,6 +363,15 @@ __device__ __forceinline__ void gm_epi(const GemmArgs& a, const GemmSeg& sg, int
 #pragma unroll
         for (int j = 0; j < W; ++j)
             if (t0 + j < ntok) sg.y[(size_t)(t0 + j) * sg.ldy + row] = __fadd_rn(old[j], v[j]);
+        return;
+    }
+    if (sg.epi == EPI_B_PEER) {  // tensor parallel: this rank's rows to every rank
+        for (int pr = 0; pr < a.npeer; ++pr) {
+            float* dst = a.peer[pr] + row;
+#pragma unroll
+            for (int j = 0; j < W; ++j)
+                if (t0 + j < ntok) dst[(size_t)(t0 + j) * sg.ldy] = v[j];
+        }
         return;
     }
 #pragma unroll
@@ -690,6 +699,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     // ---------------- teardown: every role is out of its loop
     tc_fence_before();
     __syncthreads();
+    // tensor parallel: the CTA's peer stores are done; the release at system
+    // scope carries them (through the barrier above) to k_tp_join_b's acquire
+    if (a.lar && threadIdx.x == 0) red_release_sys_add_u64(a.lar, 1ull);
     if (warp == GM_MMA) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TCOLS));

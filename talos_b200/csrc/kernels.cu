@@ -9,6 +9,7 @@
 #include <math.h>
 
 #include "kernels.cuh"
+#include "ptx.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -546,5 +547,65 @@ cudaError_t launch_attention_b(const float* q, int ldq, const float* kc, const f
     return cudaGetLastError();
 }
 
+
+// ---------------------------------------------------------------- tensor-parallel join
+
+// Bounded spin of one thread until *c >= target (system scope: peers add to c).
+__device__ __noinline__ bool tp_wait(const unsigned long long* c, unsigned long long target) {
+    if (ld_acquire_sys_u64(c) >= target) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        for (int i = 0; i < 16; ++i)
+            if (ld_acquire_sys_u64(c) >= target) return true;
+        if (globaltimer_ns() - t0 > 2000000000ull) return false;
+    }
+}
+__device__ __forceinline__ unsigned ld_volatile_u32(const unsigned* p) { return *(const volatile unsigned*)p; }
+
+// The join after each EPI_B_PEER GEMM of a tensor-parallel batched step. CTA 0
+// takes the GEMM's exit arrivals (an acquire of what its CTAs released, so their
+// peer stores are ordered before what this thread releases next), clears that
+// counter for the next GEMM, and adds 1 at system scope to counter `inst` of
+// every rank. Then every CTA waits until all tp ranks have arrived in this step:
+// (tpstep + 1) * tp, the counters growing across steps until talos_ctx_tp_resync
+// clears them. With rx set the ranks' partial rows are added to the residual in
+// rank order, x += ((rx_0 + rx_1) + ...) (src/model/llama.rs:159-161, 174-176,
+// the row-parallel product split over ranks); every rank sums the same slots in
+// the same order, so the residual stays identical on all ranks.
+// A wait that runs out (2 s) sets error bit 2 and every rank's abort word. A
+// step that has already failed, or whose abort word a peer has set, skips its
+// waits but still signals, so every rank leaves the step soon and reports it.
+__global__ void __launch_bounds__(256) k_tp_join_b(TpJoin j, BatchParams* bp) {
+    __shared__ int go;
+    if (threadIdx.x == 0) {
+        bool ok = true;
+        if (blockIdx.x == 0) {
+            // the GEMM ended before this launch (stream order): no real wait
+            ok = tp_wait(j.lar, j.lar_target);
+            *j.lar = 0ull;
+            for (int r = 0; r < j.tp; ++r) red_release_sys_add_u64(j.prarr[r] + j.inst, 1ull);
+        }
+        const bool failed = ld_volatile_u32(&bp->error) != 0u || ld_volatile_u32(j.abort) != 0u;
+        if (ok && !failed) ok = tp_wait(j.rarr + j.inst, ((unsigned long long)bp->tpstep + 1ull) * (unsigned)j.tp);
+        if (!ok) {
+            atomicOr(&bp->error, 2u);
+            for (int r = 0; r < j.tp; ++r) atomicExch_system(j.pabort[r], 1u);
+        }
+        go = ok && !failed && ld_volatile_u32(j.abort) == 0u;
+    }
+    __syncthreads();
+    if (!go || !j.rx) return;
+    const size_t n = (size_t)bp->n * j.E, slot = (size_t)MB_SEQ * j.E;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float acc = __ldcg(j.rx + i);
+        for (int r = 1; r < j.tp; ++r) acc = __fadd_rn(acc, __ldcg(j.rx + r * slot + i));
+        j.x[i] = __fadd_rn(j.x[i], acc);
+    }
+}
+
+cudaError_t launch_tp_join_b(const TpJoin& j, BatchParams* bp, int grid, cudaStream_t s) {
+    k_tp_join_b<<<grid, 256, 0, s>>>(j, bp);
+    return cudaGetLastError();
+}
 
 }  // namespace talos

@@ -82,17 +82,23 @@ cudaError_t launch_matvec_noalloc(const PackedW& w, const float* x, float* y, in
 // two scale, f16 hi / lo planes), k_gemm multiplies the packed weights into it.
 
 constexpr int MB_SEQ = 128;
+constexpr int TALOS_MAX_TP = 8;  // tensor-parallel ranks (one per GPU)
 
 struct BatchParams {
     int n;                     // active token columns (1 .. MB_SEQ)
     uint32_t token[MB_SEQ];
     uint32_t pos[MB_SEQ];
     uint32_t error;            // device-side error bits (1: token out of range, 2: a bounded wait expired)
+    uint32_t tpstep;           // tensor parallel: earlier batched steps of the context (k_tp_join_b targets)
 };
 
 // Batched epilogues: store / add rows; RoPE of q rows (stored to y); RoPE of k
-// rows and v rows, appended to the column's cache slot at its position.
-enum { EPI_B_STORE = 0, EPI_B_ADD = 1, EPI_B_SWIGLU = 2, EPI_B_ROPE = 3, EPI_B_KCACHE = 4, EPI_B_VCACHE = 5 };
+// rows and v rows, appended to the column's cache slot at its position;
+// EPI_B_PEER (tensor parallel): the rows go to every rank r at
+// GemmArgs::peer[r] + t * ldy + row (this rank's receive slot of a row-parallel
+// product, or its vocabulary range of the gathered logits).
+enum { EPI_B_STORE = 0, EPI_B_ADD = 1, EPI_B_SWIGLU = 2, EPI_B_ROPE = 3, EPI_B_KCACHE = 4, EPI_B_VCACHE = 5,
+       EPI_B_PEER = 6 };
 
 // One weight of a GEMM launch: tiles of 128 rows of A. map_lrec / map_sc are
 // A's two tensor maps (CUtensorMap, gemm_weight_maps) when wmap is set.
@@ -122,6 +128,12 @@ struct GemmArgs {
     const BatchParams* bp;
     float* ws;             // split-K partial tiles [tiles][S][NT][128]
     unsigned* cnt;         // split-K arrival counters [tiles][4], zero between launches
+    // tensor parallel (EPI_B_PEER): each rank's destination (CUDA IPC mappings;
+    // this rank's own memory at [rank]), and the local counter every CTA adds 1
+    // to at exit, after its peer stores (k_tp_join_b reads it)
+    float* peer[TALOS_MAX_TP];
+    int npeer;
+    unsigned long long* lar;
 };
 // Format columns 0 .. ncols-1 of `x` ([n][ldx] f32; columns n .. ncols-1
 // become zeros) for a GEMM whose weights have K inputs: f16 hi / lo planes
@@ -138,6 +150,25 @@ cudaError_t gemm_weight_maps(const PackedW& w, void* lrec_map, void* sc_map);
 // nt: token columns per tile (32, 64 or 128); grid: CTAs (one per SM at most).
 cudaError_t launch_gemm(const void* map, const GemmArgs& a, int type, int nt, int grid, cudaStream_t s);
 cudaError_t gemm_configure();
+
+// Tensor-parallel join after an EPI_B_PEER GEMM of `grid` CTAs (instance `inst`
+// of the step): signal every rank, wait (bounded) for all ranks' rows, and when
+// rx is set add the ranks' partial rows (rx: [tp][MB_SEQ][E], rank order) to
+// the residual x ([MB_SEQ][E]). abort: this rank's abort word, which a rank that
+// gave up a wait sets on every rank so that all of them report the failure.
+struct TpJoin {
+    unsigned long long* lar;                  // local: CTAs of the GEMM that have exited
+    unsigned lar_target;                      // the GEMM's grid
+    unsigned long long* rarr;                 // own arrival counters [instances]
+    unsigned long long* prarr[TALOS_MAX_TP];  // every rank's arrival counters
+    unsigned* abort;                          // own abort word
+    unsigned* pabort[TALOS_MAX_TP];           // every rank's abort word
+    int inst, tp;
+    const float* rx;                          // receive slots of this instance, or null
+    float* x;
+    int E;
+};
+cudaError_t launch_tp_join_b(const TpJoin& j, BatchParams* bp, int grid, cudaStream_t s);
 
 // x[s] = dequant(token_embd row of token[s]) (src/model/weights.rs:57-62)
 cudaError_t launch_embed_b(const uint8_t* embd_raw, int type, int cols, int vocab, const BatchParams* bp, float* x,
@@ -204,8 +235,6 @@ struct TokenPhase {
     MatvecArgs mv;  // PH_MATVEC
     AttnArgs at;    // PH_ATTN
 };
-
-constexpr int TALOS_MAX_TP = 8;
 
 struct TokenArgs {
     const TokenPhase* ph;       // device array of nph phases

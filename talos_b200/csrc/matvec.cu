@@ -992,23 +992,6 @@ __host__ __device__ constexpr int gcb_of(int type) {
                                               : (type == GT_Q6_K ? Fmt<GT_Q6_K>::GCB : Fmt<GT_F32>::GCB));
 }
 
-__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void red_release_add_u64(unsigned long long* p, unsigned long long v) {
-    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-// System scope: counters that CTAs on other GPUs (tensor-parallel ranks) add to.
-__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void red_release_sys_add_u64(unsigned long long* p, unsigned long long v) {
-    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
 // Bounded spin of one thread until *bar >= target.
 __device__ __noinline__ bool grid_wait_one(const unsigned long long* bar, unsigned long long target, bool sys) {
     auto ld = [&]() { return sys ? ld_acquire_sys_u64(bar) : ld_acquire_u64(bar); };
@@ -2044,6 +2027,8 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_token(const __grid_constant__
             if (tid == 0 && a.tp > 1) tk_arrive(a, p, P.xrank != 0);
         }
     }
+    // a phase left at its gate may still have norm-weight copies in flight
+    asm volatile("cp.async.wait_all;" ::: "memory");
     if (tid == 0 && blockIdx.x == 0 && !*(volatile int*)&sh.err) {
         // tensor parallel: the kernel ends only when every rank's last phase (its
         // stores into this rank's logits and argmax key) is done

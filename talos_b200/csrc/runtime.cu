@@ -466,6 +466,15 @@ struct talos_ctx {
     float* h_blog = nullptr;               // pinned [TALOS_MAX_BATCH][V]
     alignas(64) uint8_t bmaps[3][128];     // tensor maps of bplanes for 32 / 64 / 128-column tiles
     cudaGraphExec_t bgraph[3][3] = {};     // [BatchMode][token-tile size]
+    // tensor parallel: the batched steps' IPC-exported area {arrival counters
+    // [2 n_layer + 1], abort word, receive slots [2][tp][MB_SEQ][E], gathered
+    // logits [MB_SEQ][V]}, every rank's mapping of it, and the local count of
+    // exited GEMM CTAs (k_tp_join_b)
+    void* bsh = nullptr;
+    void* bsh_peer[TALOS_MAX_TP] = {};
+    size_t bsh_sync_bytes = 0, bsh_o_abort = 0, bsh_o_rx = 0, bsh_o_log = 0;
+    unsigned long long* blar = nullptr;
+    uint32_t btpstep = 0;                  // batched steps run (every rank runs the same ones)
 
     void drop_batch_graphs() {
         for (auto& row : bgraph)
@@ -653,6 +662,48 @@ static void reset_sync(talos_ctx* c) {
     }
 }
 
+// Export `mem` (a cudaMalloc base) by CUDA IPC and map every rank's export
+// into peers[] (peers[rank] = mem): one NCCL all-gather of the handles, so every
+// rank makes this call at the same point. With check_gpus, ranks sharing a GPU
+// are refused (their kernels wait on each other and must run concurrently).
+static talos_status ipc_exchange(talos_ctx* c, void* mem, void** peers, bool check_gpus) {
+    struct Xch {
+        cudaIpcMemHandle_t h;
+        int pci_domain, pci_bus, pci_dev, pad;
+    };
+    Xch me{};
+    CK(cudaIpcGetMemHandle(&me.h, mem));
+    CK(cudaDeviceGetAttribute(&me.pci_domain, cudaDevAttrPciDomainId, c->device));
+    CK(cudaDeviceGetAttribute(&me.pci_bus, cudaDevAttrPciBusId, c->device));
+    CK(cudaDeviceGetAttribute(&me.pci_dev, cudaDevAttrPciDeviceId, c->device));
+    void* d = nullptr;
+    CK(cudaMalloc(&d, sizeof(Xch) * (c->tp + 1)));
+    CK(cudaMemcpy(d, &me, sizeof me, cudaMemcpyHostToDevice));
+    ncclResult_t nr = nccl().AllGather(d, (uint8_t*)d + sizeof(Xch), sizeof(Xch), ncclUint8, c->comm, c->stream);
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    std::vector<Xch> all(c->tp);
+    if (nr == ncclSuccess && e == cudaSuccess)
+        e = cudaMemcpy(all.data(), (uint8_t*)d + sizeof(Xch), sizeof(Xch) * c->tp, cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    if (nr != ncclSuccess)
+        return set_err(TALOS_ERR_NCCL, "all-gather of IPC handles: %s", nccl().GetErrorString(nr));
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "all-gather of IPC handles: %s", cudaGetErrorString(e));
+    if (check_gpus)
+        for (int r = 0; r < c->tp; ++r)
+            for (int q = 0; q < r; ++q)
+                if (all[r].pci_domain == all[q].pci_domain && all[r].pci_bus == all[q].pci_bus &&
+                    all[r].pci_dev == all[q].pci_dev)
+                    return set_err(TALOS_ERR_UNSUPPORTED, "ranks %d and %d share one GPU (one rank per GPU)", q, r);
+    for (int r = 0; r < c->tp; ++r) {
+        if (r == c->rank) {
+            peers[r] = mem;
+            continue;
+        }
+        CK(cudaIpcOpenMemHandle(&peers[r], all[r].h, cudaIpcMemLazyEnablePeerAccess));
+    }
+    return TALOS_OK;
+}
+
 // Tensor parallel: the area other ranks write into (barrier counters, step
 // parameters with the argmax key, all-reduce receive slots [2][tp][E], full
 // logits), exported by CUDA IPC and mapped by every rank. The handles and the
@@ -678,40 +729,7 @@ static talos_status alloc_shared(talos_ctx* c) {
     c->logits = (float*)(b + o_log);
     (void)o_rx;
 
-    struct Xch {
-        cudaIpcMemHandle_t h;
-        int pci_domain, pci_bus, pci_dev, pad;
-    };
-    Xch me{};
-    CK(cudaIpcGetMemHandle(&me.h, c->shared));
-    CK(cudaDeviceGetAttribute(&me.pci_domain, cudaDevAttrPciDomainId, c->device));
-    CK(cudaDeviceGetAttribute(&me.pci_bus, cudaDevAttrPciBusId, c->device));
-    CK(cudaDeviceGetAttribute(&me.pci_dev, cudaDevAttrPciDeviceId, c->device));
-    void* d = nullptr;
-    CK(cudaMalloc(&d, sizeof(Xch) * (c->tp + 1)));
-    CK(cudaMemcpy(d, &me, sizeof me, cudaMemcpyHostToDevice));
-    ncclResult_t nr = nccl().AllGather(d, (uint8_t*)d + sizeof(Xch), sizeof(Xch), ncclUint8, c->comm, c->stream);
-    cudaError_t e = cudaStreamSynchronize(c->stream);
-    std::vector<Xch> all(c->tp);
-    if (nr == ncclSuccess && e == cudaSuccess)
-        e = cudaMemcpy(all.data(), (uint8_t*)d + sizeof(Xch), sizeof(Xch) * c->tp, cudaMemcpyDeviceToHost);
-    cudaFree(d);
-    if (nr != ncclSuccess)
-        return set_err(TALOS_ERR_NCCL, "all-gather of IPC handles: %s", nccl().GetErrorString(nr));
-    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "all-gather of IPC handles: %s", cudaGetErrorString(e));
-    for (int r = 0; r < c->tp; ++r)
-        for (int q = 0; q < r; ++q)
-            if (all[r].pci_domain == all[q].pci_domain && all[r].pci_bus == all[q].pci_bus &&
-                all[r].pci_dev == all[q].pci_dev)
-                return set_err(TALOS_ERR_UNSUPPORTED, "ranks %d and %d share one GPU (one rank per GPU)", q, r);
-    for (int r = 0; r < c->tp; ++r) {
-        if (r == c->rank) {
-            c->peer_base[r] = c->shared;
-            continue;
-        }
-        CK(cudaIpcOpenMemHandle(&c->peer_base[r], all[r].h, cudaIpcMemLazyEnablePeerAccess));
-    }
-    return TALOS_OK;
+    return ipc_exchange(c, c->shared, c->peer_base, true);
 }
 
 static talos_status ctx_create(const talos_cfg* cfg, int device, int tp, int rank, const uint8_t* id,
@@ -795,7 +813,7 @@ extern "C" talos_status talos_ctx_destroy(talos_ctx* c) {
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     c->drop_graphs();
-    if (c->bmem) cudaFree(c->bmem);
+    batch_free(c);
     if (c->h_bp) cudaFreeHost(c->h_bp);
     if (c->h_blog) cudaFreeHost(c->h_blog);
     for (auto& kv : c->w) kv.second.release();
@@ -1667,6 +1685,37 @@ static talos_status batch_free(talos_ctx* c) {
     c->bmem = nullptr;
     c->bbytes = 0;
     c->bmax = 0;
+    for (int r = 0; r < TALOS_MAX_TP; ++r) {
+        if (c->bsh_peer[r] && r != c->rank) cudaIpcCloseMemHandle(c->bsh_peer[r]);
+        c->bsh_peer[r] = nullptr;
+    }
+    if (c->bsh) cudaFree(c->bsh);
+    c->bsh = nullptr;
+    c->blar = nullptr;
+    c->btpstep = 0;
+    return TALOS_OK;
+}
+
+// Tensor parallel: the batched steps' shared area (see talos_ctx::bsh), mapped
+// by every rank; every rank allocates it at the same point (talos_ctx_set_batch,
+// or the first prefill / perplexity call that takes the batched steps).
+static talos_status batch_alloc_shared(talos_ctx* c) {
+    const size_t E = c->cfg.n_embd, V = c->cfg.vocab_size, ninst = 2 * (size_t)c->cfg.n_layer + 1;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off += align256(bytes);
+        return o;
+    };
+    take(ninst * 8);
+    c->bsh_o_abort = take(4);
+    c->bsh_sync_bytes = off;
+    c->bsh_o_rx = take(2 * (size_t)c->tp * MB_SEQ * E * 4);
+    c->bsh_o_log = take((size_t)MB_SEQ * V * 4);
+    CK(cudaMalloc(&c->bsh, off));
+    CK(cudaMemset(c->bsh, 0, off));
+    TRY(ipc_exchange(c, c->bsh, c->bsh_peer, false));
+    c->blog = (float*)((uint8_t*)c->bsh + c->bsh_o_log);
     return TALOS_OK;
 }
 
@@ -1683,13 +1732,16 @@ static talos_status batch_alloc(talos_ctx* c, int max_seqs) {
         off += align256(bytes);
         return o;
     };
-    const size_t o_bp = take(sizeof(BatchParams));
-    const size_t o_x = take(MB_SEQ * E * 4), o_q = take(MB_SEQ * c->q_rows * 4), o_att = take(MB_SEQ * E * 4),
-                 o_g = take(MB_SEQ * F * 4), o_u = take(MB_SEQ * F * 4), o_h = take(MB_SEQ * F * 4),
-                 o_log = take(MB_SEQ * V * 4);
+    // tensor parallel: this rank's q / attention rows, ff rows, kv rows; the
+    // logits are gathered in the shared area
+    const size_t Q = c->q_rows, Fl = c->ff_l;
+    const size_t o_bp = take(sizeof(BatchParams)), o_lar = take(8);
+    const size_t o_x = take(MB_SEQ * E * 4), o_q = take(MB_SEQ * Q * 4), o_att = take(MB_SEQ * Q * 4),
+                 o_g = take(MB_SEQ * Fl * 4), o_u = take(MB_SEQ * Fl * 4), o_h = take(MB_SEQ * Fl * 4),
+                 o_log = c->tp > 1 ? 0 : take(MB_SEQ * V * 4);
     const size_t o_pl = take(2 * MB_SEQ * KPmax * 2), o_xs = take(MB_SEQ * 4);
     const size_t o_ws = take((size_t)GM_MAX_WAVES * sms * 128 * 128 * 4), o_cnt = take(GM_MAX_CNT * 4);
-    const size_t seq_stride = L * c->kv_ctx * (size_t)c->kv_dim;
+    const size_t seq_stride = L * c->kv_ctx * (size_t)c->kv_l;
     const size_t o_kc = take((size_t)max_seqs * seq_stride * 4 + 4), o_vc = take((size_t)max_seqs * seq_stride * 4 + 4);
     void* mem = nullptr;
     CK(cudaMalloc(&mem, off));
@@ -1698,9 +1750,11 @@ static talos_status batch_alloc(talos_ctx* c, int max_seqs) {
     c->bmem = mem;
     c->bbytes = off;
     c->bp = (BatchParams*)(b + o_bp);
+    c->blar = (unsigned long long*)(b + o_lar);
     c->bx = (float*)(b + o_x), c->bq = (float*)(b + o_q);
     c->batt = (float*)(b + o_att), c->bg = (float*)(b + o_g), c->bu = (float*)(b + o_u), c->bh = (float*)(b + o_h);
     c->blog = (float*)(b + o_log);
+    if (c->tp > 1) TRY(batch_alloc_shared(c));
     c->bplanes = b + o_pl, c->bxs = (float*)(b + o_xs), c->bldp = (int)KPmax;
     c->bws = (float*)(b + o_ws), c->bcnt = (unsigned*)(b + o_cnt);
     c->bkc = (float*)(b + o_kc), c->bvc = (float*)(b + o_vc);
@@ -1721,7 +1775,6 @@ extern "C" talos_status talos_ctx_set_batch(talos_ctx* c, int max_seqs) {
     if (!c) return set_err(TALOS_ERR_INVALID_ARG, "NULL ctx");
     if (max_seqs < 0 || max_seqs > TALOS_MAX_BATCH)
         return set_err(TALOS_ERR_INVALID_ARG, "batch of %d sequences (at most %d)", max_seqs, TALOS_MAX_BATCH);
-    if (c->tp > 1) return set_err(TALOS_ERR_UNSUPPORTED, "batched decode under tensor parallelism");
     CK(cudaSetDevice(c->device));
     if (max_seqs == 0) return batch_free(c);
     return batch_alloc(c, max_seqs);
@@ -1771,7 +1824,8 @@ static int gm_split(int nrt, int R, int sms) {
 
 // One GEMM of the batched step: format its input unless the previous GEMM read
 // the same one, then every segment's rows for every live column.
-static talos_status gm(talos_ctx* c, GmInput& fi, GemmArgs a, const float* in, const float* norm, int ntc) {
+static talos_status gm(talos_ctx* c, GmInput& fi, GemmArgs a, const float* in, const float* norm, int ntc,
+                       int* grid_out = nullptr) {
     const int type = a.seg[0].A.type, nt = nt_of(ntc);
     const int K = a.K, KP = (K + 127) / 128 * 128;
     cudaError_t e = cudaSuccess;
@@ -1791,82 +1845,132 @@ static talos_status gm(talos_ctx* c, GmInput& fi, GemmArgs a, const float* in, c
     a.ws = c->bws;
     a.cnt = c->bcnt;
     const int units = a.nrt * a.S;  // one token tile: a step holds at most nt columns
-    e = launch_gemm(c->bmaps[ntc], a, type, nt, std::min(units, sms), c->stream);
+    const int grid = std::min(units, sms);
+    e = launch_gemm(c->bmaps[ntc], a, type, nt, grid, c->stream);
     if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "GEMM launch: %s", cudaGetErrorString(e));
+    if (grid_out) *grid_out = grid;
+    return TALOS_OK;
+}
+
+// Tensor parallel: a GEMM segment whose rows go to every rank (EPI_B_PEER) at
+// offset `off` floats of each rank's shared area with row stride ldy; the
+// GEMM's CTAs count their exits in blar.
+static void peer_out(talos_ctx* c, GemmArgs& a, size_t off) {
+    for (int r = 0; r < c->tp; ++r) a.peer[r] = (float*)((uint8_t*)c->bsh_peer[r]) + off;
+    a.npeer = c->tp;
+    a.lar = c->blar;
+}
+
+// Tensor parallel: the join after an EPI_B_PEER GEMM of `grid` CTAs (instance
+// `inst` of the step); with sum, this rank's receive slots `buf` are added to bx.
+static talos_status tp_join(talos_ctx* c, int inst, int grid, bool sum, int buf) {
+    TpJoin j{};
+    j.lar = c->blar;
+    j.lar_target = (unsigned)grid;
+    j.rarr = (unsigned long long*)c->bsh;
+    j.abort = (unsigned*)((uint8_t*)c->bsh + c->bsh_o_abort);
+    for (int r = 0; r < c->tp; ++r) {
+        j.prarr[r] = (unsigned long long*)c->bsh_peer[r];
+        j.pabort[r] = (unsigned*)((uint8_t*)c->bsh_peer[r] + c->bsh_o_abort);
+    }
+    j.inst = inst;
+    j.tp = c->tp;
+    j.rx = sum ? (const float*)((uint8_t*)c->bsh + c->bsh_o_rx) + (size_t)buf * c->tp * MB_SEQ * c->cfg.n_embd
+               : nullptr;
+    j.x = c->bx;
+    j.E = (int)c->cfg.n_embd;
+    cudaError_t e = launch_tp_join_b(j, c->bp, sm_count(c), c->stream);
+    if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "tensor-parallel join: %s", cudaGetErrorString(e));
     return TALOS_OK;
 }
 
 static talos_status enqueue_batch(talos_ctx* c, int mode, int ntc) {
     const talos_cfg& cfg = c->cfg;
-    const int E = (int)cfg.n_embd, F = (int)cfg.n_ff, V = (int)cfg.vocab_size;
+    const int E = (int)cfg.n_embd, Fl = c->ff_l, V = (int)cfg.vocab_size, Q = c->q_rows;
+    const bool tp = c->tp > 1;
+    // tensor parallel: receive slot buf of this rank, in floats from a shared area's base
+    const size_t slot = (size_t)MB_SEQ * E;
+    auto rx_off = [&](int buf) { return c->bsh_o_rx / 4 + ((size_t)buf * c->tp + c->rank) * slot; };
     const DevTensor& embd = c->w["token_embd.weight"];
     cudaError_t e = launch_embed_b((const uint8_t*)embd.mem, embd.type, E, V, c->bp, c->bx, E, c->stream);
     if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched embed: %s", cudaGetErrorString(e));
     GmInput fi;
     const bool slots = mode == BM_DECODE;
-    const size_t kv_layer = c->kv_ctx * (size_t)c->kv_dim;
+    const size_t kv_layer = c->kv_ctx * (size_t)c->kv_l;
     const size_t seq_stride = slots ? c->bseq_stride : 0;
     for (uint32_t l = 0; l < cfg.n_layer; ++l) {
         const LayerW& L = c->layers[l];
         float* kc = (slots ? c->bkc : (float*)c->kcache) + l * kv_layer;
         float* vc = (slots ? c->bvc : (float*)c->vcache) + l * kv_layer;
         // rmsnorm + q/k/v + RoPE + KV append (llama.rs:118-130): one GEMM when
-        // the three share a type
+        // the three share a type; under tensor parallelism this rank's heads
         {
             const DevTensor* w3[3] = {L.q, L.k, L.v};
             const int epi3[3] = {EPI_B_ROPE, EPI_B_KCACHE, EPI_B_VCACHE};
-            const int rows3[3] = {c->q_rows, c->kv_dim, c->kv_dim};
+            const int rows3[3] = {Q, c->kv_l, c->kv_l};
             for (int i = 0; i < 3;) {
                 GemmArgs a{};
                 a.K = E;
                 a.rope_cs = c->rope_cs;
                 a.hd = c->hd;
-                a.kv_dim = c->kv_dim;
+                a.kv_dim = c->kv_l;
                 a.kc = kc;
                 a.vc = vc;
                 a.seq_stride = seq_stride;
                 do {
-                    a.seg[a.nseg++] = gseg(w3[i], c->bq, c->q_rows, rows3[i], epi3[i]);
+                    a.seg[a.nseg++] = gseg(w3[i], c->bq, Q, rows3[i], epi3[i]);
                     ++i;
                 } while (i < 3 && a.seg[0].A.type == w3[i]->type);
                 TRY(gm(c, fi, a, c->bx, (const float*)L.attn_norm->mem, ntc));
             }
         }
-        // attention (llama.rs:135-155), o-proj + residual (:157-161)
-        e = launch_attention_b(c->bq, c->q_rows, kc, vc, seq_stride, c->kv_dim, (int)cfg.n_head,
-                               (int)cfg.n_head_kv, c->hd, c->batt, E, c->bp, c->stream);
+        // attention (llama.rs:135-155), o-proj + residual (:157-161); under
+        // tensor parallelism the o-proj is row-parallel: partial rows to every
+        // rank, summed into the residual by the join
+        e = launch_attention_b(c->bq, Q, kc, vc, seq_stride, c->kv_l, c->nh_l, c->nkv_l, c->hd, c->batt, Q, c->bp,
+                               c->stream);
         if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched attention: %s", cudaGetErrorString(e));
         {
             GemmArgs a{};
-            a.K = E;
-            a.seg[a.nseg++] = gseg(L.o, c->bx, E, E, EPI_B_ADD);
-            TRY(gm(c, fi, a, c->batt, nullptr, ntc));
+            a.K = Q;
+            int grid = 0;
+            a.seg[a.nseg++] = gseg(L.o, c->bx, E, E, tp ? EPI_B_PEER : EPI_B_ADD);
+            if (tp) peer_out(c, a, rx_off(0));
+            TRY(gm(c, fi, a, c->batt, nullptr, ntc, &grid));
+            if (tp) TRY(tp_join(c, 2 * (int)l, grid, true, 0));
         }
         // rmsnorm + SwiGLU FFN (gate and up in one GEMM launch; they share a
         // type, bind_layers) + residual (:163-176)
         {
             GemmArgs a{};
             a.K = E;
-            a.seg[a.nseg++] = gseg(L.gate, c->bg, F, F, EPI_B_STORE);
-            a.seg[a.nseg++] = gseg(L.up, c->bu, F, F, EPI_B_STORE);
+            a.seg[a.nseg++] = gseg(L.gate, c->bg, Fl, Fl, EPI_B_STORE);
+            a.seg[a.nseg++] = gseg(L.up, c->bu, Fl, Fl, EPI_B_STORE);
             TRY(gm(c, fi, a, c->bx, (const float*)L.ffn_norm->mem, ntc));
-            e = launch_swiglu_b(c->bg, c->bu, c->bh, F, F, c->bp, c->stream);
+            e = launch_swiglu_b(c->bg, c->bu, c->bh, Fl, Fl, c->bp, c->stream);
             if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched SwiGLU: %s", cudaGetErrorString(e));
         }
         {
             GemmArgs a{};
-            a.K = F;
-            a.seg[a.nseg++] = gseg(L.down, c->bx, E, E, EPI_B_ADD);
-            TRY(gm(c, fi, a, c->bh, nullptr, ntc));
+            a.K = Fl;
+            int grid = 0;
+            a.seg[a.nseg++] = gseg(L.down, c->bx, E, E, tp ? EPI_B_PEER : EPI_B_ADD);
+            if (tp) peer_out(c, a, rx_off(1));
+            TRY(gm(c, fi, a, c->bh, nullptr, ntc, &grid));
+            if (tp) TRY(tp_join(c, 2 * (int)l + 1, grid, true, 1));
         }
         fi = GmInput{};  // bx changed in place
     }
-    if (mode == BM_PREFILL) return TALOS_OK;  // the last column's logits: batch_last_logits
-    // final norm + logits (:89, :181)
+    if (mode == BM_PREFILL) return TALOS_OK;  // the last column's logits: row_logits
+    // final norm + logits (:89, :181); under tensor parallelism each rank's
+    // vocabulary range goes to every rank's gathered logits
     GemmArgs a{};
     a.K = E;
-    a.seg[a.nseg++] = gseg(&c->w["output.weight"], c->blog, V, V, EPI_B_STORE);
-    TRY(gm(c, fi, a, c->bx, (const float*)c->w["output_norm.weight"].mem, ntc));
+    int grid = 0;
+    a.seg[a.nseg++] = gseg(&c->w["output.weight"], c->blog, V, c->v_l, tp ? EPI_B_PEER : EPI_B_STORE);
+    if (tp) peer_out(c, a, c->bsh_o_log / 4 + (size_t)c->v_off);
+    TRY(gm(c, fi, a, c->bx, (const float*)c->w["output_norm.weight"].mem, ntc, &grid));
+    if (tp) TRY(tp_join(c, 2 * (int)cfg.n_layer, grid, false, 0));
     return TALOS_OK;
 }
 
@@ -1919,9 +2023,11 @@ static talos_status batch_step(talos_ctx* c, int mode, const uint32_t* tokens, c
         v.token[i] = tokens[i];
         v.pos[i] = (uint32_t)pos[i];
     }
+    v.tpstep = c->btpstep;
     k_set_batch<<<1, 1, 0, c->stream>>>(c->bp, v, !first);
     CK(cudaGetLastError());
     CK(cudaGraphLaunch(c->bgraph[mode][ntc], c->stream));
+    if (c->tp > 1) ++c->btpstep;
     return TALOS_OK;
 }
 
@@ -1952,10 +2058,12 @@ extern "C" talos_status talos_forward_batch(talos_ctx* c, const uint32_t* tokens
 }
 
 // Whether the batched steps can run consecutive positions of the main cache
-// (one GPU, f32 cache, Q4_0 / Q8_0 / Q6_K matrices); if so their buffers exist.
+// (f32 cache, Q4_0 / Q8_0 / Q6_K matrices); if so their buffers exist. The
+// decision depends only on the model and settings every rank shares, so under
+// tensor parallelism all ranks take the same path.
 static talos_status chunked_ready(talos_ctx* c, bool* ok) {
     *ok = false;
-    if (c->tp > 1 || c->kv_f16) return TALOS_OK;
+    if (c->kv_f16) return TALOS_OK;
     TRY(bind_if_dirty(c));
     if (batch_check(c) != TALOS_OK) return TALOS_OK;
     if (!c->bmem) TRY(batch_alloc(c, 0));
@@ -1980,7 +2088,9 @@ static talos_status row_logits(talos_ctx* c, const float* x) {
 
 // talos_prefill in steps of up to MB_SEQ consecutive prompt positions: one
 // weight pass per step instead of one per token. Taken when the batched step
-// runs the model and the main cache is f32 on one GPU; false in *taken otherwise.
+// runs the model and the main cache is f32; false in *taken otherwise. The last
+// position's logits: final norm + output matvec of its row on one GPU; under
+// tensor parallelism the last step computes its columns' gathered logits.
 static talos_status prefill_chunked(talos_ctx* c, const uint32_t* tokens, size_t n, size_t pos0, float* last_logits,
                                     bool* taken) {
     *taken = false;
@@ -1989,15 +2099,19 @@ static talos_status prefill_chunked(talos_ctx* c, const uint32_t* tokens, size_t
     if (!*taken) return TALOS_OK;
     int last_n = 1;
     std::vector<size_t> pos(MB_SEQ);
+    const size_t V = c->cfg.vocab_size;
     for (size_t i = 0; i < n; i += MB_SEQ) {
         const int k = (int)std::min<size_t>(MB_SEQ, n - i);
         for (int j = 0; j < k; ++j) pos[j] = pos0 + i + j;
-        TRY(batch_step(c, BM_PREFILL, tokens + i, pos.data(), k, i == 0));
+        const bool score = c->tp > 1 && last_logits && i + k == n;
+        TRY(batch_step(c, score ? BM_SCORE : BM_PREFILL, tokens + i, pos.data(), k, i == 0));
         last_n = k;
     }
-    if (last_logits) {
+    if (last_logits && c->tp > 1) {
+        CK(cudaMemcpyAsync(c->h_out, c->blog + (size_t)(last_n - 1) * V, V * 4, cudaMemcpyDeviceToHost, c->stream));
+    } else if (last_logits) {
         TRY(row_logits(c, c->bx + (size_t)(last_n - 1) * c->cfg.n_embd));
-        CK(cudaMemcpyAsync(c->h_out, c->logits, c->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, c->stream));
+        CK(cudaMemcpyAsync(c->h_out, c->logits, V * 4, cudaMemcpyDeviceToHost, c->stream));
     }
     TRY(batch_finish(c, 0, nullptr));
     if (last_logits) memcpy(last_logits, c->h_out, c->cfg.vocab_size * 4);
@@ -2132,6 +2246,18 @@ extern "C" talos_status talos_nccl_unique_id(uint8_t out[128]) {
 extern "C" talos_status talos_ctx_create_tp(const talos_cfg* cfg, int device, int tp_size, int tp_rank,
                                             const uint8_t* id, talos_ctx** out) {
     return ctx_create(cfg, device, tp_size, tp_rank, id, out);
+}
+
+extern "C" talos_status talos_ctx_tp_resync(talos_ctx* c) {
+    if (!c) return set_err(TALOS_ERR_INVALID_ARG, "NULL ctx");
+    CK(cudaSetDevice(c->device));
+    CK(cudaStreamSynchronize(c->stream));
+    reset_sync(c);  // the per-token kernel's counters and launch epoch
+    if (c->bsh) CK(cudaMemsetAsync(c->bsh, 0, c->bsh_sync_bytes, c->stream));  // arrivals, abort word
+    if (c->blar) CK(cudaMemsetAsync(c->blar, 0, 8, c->stream));
+    c->btpstep = 0;
+    CK(cudaStreamSynchronize(c->stream));
+    return TALOS_OK;
 }
 
 // ------------------------------------------------------------------ kernels as calls

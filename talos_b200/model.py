@@ -170,8 +170,9 @@ class Context:
         return "f16" if k.value == _lib.KV_F16 else "f32"
 
     def set_batch(self, max_seqs: int):
-        """Reserve KV cache slots for up to ``max_seqs`` (<= 4) sequences decoded
-        together by ``forward_batch`` (0 frees them)."""
+        """Reserve KV cache slots for up to ``max_seqs`` (<= TALOS_MAX_BATCH, 64)
+        sequences decoded together by ``forward_batch`` (0 frees them). Under
+        tensor parallelism every rank calls it with the same value."""
         _lib.check(_lib.load().talos_ctx_set_batch(self.h, int(max_seqs)))
 
     def forward_batch(self, tokens, positions) -> np.ndarray:
@@ -224,6 +225,11 @@ class Context:
 
     def reset(self):
         _lib.check(_lib.load().talos_kv_reset(self.h))
+
+    def tp_resync(self):
+        """talos_ctx_tp_resync: after any rank's step failed, every rank calls this
+        while no rank has a step in flight; the next step starts afresh."""
+        _lib.check(_lib.load().talos_ctx_tp_resync(self.h))
 
     def perplexity(self, tokens) -> tuple[float, float, int]:
         """talos_perplexity: (perplexity, NLL sum, scored positions)."""
