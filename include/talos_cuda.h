@@ -242,6 +242,28 @@ talos_status talos_forward_batch(talos_ctx* ctx, const uint32_t* tokens, const s
                                  float* logits_out);
 
 /*
+ * The prompt of one sequence of the batch: feeds tokens[0..n) at positions
+ * pos0 .. pos0+n-1 into cache slot `slot` (< max_seqs of talos_ctx_set_batch),
+ * up to 128 positions per weight pass on the tensor cores, each position
+ * attending to the ones before it (the prefill loop of src/main.rs:88-95 for
+ * one of the multi-prompt workload's sequences); the logits after the last one
+ * go to `last_logits` (host, may be NULL). Other slots are untouched.
+ */
+talos_status talos_prefill_slot(talos_ctx* ctx, int slot, const uint32_t* tokens, size_t n, size_t pos0,
+                                float* last_logits);
+
+/*
+ * Batched greedy decode on the GPU: sequence i (slot i, i < n) feeds tokens[i]
+ * at pos[i], then the argmax of its logits at pos[i]+1, ... for `steps` steps;
+ * the chosen tokens go to tokens_out[k * n + i] (host, step k). The argmax is
+ * sample::argmax (src/sample.rs:7-14: total order, last maximal index), taken
+ * per sequence on the device, so no logits leave the GPU: talos_generate_greedy
+ * for a batch, i.e. the decode loops of src/main.rs:97-113 run together.
+ */
+talos_status talos_generate_batch_greedy(talos_ctx* ctx, const uint32_t* tokens, const size_t* pos, int n,
+                                         size_t steps, uint32_t* tokens_out);
+
+/*
  * Teacher-forced perplexity of tokens[0..n) (n >= 2): eval::perplexity
  * (src/eval.rs:35-52). The tokens are scored in chunks of the context length,
  * each from an empty KV cache; at each position the negative log-likelihood of

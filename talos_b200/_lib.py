@@ -46,6 +46,9 @@ SIGNATURES = {
     "talos_ctx_set_kv_dtype": (_i, [_vp, _i]),
     "talos_ctx_set_batch": (_i, [_vp, _i]),
     "talos_forward_batch": (_i, [_vp, C.POINTER(C.c_uint32), C.POINTER(_sz), _i, C.POINTER(C.c_float)]),
+    "talos_prefill_slot": (_i, [_vp, _i, C.POINTER(C.c_uint32), _sz, _sz, C.POINTER(C.c_float)]),
+    "talos_generate_batch_greedy": (_i, [_vp, C.POINTER(C.c_uint32), C.POINTER(_sz), _i, _sz,
+                                         C.POINTER(C.c_uint32)]),
     "talos_ctx_kv_dtype": (_i, [_vp, C.POINTER(_i)]),
     "talos_ctx_device_bytes": (_i, [_vp, C.POINTER(_sz)]),
     "talos_ctx_stream": (_i, [_vp, C.POINTER(_vp)]),

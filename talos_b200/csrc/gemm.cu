@@ -62,7 +62,10 @@ namespace talos {
 constexpr int GM_BM = 128;   // weight rows per tile = TMEM lanes
 constexpr int GM_BK = 64;    // K per A/B stage
 constexpr int GM_RK = 128;   // K per raw weight slot (two stages)
-constexpr int GM_NDQ = 8;    // dequantizer warps
+#ifndef TALOS_GM_NDQ
+#define TALOS_GM_NDQ 8
+#endif
+constexpr int GM_NDQ = TALOS_GM_NDQ;  // dequantizer warps (8 or 16: each takes 16 / GM_NDQ row groups per stage)
 constexpr int GM_WP = 4, GM_XP = 5, GM_MMA = 6, GM_DQ0 = 7;
 constexpr int GM_THREADS = (GM_DQ0 + GM_NDQ) * 32;
 constexpr int GM_SMEM = 220 * 1024;
@@ -109,7 +112,7 @@ struct GmCfg {
     static constexpr int A_BYTES = 2 * GM_BM * GM_BK * 2;  // A_hi + A_lo
     static constexpr int B_BYTES = 2 * NT * GM_BK * 2;     // [x_hi; x_lo]
     static constexpr int BAR_BYTES = 1024;
-    static constexpr int EPI_BYTES = 4 * NT * 8;  // the epilogue warps' column scales and positions
+    static constexpr int EPI_BYTES = 4 * NT * 12;  // the epilogue warps' column scales, positions, slots
     static constexpr int fixed(int ns) { return ns * (A_BYTES + B_BYTES) + BAR_BYTES + EPI_BYTES; }
     static constexpr int NS = fixed(4) + 2 * RAW <= GM_SMEM ? 4 : (fixed(3) + 2 * RAW <= GM_SMEM ? 3 : 2);
     static constexpr int FIXED = fixed(NS);
@@ -318,12 +321,12 @@ __device__ __forceinline__ void gm_dequant_q6(const uint8_t* lrec, const uint8_t
 
 // The epilogue of W consecutive token columns t0 .. t0+W-1 of tile row r:
 // v[j] are the raw sums, xs[j] the column scales (2^e_t * 2^-eA, 0 past the
-// live columns), ps[j] the columns' positions. Every global load of the W
+// live columns), ps[j] the columns' positions, sl[j] their cache slots. Every global load of the W
 // columns is issued before any is used (one memory round trip per W columns,
 // not one per column). Called by all 32 lanes of an epilogue warp (shuffles).
 template <int W>
 __device__ __forceinline__ void gm_epi(const GemmArgs& a, const GemmSeg& sg, int lt, int r, int t0, int ntok,
-                                       float* v, const float* xs, const uint32_t* ps) {
+                                       float* v, const float* xs, const uint32_t* ps, const uint32_t* sl) {
 #pragma unroll
     for (int j = 0; j < W; ++j) v[j] *= xs[j];
     const int row = lt * GM_BM + r;
@@ -349,7 +352,7 @@ __device__ __forceinline__ void gm_epi(const GemmArgs& a, const GemmSeg& sg, int
                 o = (row & 1) ? __fadd_rn(__fmul_rn(pv[j], cs[j].y), __fmul_rn(v[j], cs[j].x))
                               : __fsub_rn(__fmul_rn(v[j], cs[j].x), __fmul_rn(pv[j], cs[j].y));
             float* dst = sg.epi == EPI_B_ROPE ? sg.y + (size_t)t * sg.ldy
-                                              : (sg.epi == EPI_B_KCACHE ? a.kc : a.vc) + (size_t)t * a.seq_stride +
+                                              : (sg.epi == EPI_B_KCACHE ? a.kc : a.vc) + (size_t)sl[j] * a.seq_stride +
                                                     (size_t)ps[j] * a.kv_dim;
             dst[row] = o;
         }
@@ -402,6 +405,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     int* s_flag = (int*)(tmem_slot + 1);     // [0]: some role gave up on a wait
     float* ep_xs = (float*)(sR + C::NRAW * C::RAW + C::BAR_BYTES);  // [4 warps][NT] column scales
     uint32_t* ep_pos = (uint32_t*)(ep_xs + 4 * NT);                   // [4 warps][NT] column positions
+    uint32_t* ep_slot = ep_pos + 4 * NT;                              // [4 warps][NT] column cache slots
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     const int ntok = a.bp->n;
@@ -565,7 +569,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         }
         __syncwarp();
     } else if (warp >= GM_DQ0) {
-        // ---------------- dequantizers: warp dw takes row groups dw and dw + 8
+        // ---------------- dequantizers: warp dw takes row groups dw, dw + GM_NDQ, ...
         const int dw = warp - GM_DQ0;
         uint32_t ri = 0, si = 0;
         int cur_si = -1;
@@ -595,8 +599,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                     uint8_t* Ahi = sA + s * C::A_BYTES;
                     uint8_t* Alo = Ahi + GM_BM * GM_BK * 2;
 #pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        const int gi = dw + 8 * j;
+                    for (int j = 0; j < 16 / GM_NDQ; ++j) {
+                        const int gi = dw + GM_NDQ * j;
                         const uint8_t* lrec = raw + gi * GmFmt<TYPE>::LREC;
                         const uint8_t* scs = raw + 16 * GmFmt<TYPE>::LREC + gi * GmFmt<TYPE>::SC;
                         if (TYPE == GT_Q6_K)
@@ -623,6 +627,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         const int q = warp, r = q * 32 + lane;
         float* exs = ep_xs + q * NT;
         uint32_t* eps = ep_pos + q * NT;
+        uint32_t* esl = ep_slot + q * NT;
         uint32_t nu = 0;
         for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++nu) {
             const GmUnit U = gm_unit(a, u, ntt);
@@ -636,6 +641,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                     const int t = t0 + j;
                     exs[j] = t < ntok ? a.xs[t] * wsc : 0.f;
                     eps[j] = t < ntok ? a.bp->pos[t] : 0u;
+                    esl[j] = t < ntok ? a.bp->slot[t] : 0u;
                 }
                 __syncwarp();
             }
@@ -658,8 +664,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 16; ++j) part[(size_t)(c + j) * GM_BM + r] = vh[j];
                 } else {
-                    gm_epi<8>(a, sg, U.lt, r, t0 + c, ntok, vh, exs + c, eps + c);
-                    gm_epi<8>(a, sg, U.lt, r, t0 + c + 8, ntok, vh + 8, exs + c + 8, eps + c + 8);
+                    gm_epi<8>(a, sg, U.lt, r, t0 + c, ntok, vh, exs + c, eps + c, esl + c);
+                    gm_epi<8>(a, sg, U.lt, r, t0 + c + 8, ntok, vh + 8, exs + c + 8, eps + c + 8, esl + c + 8);
                 }
             }
             tc_fence_before();
@@ -692,7 +698,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 8; ++j) v[j] += w[j];
                 }
-                gm_epi<8>(a, sg, U.lt, r, t0 + c, ntok, v, exs + c, eps + c);
+                gm_epi<8>(a, sg, U.lt, r, t0 + c, ntok, v, exs + c, eps + c, esl + c);
             }
         }
     }

@@ -457,8 +457,9 @@ __global__ void __launch_bounds__(ATB_WARPS * 32) k_attention_b(const float* q, 
     const bool act = 4 * lane < hd;
     float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
     if (act) q4 = *(const float4*)(q + (size_t)s * ldq + (size_t)h * hd + 4 * lane);
-    const float* K0 = kc + (size_t)s * seq_stride + (size_t)kh * hd + 4 * lane;
-    const float* V0 = vc + (size_t)s * seq_stride + (size_t)kh * hd + 4 * lane;
+    const size_t so = (size_t)bp->slot[s] * seq_stride;
+    const float* K0 = kc + so + (size_t)kh * hd + 4 * lane;
+    const float* V0 = vc + so + (size_t)kh * hd + 4 * lane;
     float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
     for (int t0 = warp; t0 < seq; t0 += ATB_WARPS * ATB_ROUND) {
         float4 kv[ATB_ROUND], vv[ATB_ROUND];
@@ -529,6 +530,45 @@ __global__ void k_swiglu_b(const float* g, const float* u, float* h, int ld, int
         const size_t o = (size_t)s * ld + i;
         h[o] = __fmul_rn(silu_ref(g[o]), u[o]);
     }
+}
+
+// One CTA per column: its logits row's sample::argmax key (argmax_key: total
+// order, the larger index on ties), reduced warp by warp then across warps.
+__global__ void __launch_bounds__(1024) k_greedy_advance_b(const float* logits, int V, BatchParams* bp,
+                                                           uint32_t* gen, int cap) {
+    __shared__ unsigned long long wk[32];
+    const int s = blockIdx.x;
+    if (s >= bp->n) return;
+    const float* row = logits + (size_t)s * V;
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const unsigned long long k = argmax_key(row[i], (uint32_t)i);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long oth = __shfl_xor_sync(0xffffffffu, best, o);
+        best = oth > best ? oth : best;
+    }
+    if ((threadIdx.x & 31) == 0) wk[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = wk[w] > best ? wk[w] : best;
+        best = wk[0] > best ? wk[0] : best;
+        const uint32_t tok = (uint32_t)(best & 0xffffffffull);
+        const uint32_t n = bp->ngen[s];
+        if (n < (uint32_t)cap) gen[(size_t)s * cap + n] = tok;
+        bp->ngen[s] = n + 1;
+        bp->token[s] = tok;
+        bp->pos[s] += 1;
+        if (s == 0) bp->tpstep += 1;  // read only by the next step's kernels
+    }
+}
+
+cudaError_t launch_greedy_advance_b(const float* logits, int V, BatchParams* bp, uint32_t* gen, int cap,
+                                    cudaStream_t s) {
+    k_greedy_advance_b<<<MB_SEQ, 1024, 0, s>>>(logits, V, bp, gen, cap);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_swiglu_b(const float* g, const float* u, float* h, int ld, int n_ff, const BatchParams* bp,

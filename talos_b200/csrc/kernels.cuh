@@ -88,6 +88,8 @@ struct BatchParams {
     int n;                     // active token columns (1 .. MB_SEQ)
     uint32_t token[MB_SEQ];
     uint32_t pos[MB_SEQ];
+    uint32_t slot[MB_SEQ];     // cache slot of each column (steps on the sequences' slots)
+    uint32_t ngen[MB_SEQ];     // batched greedy: tokens chosen so far per column
     uint32_t error;            // device-side error bits (1: token out of range, 2: a bounded wait expired)
     uint32_t tpstep;           // tensor parallel: earlier batched steps of the context (k_tp_join_b targets)
 };
@@ -174,6 +176,11 @@ cudaError_t launch_tp_join_b(const TpJoin& j, BatchParams* bp, int grid, cudaStr
 cudaError_t launch_embed_b(const uint8_t* embd_raw, int type, int cols, int vocab, const BatchParams* bp, float* x,
                            int ldx, cudaStream_t s);
 // h[s][i] = silu(g[s][i]) * u[s][i] for the live columns (src/math/ops.rs:28-37)
+// Batched greedy: per live column s, the argmax of its logits row (total order,
+// last maximal index: sample::argmax) becomes its next token at pos + 1 and is
+// appended to gen[s * cap + ngen[s]]; then tpstep advances by one.
+cudaError_t launch_greedy_advance_b(const float* logits, int V, BatchParams* bp, uint32_t* gen, int cap,
+                                    cudaStream_t s);
 cudaError_t launch_swiglu_b(const float* g, const float* u, float* h, int ld, int n_ff, const BatchParams* bp,
                             cudaStream_t s);
 // GQA attention per (head, sequence) over positions 0 .. pos[s] (src/model/llama.rs:135-155)

@@ -465,7 +465,9 @@ struct talos_ctx {
     size_t bseq_stride = 0;                // floats per sequence in bkc / bvc
     float* h_blog = nullptr;               // pinned [TALOS_MAX_BATCH][V]
     alignas(64) uint8_t bmaps[3][128];     // tensor maps of bplanes for 32 / 64 / 128-column tiles
-    cudaGraphExec_t bgraph[3][3] = {};     // [BatchMode][token-tile size]
+    cudaGraphExec_t bgraph[5][3] = {};     // [BatchMode][token-tile size]
+    uint32_t* bgen = nullptr;              // batched greedy: [MB_SEQ][kv_ctx] chosen tokens
+    int bgen_cap = 0;
     // tensor parallel: the batched steps' IPC-exported area {arrival counters
     // [2 n_layer + 1], abort word, receive slots [2][tp][MB_SEQ][E], gathered
     // logits [MB_SEQ][V]}, every rank's mapping of it, and the local count of
@@ -1665,14 +1667,20 @@ static talos_status profile_fused(talos_ctx* c, double* kernel_ms, uint32_t* lau
 //    cache slot and position, and their logits;
 //  * BM_PREFILL (talos_prefill): consecutive prompt positions of the one
 //    sequence of the main cache (src/main.rs:88-95), no logits;
-//  * BM_SCORE (talos_perplexity): the same with every column's logits.
+//  * BM_SCORE (talos_perplexity): the same with every column's logits;
+//  * BM_FILL (talos_prefill_slot): consecutive prompt positions of one
+//    sequence of the batch, into its cache slot, no logits;
+//  * BM_GREEDY (talos_generate_batch_greedy): BM_DECODE, then each column's
+//    argmax becomes its next token on the device (replayed step after step).
 // The step is the layered sequence of src/model/llama.rs:96-183 per column:
 // embedding row; per layer GEMM q/k/v (RoPE, cache append), attention, GEMM
 // o-proj (+ residual), GEMM gate/up (SwiGLU), GEMM down (+ residual); then the
 // final norm and the output GEMM. A column at position p attends to positions
 // 0 .. p of its cache, so prompt positions of one step see each other's rows.
 
-enum BatchMode { BM_DECODE = 0, BM_PREFILL = 1, BM_SCORE = 2 };
+enum BatchMode { BM_DECODE = 0, BM_PREFILL = 1, BM_SCORE = 2, BM_FILL = 3, BM_GREEDY = 4 };
+static bool mode_slots(int mode) { return mode == BM_DECODE || mode == BM_FILL || mode == BM_GREEDY; }
+static bool mode_logits(int mode) { return mode != BM_PREFILL && mode != BM_FILL; }
 static int nt_of(int ntc) { return 32 << ntc; }
 static int ntc_for(int n) { return n <= 32 ? 0 : (n <= 64 ? 1 : 2); }
 constexpr int GM_MAX_WAVES = 5;   // split-K never makes more than 5 units per SM
@@ -1743,6 +1751,8 @@ static talos_status batch_alloc(talos_ctx* c, int max_seqs) {
     const size_t o_ws = take((size_t)GM_MAX_WAVES * sms * 128 * 128 * 4), o_cnt = take(GM_MAX_CNT * 4);
     const size_t seq_stride = L * c->kv_ctx * (size_t)c->kv_l;
     const size_t o_kc = take((size_t)max_seqs * seq_stride * 4 + 4), o_vc = take((size_t)max_seqs * seq_stride * 4 + 4);
+    const int gen_cap = max_seqs ? (int)c->kv_ctx : 0;
+    const size_t o_gen = take((size_t)MB_SEQ * gen_cap * 4 + 4);
     void* mem = nullptr;
     CK(cudaMalloc(&mem, off));
     CK(cudaMemsetAsync(mem, 0, off, c->stream));
@@ -1758,6 +1768,7 @@ static talos_status batch_alloc(talos_ctx* c, int max_seqs) {
     c->bplanes = b + o_pl, c->bxs = (float*)(b + o_xs), c->bldp = (int)KPmax;
     c->bws = (float*)(b + o_ws), c->bcnt = (unsigned*)(b + o_cnt);
     c->bkc = (float*)(b + o_kc), c->bvc = (float*)(b + o_vc);
+    c->bgen = (uint32_t*)(b + o_gen), c->bgen_cap = gen_cap;
     c->bseq_stride = seq_stride;
     if (gemm_map_bytes() > sizeof c->bmaps[0]) return set_err(TALOS_ERR_CUDA, "tensor map larger than its slot");
     for (int i = 0; i < 3; ++i) {
@@ -1895,7 +1906,7 @@ static talos_status enqueue_batch(talos_ctx* c, int mode, int ntc) {
     cudaError_t e = launch_embed_b((const uint8_t*)embd.mem, embd.type, E, V, c->bp, c->bx, E, c->stream);
     if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched embed: %s", cudaGetErrorString(e));
     GmInput fi;
-    const bool slots = mode == BM_DECODE;
+    const bool slots = mode_slots(mode);
     const size_t kv_layer = c->kv_ctx * (size_t)c->kv_l;
     const size_t seq_stride = slots ? c->bseq_stride : 0;
     for (uint32_t l = 0; l < cfg.n_layer; ++l) {
@@ -1961,7 +1972,13 @@ static talos_status enqueue_batch(talos_ctx* c, int mode, int ntc) {
         }
         fi = GmInput{};  // bx changed in place
     }
-    if (mode == BM_PREFILL) return TALOS_OK;  // the last column's logits: row_logits
+    if (!mode_logits(mode)) {
+        // prefill: the last column's logits come separately. Every step passes
+        // every join instance (their targets count steps), so under tensor
+        // parallelism the logits join still runs, without data.
+        if (tp) TRY(tp_join(c, 2 * (int)cfg.n_layer, 0, false, 0));
+        return TALOS_OK;
+    }
     // final norm + logits (:89, :181); under tensor parallelism each rank's
     // vocabulary range goes to every rank's gathered logits
     GemmArgs a{};
@@ -1971,6 +1988,10 @@ static talos_status enqueue_batch(talos_ctx* c, int mode, int ntc) {
     if (tp) peer_out(c, a, c->bsh_o_log / 4 + (size_t)c->v_off);
     TRY(gm(c, fi, a, c->bx, (const float*)c->w["output_norm.weight"].mem, ntc, &grid));
     if (tp) TRY(tp_join(c, 2 * (int)cfg.n_layer, grid, false, 0));
+    if (mode == BM_GREEDY) {
+        e = launch_greedy_advance_b(c->blog, V, c->bp, c->bgen, c->bgen_cap, c->stream);
+        if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "batched greedy: %s", cudaGetErrorString(e));
+    }
     return TALOS_OK;
 }
 
@@ -2010,22 +2031,32 @@ static talos_status batch_graph(talos_ctx* c, int mode, int ntc) {
     return TALOS_OK;
 }
 
-// One batched step of n columns: parameters set by a kernel (stream-ordered, so
-// the host never rewrites a buffer a pending copy reads), then the graph of the
-// smallest token tile that holds n.
-static talos_status batch_step(talos_ctx* c, int mode, const uint32_t* tokens, const size_t* pos, int n, bool first) {
-    if (n < 1 || n > MB_SEQ) return set_err(TALOS_ERR_INVALID_ARG, "%d columns in a batched step", n);
-    const int ntc = ntc_for(n);
-    TRY(batch_graph(c, mode, ntc));
+// The parameters of a batched step of n columns, set by a kernel
+// (stream-ordered, so the host never rewrites a buffer a pending copy reads).
+// slots: each column's cache slot (NULL: column i in slot i).
+static talos_status set_batch_params(talos_ctx* c, const uint32_t* tokens, const size_t* pos, const int* slots,
+                                     int n, bool first) {
     BatchParams v{};
     v.n = n;
     for (int i = 0; i < n; ++i) {
         v.token[i] = tokens[i];
         v.pos[i] = (uint32_t)pos[i];
+        v.slot[i] = slots ? (uint32_t)slots[i] : (uint32_t)i;
     }
     v.tpstep = c->btpstep;
     k_set_batch<<<1, 1, 0, c->stream>>>(c->bp, v, !first);
     CK(cudaGetLastError());
+    return TALOS_OK;
+}
+
+// One batched step of n columns: its parameters, then the graph of the
+// smallest token tile that holds n.
+static talos_status batch_step(talos_ctx* c, int mode, const uint32_t* tokens, const size_t* pos, const int* slots,
+                               int n, bool first) {
+    if (n < 1 || n > MB_SEQ) return set_err(TALOS_ERR_INVALID_ARG, "%d columns in a batched step", n);
+    const int ntc = ntc_for(n);
+    TRY(batch_graph(c, mode, ntc));
+    TRY(set_batch_params(c, tokens, pos, slots, n, first));
     CK(cudaGraphLaunch(c->bgraph[mode][ntc], c->stream));
     if (c->tp > 1) ++c->btpstep;
     return TALOS_OK;
@@ -2053,8 +2084,67 @@ extern "C" talos_status talos_forward_batch(talos_ctx* c, const uint32_t* tokens
     for (int i = 0; i < n; ++i) TRY(check_tok_pos(c, tokens[i], pos[i]));
     TRY(bind_if_dirty(c));
     TRY(batch_check(c));
-    TRY(batch_step(c, BM_DECODE, tokens, pos, n, true));
+    TRY(batch_step(c, BM_DECODE, tokens, pos, nullptr, n, true));
     return batch_finish(c, n, logits_out);
+}
+
+extern "C" talos_status talos_prefill_slot(talos_ctx* c, int slot, const uint32_t* tokens, size_t n, size_t pos0,
+                                           float* last_logits) {
+    if (!c || (!tokens && n)) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    if (slot < 0 || slot >= c->bmax)
+        return set_err(TALOS_ERR_INVALID_ARG, "slot %d (the context holds %d; talos_ctx_set_batch)", slot, c->bmax);
+    if (n == 0) return TALOS_OK;
+    CK(cudaSetDevice(c->device));
+    for (size_t i = 0; i < n; ++i) TRY(check_tok_pos(c, tokens[i], pos0 + i));
+    TRY(bind_if_dirty(c));
+    TRY(batch_check(c));
+    std::vector<size_t> pos(MB_SEQ);
+    const std::vector<int> slots(MB_SEQ, slot);
+    int last_n = 1;
+    for (size_t i = 0; i < n; i += MB_SEQ) {
+        const int k = (int)std::min<size_t>(MB_SEQ, n - i);
+        for (int j = 0; j < k; ++j) pos[j] = pos0 + i + j;
+        // the last step also computes its columns' logits when they are wanted
+        const int mode = last_logits && i + k == n ? BM_DECODE : BM_FILL;
+        TRY(batch_step(c, mode, tokens + i, pos.data(), slots.data(), k, i == 0));
+        last_n = k;
+    }
+    const size_t V = c->cfg.vocab_size;
+    if (last_logits)
+        CK(cudaMemcpyAsync(c->h_out, c->blog + (size_t)(last_n - 1) * V, V * 4, cudaMemcpyDeviceToHost, c->stream));
+    TRY(batch_finish(c, 0, nullptr));
+    if (last_logits) memcpy(last_logits, c->h_out, V * 4);
+    return TALOS_OK;
+}
+
+extern "C" talos_status talos_generate_batch_greedy(talos_ctx* c, const uint32_t* tokens, const size_t* pos, int n,
+                                                    size_t steps, uint32_t* tokens_out) {
+    if (!c || !tokens || !pos || (!tokens_out && steps)) return set_err(TALOS_ERR_INVALID_ARG, "NULL argument");
+    if (n < 1 || n > c->bmax)
+        return set_err(TALOS_ERR_INVALID_ARG, "%d sequences (the context holds %d; talos_ctx_set_batch)", n, c->bmax);
+    if (steps == 0) return TALOS_OK;
+    CK(cudaSetDevice(c->device));
+    for (int i = 0; i < n; ++i) {
+        TRY(check_tok_pos(c, tokens[i], pos[i]));
+        if (pos[i] + steps > c->kv_ctx)
+            return set_err(TALOS_ERR_INVALID_ARG, "sequence %d: positions %zu .. %zu beyond the context (%zu)", i,
+                           pos[i], pos[i] + steps - 1, c->kv_ctx);
+    }
+    TRY(bind_if_dirty(c));
+    TRY(batch_check(c));
+    const int ntc = ntc_for(n);
+    TRY(batch_graph(c, BM_GREEDY, ntc));
+    TRY(set_batch_params(c, tokens, pos, nullptr, n, true));
+    // the graph advances every column's token and position itself (and the
+    // tensor-parallel step count), so the replays need no host work
+    for (size_t k = 0; k < steps; ++k) CK(cudaGraphLaunch(c->bgraph[BM_GREEDY][ntc], c->stream));
+    if (c->tp > 1) c->btpstep += (uint32_t)steps;
+    TRY(batch_finish(c, 0, nullptr));
+    std::vector<uint32_t> g((size_t)n * c->bgen_cap);
+    CK(cudaMemcpy(g.data(), c->bgen, g.size() * 4, cudaMemcpyDeviceToHost));
+    for (size_t k = 0; k < steps; ++k)
+        for (int i = 0; i < n; ++i) tokens_out[k * n + i] = g[(size_t)i * c->bgen_cap + k];
+    return TALOS_OK;
 }
 
 // Whether the batched steps can run consecutive positions of the main cache
@@ -2099,12 +2189,13 @@ static talos_status prefill_chunked(talos_ctx* c, const uint32_t* tokens, size_t
     if (!*taken) return TALOS_OK;
     int last_n = 1;
     std::vector<size_t> pos(MB_SEQ);
+    const std::vector<int> slot0(MB_SEQ, 0);  // the main cache
     const size_t V = c->cfg.vocab_size;
     for (size_t i = 0; i < n; i += MB_SEQ) {
         const int k = (int)std::min<size_t>(MB_SEQ, n - i);
         for (int j = 0; j < k; ++j) pos[j] = pos0 + i + j;
         const bool score = c->tp > 1 && last_logits && i + k == n;
-        TRY(batch_step(c, score ? BM_SCORE : BM_PREFILL, tokens + i, pos.data(), k, i == 0));
+        TRY(batch_step(c, score ? BM_SCORE : BM_PREFILL, tokens + i, pos.data(), slot0.data(), k, i == 0));
         last_n = k;
     }
     if (last_logits && c->tp > 1) {
@@ -2137,6 +2228,7 @@ extern "C" talos_status talos_perplexity(talos_ctx* c, const uint32_t* tokens, s
     const int V = (int)c->cfg.vocab_size;
     bool first = true;
     std::vector<size_t> pos(MB_SEQ);
+    const std::vector<int> slot0(MB_SEQ, 0);  // the main cache
     // chunks of the context length, each from an empty cache (src/eval.rs:35-52)
     const size_t chunk = c->kv_ctx;
     for (size_t c0 = 0; e == cudaSuccess && st == TALOS_OK && c0 + 1 < n; c0 += chunk) {
@@ -2147,7 +2239,7 @@ extern "C" talos_status talos_perplexity(talos_ctx* c, const uint32_t* tokens, s
             for (size_t p0 = 0; e == cudaSuccess && st == TALOS_OK && p0 + 1 < len; p0 += MB_SEQ) {
                 const int k = (int)std::min<size_t>(MB_SEQ, len - 1 - p0);
                 for (int j = 0; j < k; ++j) pos[j] = p0 + j;
-                st = batch_step(c, BM_SCORE, tokens + c0 + p0, pos.data(), k, first);
+                st = batch_step(c, BM_SCORE, tokens + c0 + p0, pos.data(), slot0.data(), k, first);
                 first = false;
                 for (int j = 0; j < k && st == TALOS_OK && e == cudaSuccess; ++j)
                     e = launch_token_nll(c->blog + (size_t)j * V, V, tokens[c0 + p0 + j + 1], acc, c->stream);

@@ -33,6 +33,21 @@ The Llama-3-70B shape (the 70B benchmark model: all Q4_0, seed 3) on one GPU:
 writes the 39.7 GB GGUF file to DIR (default /dev/shm; about 95 s), loads it,
 times a 32-token prefill, the per-token decode (device greedy loop, best of
 3 x 48 tokens) and 12 batched steps of 4 sequences, then deletes the file.
+
+The 70B multi-prompt workload (32 sequences, each a 512-token uniform-random
+prompt then 128 greedy tokens) on 1, 2, 4 or 8 GPUs, one process per GPU:
+
+    python -m talos_b200.kbench --config5 --tp N [--seqs 32] [--prompt 512] [--gen 128]
+                                [--model-dir DIR] [--layers L]
+
+writes the same model file (kept when it exists; --layers L for a reduced
+depth), loads it on every rank with a context of prompt + gen positions,
+prefills each sequence's slot (talos_prefill_slot) and runs the greedy tokens
+of all sequences together (talos_generate_batch_greedy). Both phases are timed
+with CUDA events on each rank's context stream; the reported time is the max
+over ranks. Reports tok/s and, for the decode, the fraction of the measured HBM
+copy bandwidth that the bytes each rank must read per step (its weight shard
+and its KV rows) need at that rate.
 """
 from __future__ import annotations
 
@@ -64,13 +79,20 @@ def main(argv=None):
     ap.add_argument("--seed", type=int, default=7)
     ap.add_argument("--device", type=int, default=0)
     ap.add_argument("--step", action="store_true")
-    ap.add_argument("--layers", type=int, default=2)
+    ap.add_argument("--layers", type=int, default=None)  # --step / --batch: 2; --config5: 80
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--step-kernel", default="auto", choices=["auto", "fused", "layered"])
     ap.add_argument("--batch", type=int, default=0)
     ap.add_argument("--llama70b", action="store_true")
     ap.add_argument("--model-dir", default="/dev/shm")
+    ap.add_argument("--config5", action="store_true")
+    ap.add_argument("--tp", type=int, default=1)
+    ap.add_argument("--seqs", type=int, default=32)
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--gen", type=int, default=128)
     a = ap.parse_args(argv)
+    if a.config5:
+        return config5_bench(a)
     if a.llama70b:
         return llama70b_bench(a)
     if a.batch:
@@ -159,7 +181,8 @@ def step_bench(a) -> int:
 
     build.build()
     torch.cuda.set_device(a.device)
-    shape = dataclasses.replace(synth.MISTRAL_7B, n_layer=a.layers, ctx=64)
+    layers = a.layers or 2
+    shape = dataclasses.replace(synth.MISTRAL_7B, n_layer=layers, ctx=64)
     t0 = time.time()
     data = synth.llama_bytes(shape, 1, wtype=gguf.Q4_0, out_type=gguf.Q6_K)
     gen_s = time.time() - t0
@@ -178,8 +201,8 @@ def step_bench(a) -> int:
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / a.steps
     E, F, V = shape.n_embd, shape.n_ff, shape.vocab
-    wbytes = a.layers * (2 * E * E + 2 * shape.kv_dim * E + 3 * E * F) * 18 // 32 + V * E * 210 // 256
-    out = {"kernel": "decode_step", "step_kernel": m.ctx.step_kernel(), "layers": a.layers,
+    wbytes = layers * (2 * E * E + 2 * shape.kv_dim * E + 3 * E * F) * 18 // 32 + V * E * 210 // 256
+    out = {"kernel": "decode_step", "step_kernel": m.ctx.step_kernel(), "layers": layers,
            "ms_per_step": ms, "weight_bytes": wbytes, "gbs": wbytes / (ms * 1e-3) / 1e9, "model_gen_s": gen_s}
     print(json.dumps(out), flush=True)
     m.close()
@@ -193,7 +216,7 @@ def batch_bench(a) -> int:
     from talos_b200 import Model, build, gguf, synth
 
     build.build()
-    shape = dataclasses.replace(synth.MISTRAL_7B, n_layer=a.layers, ctx=1024)
+    shape = dataclasses.replace(synth.MISTRAL_7B, n_layer=a.layers or 2, ctx=1024)
     data = synth.llama_bytes(shape, 1, wtype=gguf.Q4_0, out_type=gguf.Q6_K)
     m = Model.load_bytes(data, device=a.device, max_ctx=1024)
     del data
@@ -207,7 +230,7 @@ def batch_bench(a) -> int:
         lg = m.ctx.forward_batch(toks, [p + 3 + i for p in pos])
         toks = [argmax_last(r) for r in lg]
     dt = time.perf_counter() - t0
-    out = {"kernel": "decode_batch", "batch": a.batch, "layers": a.layers, "steps": a.steps,
+    out = {"kernel": "decode_batch", "batch": a.batch, "layers": a.layers or 2, "steps": a.steps,
            "ms_per_step": dt / a.steps * 1e3, "tok_s": a.batch * a.steps / dt}
     print(json.dumps(out), flush=True)
     m.close()
@@ -260,6 +283,113 @@ def llama70b_bench(a) -> int:
     out = {"kernel": "decode_70b", "step_kernel": "fused", "model_gen_s": gen, "load_s": load,
            "prefill_32_ms": pf * 1e3, "decode_ms_per_token": best * 1e3, "decode_tok_s": 1 / best,
            "algo_gbs": algo / best / 1e9, "batch4_ms_per_step": bt * 1e3, "batch4_tok_s": 4 / bt}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+def _c5_rank(rank, tp, path, a, q_id, q_out):
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    try:
+        import torch
+
+        from talos_b200 import Model, nccl_unique_id, synth
+
+        torch.cuda.set_device(rank)
+        kw = {}
+        if tp > 1:
+            if rank == 0:
+                uid = nccl_unique_id()
+                for _ in range(tp - 1):
+                    q_id.put(uid)
+            else:
+                uid = q_id.get(timeout=600)
+            kw = dict(tp_size=tp, tp_rank=rank, nccl_id=uid)
+        m = Model.load(path, device=rank, max_ctx=a.prompt + a.gen, **kw)
+        V = m.ctx.cfg.vocab_size
+        prompts = [synth.token_ids(3 + i, a.prompt, V) for i in range(a.seqs)]
+        m.set_batch(a.seqs)
+        stream = torch.cuda.ExternalStream(m.ctx.stream(), device=torch.device("cuda", rank))
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        # warm-up: one sequence's prompt and two greedy steps (graph capture)
+        m.ctx.prefill_slot(0, prompts[0][:256], 0, want_logits=True)
+        m.ctx.generate_batch_greedy([1] * a.seqs, [256] * a.seqs, 2)
+        torch.cuda.synchronize()
+        ev[0].record(stream)
+        firsts = [argmax_last(m.ctx.prefill_slot(i, p, 0)) for i, p in enumerate(prompts)]
+        ev[1].record(stream)
+        ev[2].record(stream)
+        gen = m.ctx.generate_batch_greedy(firsts, [a.prompt] * a.seqs, a.gen)
+        ev[3].record(stream)
+        torch.cuda.synchronize()
+        q_out.put((rank, ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3]), gen[:, :4].tolist(), None))
+        m.close()
+    except Exception:
+        import traceback
+
+        q_out.put((rank, None, None, None, traceback.format_exc()))
+
+
+def config5_bench(a) -> int:
+    import dataclasses
+    import multiprocessing as mp
+    import shutil
+    import time
+
+    from talos_b200 import build, gguf, synth
+
+    build.build()
+    shape = dataclasses.replace(synth.LLAMA3_70B, n_layer=a.layers or 80)
+    path = os.path.join(a.model_dir, f"talos_kbench_llama70b_{shape.n_layer}l_q4_0.gguf")
+    gen_s = 0.0
+    if not os.path.exists(path):
+        need = 42e9 * shape.n_layer / 80
+        if shutil.disk_usage(a.model_dir).free < need:
+            print(json.dumps({"kernel": "config5", "skipped": f"under {need / 1e9:.0f} GB free in {a.model_dir}"}))
+            return 0
+        t = time.time()
+        synth.write_llama(path + ".tmp", shape, 3, wtype=gguf.Q4_0)
+        os.replace(path + ".tmp", path)
+        gen_s = time.time() - t
+    ctx = mp.get_context("spawn")
+    q_id, q_out = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_c5_rank, args=(r, a.tp, path, a, q_id, q_out)) for r in range(a.tp)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(a.tp):
+        r, pf, dc, toks, err = q_out.get(timeout=3600)
+        res[r] = (pf, dc, toks, err)
+    for p in procs:
+        p.join(timeout=120)
+    errs = {r: v[3] for r, v in res.items() if v[3]}
+    if errs:
+        print(json.dumps({"kernel": "config5", "tp": a.tp, "error": errs}))
+        return 1
+    pf = max(v[0] for v in res.values()) / 1e3
+    dc = max(v[1] for v in res.values()) / 1e3
+    agree = all(v[2] == res[0][2] for v in res.values())
+    E, F, V, L = shape.n_embd, shape.n_ff, shape.vocab, shape.n_layer
+    kv = shape.n_head_kv * (E // shape.n_head)
+    # bytes one rank reads per decode step: its Q4_0 shard of every matrix and
+    # of the output, plus its KV rows of every sequence at the step's positions
+    w_rank = (L * (2 * E * E + 2 * kv * E + 3 * E * F) + V * E) * 18 // 32 / a.tp
+    mean_pos = a.prompt + (a.gen + 1) / 2
+    kv_rank = a.seqs * mean_pos * L * (kv / a.tp) * 4 * 2
+    step_s = dc / a.gen
+    peak = None
+    try:
+        with open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                               "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["hbm_gbs"])
+    except Exception:
+        peak = 6650.0
+    gbs = (w_rank + kv_rank) / step_s / 1e9
+    out = {"kernel": "config5", "model": f"llama3-70b-shape ({L} layers) q4_0 seed 3", "tp": a.tp,
+           "seqs": a.seqs, "prompt": a.prompt, "gen": a.gen, "model_gen_s": round(gen_s, 1),
+           "prefill_s": pf, "prefill_tok_s": a.seqs * a.prompt / pf,
+           "decode_s": dc, "decode_tok_s": a.seqs * a.gen / dc, "decode_ms_per_step": step_s * 1e3,
+           "decode_bytes_per_rank_step": w_rank + kv_rank, "decode_gbs_per_rank": gbs,
+           "decode_frac_of_measured_hbm": gbs / peak, "ranks_agree": agree, "first_tokens": res[0][2][:2]}
     print(json.dumps(out), flush=True)
     return 0
 

@@ -189,6 +189,31 @@ class Context:
                                                    out.ctypes.data_as(C.POINTER(C.c_float))))
         return out
 
+    def prefill_slot(self, slot: int, tokens, pos0: int = 0, want_logits: bool = True):
+        """talos_prefill_slot: sequence ``slot``'s prompt at pos0.. into its cache
+        slot; the logits after the last token (or None)."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        out = np.empty(self.cfg.vocab_size, np.float32) if want_logits else None
+        _lib.check(_lib.load().talos_prefill_slot(self.h, int(slot), t.ctypes.data_as(C.POINTER(C.c_uint32)),
+                                                  t.size, int(pos0),
+                                                  out.ctypes.data_as(C.POINTER(C.c_float)) if out is not None
+                                                  else None))
+        return out
+
+    def generate_batch_greedy(self, tokens, positions, steps: int) -> np.ndarray:
+        """talos_generate_batch_greedy: sequences 0 .. n-1 from (tokens[i],
+        positions[i]); returns the chosen tokens as [steps, n]."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        p = np.ascontiguousarray(positions, np.uint64)
+        n = len(t)
+        if len(p) != n:
+            raise ValueError("tokens and positions differ in length")
+        out = np.empty((max(int(steps), 1), n), np.uint32)
+        _lib.check(_lib.load().talos_generate_batch_greedy(self.h, t.ctypes.data_as(C.POINTER(C.c_uint32)),
+                                                           p.ctypes.data_as(C.POINTER(C.c_size_t)), n, int(steps),
+                                                           out.ctypes.data_as(C.POINTER(C.c_uint32))))
+        return out[: int(steps)]
+
     def device_bytes(self) -> int:
         n = C.c_size_t()
         _lib.check(_lib.load().talos_ctx_device_bytes(self.h, C.byref(n)))

@@ -151,3 +151,60 @@ def test_cap_context_releases_batch_slots():
     m.ctx.set_batch(2)
     assert m.ctx.forward_batch([1, 2], [0, 0]).shape == (2, 4096)
     m.close()
+
+
+def oracle_greedy(cpu, toks, n_gen):
+    """Prompt then n_gen greedy tokens on one oracle model: (last prompt logits, tokens)."""
+    cpu.reset()
+    for p, t in enumerate(toks):
+        lg = cpu.forward(int(t), p)
+    last, gen, pos = lg, [], len(toks)
+    t = oracle.argmax(lg)
+    for _ in range(n_gen):
+        gen.append(t)
+        lg = cpu.forward(t, pos)
+        pos += 1
+        t = oracle.argmax(lg)
+    return last, gen
+
+
+@pytest.mark.parametrize("wtype", [gguf.Q4_0, gguf.Q8_0])
+def test_prefill_slot_then_batch_greedy(wtype):
+    """The multi-prompt workload: each sequence's prompt into its slot
+    (talos_prefill_slot; 150 tokens take two passes), then every sequence's
+    greedy tokens together on the device (talos_generate_batch_greedy). Tokens
+    identical to one oracle run per sequence."""
+    data = tiny_model(wtype)
+    lens = [20, 7, 150, 33, 1]
+    prompts = [prompt(n, 4096, 40 + i) for i, n in enumerate(lens)]
+    n_gen = 12
+    cpu = oracle.Model(data=data)
+    want = [oracle_greedy(cpu, p, n_gen) for p in prompts]
+    m = Model.load_bytes(data)
+    m.ctx.set_batch(len(prompts))
+    firsts = []
+    for i, p in enumerate(prompts):
+        last = m.ctx.prefill_slot(i, p, 0)
+        assert np.max(np.abs(last - want[i][0])) <= 1e-3, f"sequence {i}"
+        firsts.append(oracle.argmax(last))
+    gen = m.ctx.generate_batch_greedy(firsts, lens, n_gen)  # [step, seq]
+    for i in range(len(prompts)):
+        assert [firsts[i]] + [int(x) for x in gen[:-1, i]] == want[i][1], f"sequence {i}"
+    # a second call continues from where the first left every sequence
+    more = m.ctx.generate_batch_greedy([int(x) for x in gen[-1]], [n + n_gen for n in lens], 2)
+    for i, p in enumerate(prompts):
+        _, longer = oracle_greedy(cpu, p, n_gen + 2)
+        assert [int(x) for x in gen[-1:, i]] + [int(x) for x in more[:-1, i]] == longer[n_gen:], f"sequence {i}"
+    m.close()
+
+
+def test_prefill_slot_argument_errors():
+    m = Model.load_bytes(tiny_model(gguf.Q4_0))
+    with pytest.raises(TalosError):
+        m.ctx.prefill_slot(0, [1, 2, 3])  # no slots reserved
+    m.ctx.set_batch(2)
+    with pytest.raises(TalosError):
+        m.ctx.prefill_slot(2, [1, 2, 3])
+    with pytest.raises(TalosError):
+        m.ctx.generate_batch_greedy([1, 2], [250, 0], 10)  # positions past the 256-position context
+    m.close()

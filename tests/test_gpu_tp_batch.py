@@ -28,7 +28,7 @@ from .test_tp_cpu import TP_SHAPE
 pytestmark = [pytest.mark.gpu, pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")]
 
 TOL = 1e-3  # src/math/metal/mod.rs:527-531, 1e-3 * max(|cpu|, 1), taken as an absolute bar on O(1) logits
-SHAPE = synth.with_ctx(TP_SHAPE, 64)
+SHAPE = synth.with_ctx(TP_SHAPE, 256)
 
 
 def _model(wt):
@@ -105,7 +105,17 @@ def _job_timeout(m, rank, bar, a):
     return res
 
 
-JOBS = {"batch": _job_batch, "prefill": _job_prefill, "timeout": _job_timeout}
+def _job_greedy(m, rank, bar, a):
+    """Prompts into the sequences' slots, then batched greedy on the device."""
+    prompts = a["prompts"]
+    m.set_batch(len(prompts))
+    lasts = [m.ctx.prefill_slot(i, p, 0) for i, p in enumerate(prompts)]
+    firsts = [oracle.argmax(x) for x in lasts]
+    gen = m.ctx.generate_batch_greedy(firsts, [len(p) for p in prompts], a["G"])
+    return np.stack(lasts), firsts, gen
+
+
+JOBS = {"batch": _job_batch, "prefill": _job_prefill, "timeout": _job_timeout, "greedy": _job_greedy}
 
 
 def _rank(rank, world, job, data, args, q_id, q_out, bar):
@@ -183,8 +193,9 @@ def test_tp2_batched_decode_matches_oracle(wt):
 
 def test_tp2_prefill_and_perplexity_match_oracle():
     data = _model(gguf.Q4_0)
-    prompt = synth.token_ids(81, 40, SHAPE.vocab)
-    ppl_toks = synth.token_ids(82, 150, SHAPE.vocab)  # chunks of the 64-position context
+    # 150 positions: a prefill step without logits, then one with them
+    prompt = synth.token_ids(81, 150, SHAPE.vocab)
+    ppl_toks = synth.token_ids(82, 300, SHAPE.vocab)  # chunks of the 256-position context
     ranks = run_job("prefill", data, {"prompt": prompt, "ppl_tokens": ppl_toks})
     cpu = oracle.Model(data=data)
     ref = _oracle_seq(cpu, prompt)[-1]
@@ -195,7 +206,7 @@ def test_tp2_prefill_and_perplexity_match_oracle():
     for last, nxt, (ppl, nll, n) in ranks:
         assert np.max(np.abs(last - ref)) <= TOL
         assert np.max(np.abs(nxt - ref_next)) <= TOL
-        assert n == 147  # chunks of 64, 64, 22 tokens score 63 + 63 + 21 positions
+        assert n == 298  # chunks of 256 and 44 tokens score 255 + 43 positions
         assert abs(ppl - want_ppl) <= 1e-3 * want_ppl
     assert np.array_equal(ranks[0][0], ranks[1][0])
 
@@ -224,3 +235,23 @@ def test_tp2_withheld_step_times_out_and_resyncs():
     for r in (r0, r1):
         assert np.max(np.abs(r["t0"] - ref[0])) <= TOL
         assert np.max(np.abs(r["t1"] - ref[1])) <= TOL
+
+
+def test_tp2_prefill_slots_and_batch_greedy_match_oracle():
+    data = _model(gguf.Q4_0)
+    lens, G = [20, 3, 150, 9], 8  # 150: a fill step without logits, then one with them
+    prompts = [synth.token_ids(100 + i, n, SHAPE.vocab) for i, n in enumerate(lens)]
+    r0, r1 = run_job("greedy", data, {"prompts": prompts, "G": G})
+    assert np.array_equal(r0[0], r1[0]) and np.array_equal(r0[2], r1[2]), "ranks disagree"
+    cpu = oracle.Model(data=data)
+    lasts, firsts, gen = r0
+    for i, p in enumerate(prompts):
+        cpu.reset()
+        ref = _oracle_seq(cpu, p)[-1]
+        assert np.max(np.abs(lasts[i] - ref)) <= TOL
+        toks, t, pos = [], oracle.argmax(ref), len(p)
+        for _ in range(G):
+            toks.append(t)
+            t = oracle.argmax(cpu.forward(t, pos))
+            pos += 1
+        assert [firsts[i]] + [int(x) for x in gen[:-1, i]] == toks, f"sequence {i}"
