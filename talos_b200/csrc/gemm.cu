@@ -22,8 +22,9 @@
 //    (~22 bits); the epilogue multiplies by 2^e_t. No input overflows f16 and
 //    small inputs keep their relative precision.
 //  * Per K step of 16: D[:, 0:2N] += A_hi x [x_hi | x_lo] and
-//    D[:, 0:N] += A_lo x x_hi (the A_lo x_lo term is below f32 rounding); the
-//    result is D[:, t] + D[:, N + t].
+//    D[:, 0:N] += A_lo x x_hi (the A_lo x_lo term is below f32 rounding; up to
+//    64 columns this term has columns 2N .. 3N of its own); the result is
+//    D[:, t] + D[:, N + t] (+ D[:, 2N + t]).
 //
 // Structure: one CTA per SM (persistent over work units = 128-row tile x token
 // tile x K slice), warp-specialised:
@@ -41,11 +42,15 @@
 //  * warp 5: activation producer. One tiled TMA copy per stage
 //    (cp.async.bulk.tensor.3d, no multicast) of the formatted [x_hi; x_lo]
 //    planes into the B stage.
-//  * warp 6: allocates TMEM (two accumulators of 2N f32 columns), one thread
-//    issues tcgen05.mma.cta_group::1.kind::f16 (M 128, N 2N / N, K 16) and
-//    tcgen05.commit to the stage's "empty" and the accumulator's "full" barrier.
-//  * warps 7-14: dequantizers. Raw slot -> A_hi / A_lo stage tiles (f16),
-//    fence.proxy.async, arrive.
+//  * warp 6: allocates TMEM (two accumulators: double buffering across units);
+//    its lane 0 issues tcgen05.mma.cta_group::1.kind::f16 (M 128, K 16) of A_hi
+//    against [x_hi | x_lo] (N 2NT) and tcgen05.commit to the stage's "empty" and
+//    the accumulator's "full" barrier. Up to 64 token columns warp 7 issues the
+//    A_lo x x_hi MMAs (N NT) into a third part of the accumulator (two issuers:
+//    one thread's issue costs more than a narrow MMA takes); at 128 columns warp
+//    6 issues both into the same 2N columns.
+//  * warps 8-15: dequantizers. Raw slot -> A_hi / A_lo stage tiles (f16, one
+//    stmatrix per four 8 x 8 blocks), fence.proxy.async, arrive.
 // A and B stage tiles are K-major with the 128-byte swizzle of tcgen05 (and of
 // TMA): one 128-byte row per matrix row (64 inputs of f16), its 16-byte chunk c
 // stored at chunk c ^ (row % 8), 8-row atoms 1024 bytes apart.
@@ -66,7 +71,7 @@ constexpr int GM_RK = 128;   // K per raw weight slot (two stages)
 #define TALOS_GM_NDQ 8
 #endif
 constexpr int GM_NDQ = TALOS_GM_NDQ;  // dequantizer warps (8 or 16: each takes 16 / GM_NDQ row groups per stage)
-constexpr int GM_WP = 4, GM_XP = 5, GM_MMA = 6, GM_DQ0 = 7;
+constexpr int GM_WP = 4, GM_XP = 5, GM_MMA = 6, GM_MMA2 = 7, GM_DQ0 = 8;
 constexpr int GM_THREADS = (GM_DQ0 + GM_NDQ) * 32;
 constexpr int GM_SMEM = 220 * 1024;
 constexpr int GM_MAXRAW = 8;
@@ -119,7 +124,13 @@ struct GmCfg {
     static constexpr int NRAW_FIT = (GM_SMEM - FIXED) / RAW;
     static constexpr int NRAW = NRAW_FIT > GM_MAXRAW ? GM_MAXRAW : NRAW_FIT;
     static constexpr int SMEM = FIXED + NRAW * RAW;
-    static constexpr int TCOLS = 4 * NT;  // two accumulators of 2N columns
+    // Up to 64 columns the A_lo MMAs have an issuer (warp GM_MMA2) and an
+    // accumulator of their own: D = [A_hi x (x_hi | x_lo) : 2N][A_lo x x_hi : N].
+    // At 128 columns (tensor-bound) one thread issues both into 2N columns.
+    static constexpr int ISS = NT <= 64 ? 2 : 1;
+    static constexpr int ACCW = ISS == 2 ? 3 * NT : 2 * NT;  // TMEM columns of one accumulator
+    static constexpr int TCOLS = 2 * ACCW <= 128 ? 128 : (2 * ACCW <= 256 ? 256 : 512);  // two accumulators
+    static_assert(2 * ACCW <= 512, "TMEM");
     static_assert(NRAW >= 2, "raw ring too small");
 };
 
@@ -221,29 +232,33 @@ __device__ __forceinline__ int gm_wexp(const GemmSeg& sg) {
 //
 // Thread (lr, t) = (lane / 4, lane % 4) of a group task holds, per 32-element
 // block (16 for Q6_K), the k pairs {2t, 2t+1}, {2t+8, 2t+9}, {16+2t, 17+2t},
-// {24+2t, 25+2t} (the packed lane records); each pair is one 4-byte f16x2 word
-// of the row's 16-byte chunk kg (the pair's 8-k group): swizzled position
-// row * 128 + (kg ^ row % 8) * 16 + 4 t. A warp's 32 words of one kg fill 32
-// distinct banks.
-
-__device__ __forceinline__ void gm_put(uint8_t* A, int kg, int row, int t, __half2 v) {
-    uint32_t u = *reinterpret_cast<uint32_t*>(&v);
-    *(uint32_t*)(A + row * 128 + ((kg ^ (row & 7)) << 4) + t * 4) = u;
+// {24+2t, 25+2t} (the packed lane records): for each 8-k group kg of the block,
+// row lr's columns 2t, 2t+1 of an 8 x 8 f16 matrix, the fragment layout of
+// stmatrix. One stmatrix.x4 per four groups writes the warp's 8 rows; lane L
+// gives the address of row L % 8 of group kg0 + L / 8, in the swizzled layout
+// (the row's 16-byte chunk kg at row * 128 + (kg ^ row % 8) * 16).
+__device__ __forceinline__ void gm_stsm4(uint8_t* A, int gi, int kg0, int lane, uint32_t r0, uint32_t r1,
+                                         uint32_t r2, uint32_t r3) {
+    const int m = lane >> 3, r = lane & 7;
+    const uint32_t addr = smem_u32(A + (gi * 8 + r) * 128 + (((kg0 + m) ^ r) << 4));
+    asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r0), "r"(r1),
+                 "r"(r2), "r"(r3)
+                 : "memory");
 }
-__device__ __forceinline__ void gm_split_store(uint8_t* Ahi, uint8_t* Alo, int kg, int row, int t, __half2 q,
-                                               __half2 d) {
-    const __half2 hi = __hmul2(q, d);
-    const __half2 lo = __hfma2(q, d, __hneg2(hi));  // exact remainder (see the file comment)
-    gm_put(Ahi, kg, row, t, hi);
-    gm_put(Alo, kg, row, t, lo);
+// (q - z) d = hi + lo exactly (see the file comment), as f16x2 words.
+__device__ __forceinline__ void gm_split(__half2 q, __half2 d, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __hmul2(q, d);
+    const __half2 l = __hfma2(q, d, __hneg2(h));
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
 }
-__device__ __forceinline__ void gm_split_store_f32(uint8_t* Ahi, uint8_t* Alo, int kg, int row, int t, float v0,
-                                                   float v1) {
-    const __half2 hi = __floats2half2_rn(v0, v1);
-    const float2 hf = __half22float2(hi);
-    const __half2 lo = __floats2half2_rn(v0 - hf.x, v1 - hf.y);
-    gm_put(Ahi, kg, row, t, hi);
-    gm_put(Alo, kg, row, t, lo);
+// Two f32 values -> f16x2 hi and the f16x2 of their remainders.
+__device__ __forceinline__ void gm_split_f32(float v0, float v1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(v0, v1);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(v0 - hf.x, v1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 // Q8_0 bytes (two int8 in byte positions sel) -> f16x2 exactly: 1024 + (q + 128) - 1152.
 __device__ __forceinline__ __half2 q8_pair(uint32_t w, uint32_t sel) {
@@ -257,7 +272,7 @@ __device__ __forceinline__ __half2 q8_pair(uint32_t w, uint32_t sel) {
 template <int TYPE>
 __device__ __forceinline__ void gm_dequant(const uint8_t* lrec, const uint8_t* scs, uint8_t* Ahi, uint8_t* Alo, int gi,
                                            int h, int lane, float wsc) {
-    const int lr = lane >> 2, t = lane & 3, row = gi * 8 + lr;
+    const int lr = lane >> 2;
     if (TYPE == GT_Q4_0) {
         const uint4 rec = *(const uint4*)(lrec + lane * 16);
         const uint32_t sc2 = *(const uint32_t*)(scs + lr * 8 + h * 4);
@@ -267,15 +282,12 @@ __device__ __forceinline__ void gm_dequant(const uint8_t* lrec, const uint8_t* s
             const float d = __half2float(__ushort_as_half((unsigned short)(sc2 >> (16 * jj)))) * wsc;
             const __half2 dd = __float2half2_rn(d);
             const uint32_t w = wv[jj];
-            uint32_t q;
-            q = q4_lo_f16x2(w);
-            gm_split_store(Ahi, Alo, 4 * jj + 0, row, t, *reinterpret_cast<__half2*>(&q), dd);
-            q = q4_hi_f16x2(w);
-            gm_split_store(Ahi, Alo, 4 * jj + 1, row, t, *reinterpret_cast<__half2*>(&q), dd);
-            q = q4_lo_f16x2(w >> 8);
-            gm_split_store(Ahi, Alo, 4 * jj + 2, row, t, *reinterpret_cast<__half2*>(&q), dd);
-            q = q4_hi_f16x2(w >> 8);
-            gm_split_store(Ahi, Alo, 4 * jj + 3, row, t, *reinterpret_cast<__half2*>(&q), dd);
+            uint32_t q[4] = {q4_lo_f16x2(w), q4_hi_f16x2(w), q4_lo_f16x2(w >> 8), q4_hi_f16x2(w >> 8)};
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) gm_split(*reinterpret_cast<__half2*>(&q[m]), dd, hi[m], lo[m]);
+            gm_stsm4(Ahi, gi, 4 * jj, lane, hi[0], hi[1], hi[2], hi[3]);
+            gm_stsm4(Alo, gi, 4 * jj, lane, lo[0], lo[1], lo[2], lo[3]);
         }
     } else if (TYPE == GT_Q8_0) {
         const uint4 rec = *(const uint4*)(lrec + lane * 32 + h * 16);
@@ -286,10 +298,13 @@ __device__ __forceinline__ void gm_dequant(const uint8_t* lrec, const uint8_t* s
             const float d = __half2float(__ushort_as_half((unsigned short)(sc2 >> (16 * jj)))) * wsc;
             const __half2 dd = __float2half2_rn(d);
             // bytes of block jj: {2t, 2t+1, 2t+8, 2t+9} then {16+2t, 17+2t, 24+2t, 25+2t}
-            gm_split_store(Ahi, Alo, 4 * jj + 0, row, t, q8_pair(wv[2 * jj], 0x4140), dd);
-            gm_split_store(Ahi, Alo, 4 * jj + 1, row, t, q8_pair(wv[2 * jj], 0x4342), dd);
-            gm_split_store(Ahi, Alo, 4 * jj + 2, row, t, q8_pair(wv[2 * jj + 1], 0x4140), dd);
-            gm_split_store(Ahi, Alo, 4 * jj + 3, row, t, q8_pair(wv[2 * jj + 1], 0x4342), dd);
+            uint32_t hi[4], lo[4];
+            gm_split(q8_pair(wv[2 * jj], 0x4140), dd, hi[0], lo[0]);
+            gm_split(q8_pair(wv[2 * jj], 0x4342), dd, hi[1], lo[1]);
+            gm_split(q8_pair(wv[2 * jj + 1], 0x4140), dd, hi[2], lo[2]);
+            gm_split(q8_pair(wv[2 * jj + 1], 0x4342), dd, hi[3], lo[3]);
+            gm_stsm4(Ahi, gi, 4 * jj, lane, hi[0], hi[1], hi[2], hi[3]);
+            gm_stsm4(Alo, gi, 4 * jj, lane, lo[0], lo[1], lo[2], lo[3]);
         }
     }
 }
@@ -297,11 +312,12 @@ __device__ __forceinline__ void gm_dequant(const uint8_t* lrec, const uint8_t* s
 // Q6_K needs the sub-block position inside its 1024-input chunk for the scales.
 __device__ __forceinline__ void gm_dequant_q6(const uint8_t* lrec, const uint8_t* scs, uint8_t* Ahi, uint8_t* Alo,
                                               int gi, int h, int lane, float wsc, int step0) {
-    const int lr = lane >> 2, t = lane & 3, row = gi * 8 + lr;
+    const int lr = lane >> 2;
     const uint4 rec = *(const uint4*)(lrec + h * 512 + lane * 16);
     const uint32_t wv[4] = {rec.x, rec.y, rec.z, rec.w};
     const int8_t* scp = (const int8_t*)scs + lr * 64;
     const uint16_t* dp = (const uint16_t*)(scs + 512) + lr * 4;
+    uint32_t hi[8], lo[8];  // 8-k groups 2s (k 2t, 2t+1 of sub-block s) and 2s+1 (k 2t+8, 2t+9)
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
         const int step = step0 + h * 4 + s;  // sub-block index in the chunk, 0..63
@@ -312,9 +328,13 @@ __device__ __forceinline__ void gm_dequant_q6(const uint8_t* lrec, const uint8_t
         const float v1 = __fmul_rn(dsc, (float)((int)((w >> 8) & 0xFF) - 32)) * wsc;
         const float v2 = __fmul_rn(dsc, (float)((int)((w >> 16) & 0xFF) - 32)) * wsc;
         const float v3 = __fmul_rn(dsc, (float)((int)(w >> 24) - 32)) * wsc;
-        gm_split_store_f32(Ahi, Alo, 2 * s, row, t, v0, v1);      // k 2t, 2t+1 of the sub-block
-        gm_split_store_f32(Ahi, Alo, 2 * s + 1, row, t, v2, v3);  // k 2t+8, 2t+9
+        gm_split_f32(v0, v1, hi[2 * s], lo[2 * s]);
+        gm_split_f32(v2, v3, hi[2 * s + 1], lo[2 * s + 1]);
     }
+    gm_stsm4(Ahi, gi, 0, lane, hi[0], hi[1], hi[2], hi[3]);
+    gm_stsm4(Ahi, gi, 4, lane, hi[4], hi[5], hi[6], hi[7]);
+    gm_stsm4(Alo, gi, 0, lane, lo[0], lo[1], lo[2], lo[3]);
+    gm_stsm4(Alo, gi, 4, lane, lo[4], lo[5], lo[6], lo[7]);
 }
 
 // ---------------------------------------------------------------- epilogue
@@ -420,17 +440,17 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         for (int i = 0; i < C::NS; ++i) {
             mbar_init(&a_full[i], GM_NDQ);
             mbar_init(&b_full[i], 1);
-            mbar_init(&st_empty[i], 1);
+            mbar_init(&st_empty[i], C::ISS);
         }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_full[i], C::ISS);
             mbar_init(&acc_empty[i], 4);
         }
-        mbar_init(done, 1);
+        mbar_init(done, C::ISS);
         s_flag[0] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == GM_MMA) {  // TMEM: two accumulators of 2 NT f32 columns
+    if (warp == GM_MMA) {  // TMEM: two accumulators of ACCW f32 columns
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"((uint32_t)C::TCOLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -521,9 +541,16 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             const uint32_t first = si > (uint32_t)C::NS ? si - C::NS : 0;
             for (uint32_t j = first; j < si; ++j) mbar_wait(&b_full[j % C::NS], (j / C::NS) & 1);
         }
-    } else if (warp == GM_MMA) {
-        // ---------------- MMA issuer
-        if (lane == 0) {
+    } else if (warp == GM_MMA || warp == GM_MMA2) {
+        // ---------------- MMA issuers. One thread's tcgen05.mma costs it ~55 cycles,
+        // more than a 128 x 64 x 16 MMA takes the tensor core, so below 128 columns
+        // the A_hi MMAs (warp GM_MMA) and the A_lo MMAs (warp GM_MMA2) have an
+        // issuer each, into separate accumulators. Descriptors are formed once per
+        // stage: a K step of 16 inputs is +32 bytes = +2 in the start-address field.
+        const bool lo_iss = warp == GM_MMA2;
+        if (lane == 0 && (C::ISS == 2 || !lo_iss)) {
+            const uint32_t idesc = lo_iss ? umma_idesc(NT) : umma_idesc(2 * NT);
+            const uint32_t col = lo_iss ? 2 * NT : 0;
             uint32_t si = 0, nu = 0;
             for (int u = blockIdx.x; u < nunits && !stop(); u += gridDim.x, ++nu) {
                 const GmUnit U = gm_unit(a, u, ntt);
@@ -533,8 +560,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d = tmem + ab * (2 * NT);
-                bool first = true;
+                const uint32_t d = tmem + ab * C::ACCW + col;
+                uint32_t acc = 0u;
                 bool ok = true;
                 for (int rs = U.r0; rs < U.r1 && ok; ++rs)
                     for (int h = 0; h < 2; ++h, ++si) {
@@ -545,16 +572,24 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                             break;
                         }
                         tc_fence_after();
-                        const uint32_t ah = smem_u32(sA + s * C::A_BYTES), al = ah + GM_BM * GM_BK * 2;
-                        const uint32_t bb = smem_u32(sB + s * C::B_BYTES);
+                        const uint32_t ah = smem_u32(sA + s * C::A_BYTES);
+                        const uint64_t bd = umma_desc_sw128(smem_u32(sB + s * C::B_BYTES));
+                        if (C::ISS == 2) {
+                            const uint64_t ad = umma_desc_sw128(lo_iss ? ah + GM_BM * GM_BK * 2 : ah);
 #pragma unroll
-                        for (int kk = 0; kk < GM_BK / 16; ++kk) {
-                            const uint64_t bd = umma_desc_sw128(bb + kk * 32);
-                            umma_f16(d, umma_desc_sw128(ah + kk * 32), bd, umma_idesc(2 * NT),
-                                     (first && kk == 0) ? 0u : 1u);
-                            umma_f16(d, umma_desc_sw128(al + kk * 32), bd, umma_idesc(NT), 1u);
+                            for (int kk = 0; kk < GM_BK / 16; ++kk) {
+                                umma_f16(d, ad + 2 * kk, bd + 2 * kk, idesc, acc);
+                                acc = 1u;
+                            }
+                        } else {
+                            const uint64_t hd = umma_desc_sw128(ah), ld = umma_desc_sw128(ah + GM_BM * GM_BK * 2);
+#pragma unroll
+                            for (int kk = 0; kk < GM_BK / 16; ++kk) {
+                                umma_f16(d, hd + 2 * kk, bd + 2 * kk, idesc, acc);
+                                umma_f16(d, ld + 2 * kk, bd + 2 * kk, umma_idesc(NT), 1u);
+                                acc = 1u;
+                            }
                         }
-                        first = false;
                         umma_commit(&st_empty[s]);  // the stage's A and B are free once these MMAs finish
                     }
                 if (!ok) {
@@ -563,9 +598,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                 }
                 umma_commit(&acc_full[ab]);
             }
-            // every MMA issued has finished before TMEM is freed
+            // every MMA issued has finished before TMEM is freed (by warp GM_MMA)
             umma_commit(done);
-            mbar_wait(done, 0);
+            if (!lo_iss) mbar_wait(done, 0);
         }
         __syncwarp();
     } else if (warp >= GM_DQ0) {
@@ -650,7 +685,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                 break;
             }
             tc_fence_after();
-            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * (2 * NT);
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * C::ACCW;
             float* part = a.S > 1 ? a.ws + ((size_t)(U.tile * a.S + U.ks) * NT) * GM_BM : nullptr;
 #pragma unroll 1
             for (int c = 0; c < NT; c += 16) {
@@ -660,6 +695,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                 tmem_wait_ld();
 #pragma unroll
                 for (int j = 0; j < 16; ++j) vh[j] += vl[j];
+                if (C::ISS == 2) {  // + A_lo x x_hi
+                    tmem_ld16(tbase + 2 * NT + c, vl);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) vh[j] += vl[j];
+                }
                 if (part) {
 #pragma unroll
                     for (int j = 0; j < 16; ++j) part[(size_t)(c + j) * GM_BM + r] = vh[j];
