@@ -184,6 +184,19 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+// Bounded wait of a role that mostly waits (producers, MMA issuers, epilogue):
+// it sleeps between polls so that its sub-partition's issue slots go to the
+// dequantizer warps beside it (128-column tiles: 94 -> 85 us on 28672 x 4096).
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        __nanosleep(64);
+        if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > 2000000000ull) return false;
+    }
+}
+
 // ---------------------------------------------------------------- work units
 
 struct GmUnit {
@@ -483,7 +496,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                 uint8_t* dst = sR + slot * C::RAW;
                 bool w_ok = true;
                 if (lane == 0) {
-                    w_ok = mbar_wait(&raw_empty[slot], ((ri / C::NRAW) & 1) ^ 1);
+                    w_ok = mbar_wait_idle(&raw_empty[slot], ((ri / C::NRAW) & 1) ^ 1);
                     if (w_ok) {
                         mbar_expect_tx(&raw_full[slot], bytes);
                         if (sg.wmap) {  // out-of-range groups of the last tile read as zeros
@@ -526,7 +539,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                     const int s = si % C::NS;
                     bool w_ok = true;
                     if (lane == 0) {
-                        w_ok = mbar_wait(&st_empty[s], ((si / C::NS) & 1) ^ 1);
+                        w_ok = mbar_wait_idle(&st_empty[s], ((si / C::NS) & 1) ^ 1);
                         if (w_ok) mbar_expect_tx(&b_full[s], C::B_BYTES);
                     }
                     if (!__shfl_sync(0xffffffffu, (int)w_ok, 0)) {
@@ -555,7 +568,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             for (int u = blockIdx.x; u < nunits && !stop(); u += gridDim.x, ++nu) {
                 const GmUnit U = gm_unit(a, u, ntt);
                 const int ab = nu & 1;
-                if (!mbar_wait(&acc_empty[ab], ((nu >> 1) & 1) ^ 1)) {
+                if (!mbar_wait_idle(&acc_empty[ab], ((nu >> 1) & 1) ^ 1)) {
                     fail();
                     break;
                 }
@@ -567,7 +580,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                     for (int h = 0; h < 2; ++h, ++si) {
                         const int s = si % C::NS;
                         const uint32_t par = (si / C::NS) & 1;
-                        if (!mbar_wait(&a_full[s], par) || !mbar_wait(&b_full[s], par)) {
+                        if (!mbar_wait_idle(&a_full[s], par) || !mbar_wait_idle(&b_full[s], par)) {
                             ok = false;
                             break;
                         }
@@ -680,7 +693,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                 }
                 __syncwarp();
             }
-            if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[ab], (nu >> 1) & 1))) {
+            if (!__all_sync(0xffffffffu, mbar_wait_idle(&acc_full[ab], (nu >> 1) & 1))) {
                 if (lane == 0) fail();
                 break;
             }
