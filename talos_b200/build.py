@@ -31,7 +31,7 @@ NVCC_FLAGS = [
 
 # NCCL (opened with dlopen at run time) bootstraps tensor-parallel contexts;
 # only its header is needed here. The all-reduce runs inside the per-token kernel.
-LINK = ["-ldl"]
+LINK = ["-ldl", "-Xlinker", "--no-undefined"]  # a missing definition fails the build, not the first load
 
 
 def _nvcc() -> str:

@@ -529,7 +529,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         }
     } else if (warp == GM_XP) {
         // ---------------- activation producer: one TMA box per stage, the stage's
-        // 64 inputs of the tile's columns in both planes (128-byte swizzle)
+        // 64 inputs of the tile's columns in both planes (128-byte swizzle). With
+        // programmatic dependent launch the kernel may start while the kernel
+        // before it (the input's formatter) still runs: the roles that read what
+        // it writes (this one and the epilogue) wait for it here; weight copies,
+        // dequantization and TMEM set-up go ahead.
+        pdl_wait();
         uint32_t si = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < nunits && ok && !stop(); u += gridDim.x) {
@@ -672,6 +677,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         // ---------------- epilogue: warp q owns TMEM lanes / tile rows 32q .. 32q+31.
         // The four warps never wait for each other: with split-K each warp has its
         // own arrival counter per output tile (cnt[tile * 4 + q]).
+        pdl_wait();  // column scales, residual rows, caches: after the previous kernel
         const int q = warp, r = q * 32 + lane;
         float* exs = ep_xs + q * NT;
         uint32_t* eps = ep_pos + q * NT;
@@ -775,10 +781,13 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 // x[t] (RMSNorm with norm_w first when set: src/math/ops.rs:5-12, (x * s) * w),
 // scaled by 2^-e_t so its largest |value| lies in [2^14, 2^15), split into
 // f16 hi / lo planes [2][Tp][ldp] (zeros past K and for t >= n); xs[t] = 2^e_t.
+// R: elements per thread (the row is read once into registers); KP <= 1024 R.
+template <int R>
 __global__ void __launch_bounds__(1024) k_xfmt_g(const float* x, int ldx, int K, int KP, int ldp, int Tp,
                                                  const float* norm_w, float eps, const BatchParams* bp, __half* planes,
                                                  float* xs) {
     __shared__ float red[32];
+    pdl_launch();  // the GEMM that reads these planes may start its weight copies now
     const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     __half* hi = planes + (size_t)t * ldp;
     __half* lo = planes + ((size_t)Tp + t) * ldp;
@@ -797,21 +806,34 @@ __global__ void __launch_bounds__(1024) k_xfmt_g(const float* x, int ldx, int K,
         __syncthreads();
         if (lane == 0) red[warp] = v;
         __syncthreads();
-        float tot = is_max ? 0.f : 0.f;
+        float tot = 0.f;
         const int nw = blockDim.x >> 5;
         for (int i = 0; i < nw; ++i) tot = is_max ? fmaxf(tot, red[i]) : tot + red[i];
         return tot;
     };
-    float s = 1.f;
+    float v[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        const int k = tid + i * 1024;
+        v[i] = k < K ? xr[k] : 0.f;
+    }
     if (norm_w) {
         float ss = 0.f;
-        for (int k = tid; k < K; k += blockDim.x) ss = fmaf(xr[k], xr[k], ss);
+#pragma unroll
+        for (int i = 0; i < R; ++i)
+            if (tid + i * 1024 < K) ss = fmaf(v[i], v[i], ss);
         const float tot = block_reduce(ss, false);
-        s = 1.0f / sqrtf(tot / (float)K + eps);
+        const float s = 1.0f / sqrtf(tot / (float)K + eps);
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            const int k = tid + i * 1024;
+            if (k < K) v[i] = __fmul_rn(__fmul_rn(v[i], s), norm_w[k]);
+        }
     }
-    auto val = [&](int k) -> float { return norm_w ? __fmul_rn(__fmul_rn(xr[k], s), norm_w[k]) : xr[k]; };
     float m = 0.f;
-    for (int k = tid; k < K; k += blockDim.x) m = fmaxf(m, fabsf(val(k)));
+#pragma unroll
+    for (int i = 0; i < R; ++i)
+        if (tid + i * 1024 < K) m = fmaxf(m, fabsf(v[i]));
     m = block_reduce(m, true);
     int e = 0;
     if (m > 0.f && isfinite(m)) {
@@ -821,11 +843,15 @@ __global__ void __launch_bounds__(1024) k_xfmt_g(const float* x, int ldx, int K,
     }
     const float down = ldexpf(1.f, -e);
     if (tid == 0) xs[t] = ldexpf(1.f, e);
-    for (int k = tid; k < KP; k += blockDim.x) {
-        const float v = k < K ? val(k) * down : 0.f;
-        const __half h = __float2half_rn(v);
-        hi[k] = h;
-        lo[k] = __float2half_rn(v - __half2float(h));
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        const int k = tid + i * 1024;
+        if (k < KP) {
+            const float y = k < K ? v[i] * down : 0.f;
+            const __half h = __float2half_rn(y);
+            hi[k] = h;
+            lo[k] = __float2half_rn(y - __half2float(h));
+        }
     }
 }
 
@@ -917,18 +943,27 @@ cudaError_t gemm_weight_maps(const PackedW& w, void* lrec_map, void* sc_map) {
 size_t gemm_map_bytes() { return sizeof(CUtensorMap); }
 
 template <int TYPE, int NT>
-static cudaError_t gemm_go(const void* map, const GemmArgs& a, int grid, cudaStream_t s) {
-    k_gemm<TYPE, NT><<<grid, GM_THREADS, GmCfg<TYPE, NT>::SMEM, s>>>(*(const CUtensorMap*)map, a);
-    return cudaGetLastError();
+static cudaError_t gemm_go(const void* map, const GemmArgs& a, int grid, cudaStream_t s, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(GM_THREADS);
+    cfg.dynamicSmemBytes = GmCfg<TYPE, NT>::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_gemm<TYPE, NT>, *(const CUtensorMap*)map, a);
 }
 
-cudaError_t launch_gemm(const void* map, const GemmArgs& a, int type, int nt, int grid, cudaStream_t s) {
+cudaError_t launch_gemm(const void* map, const GemmArgs& a, int type, int nt, int grid, cudaStream_t s, bool pdl) {
     if (a.KP % GM_RK || a.nseg < 1 || a.nseg > 3 || a.S < 1 || grid < 1) return cudaErrorInvalidValue;
 #define TALOS_GM_GO(T)                                      \
     if (type == T) {                                        \
-        if (nt == 32) return gemm_go<T, 32>(map, a, grid, s);   \
-        if (nt == 64) return gemm_go<T, 64>(map, a, grid, s);   \
-        if (nt == 128) return gemm_go<T, 128>(map, a, grid, s); \
+        if (nt == 32) return gemm_go<T, 32>(map, a, grid, s, pdl);   \
+        if (nt == 64) return gemm_go<T, 64>(map, a, grid, s, pdl);   \
+        if (nt == 128) return gemm_go<T, 128>(map, a, grid, s, pdl); \
     }
     TALOS_GM_GO(GT_Q4_0)
     TALOS_GM_GO(GT_Q8_0)
@@ -939,8 +974,16 @@ cudaError_t launch_gemm(const void* map, const GemmArgs& a, int type, int nt, in
 
 cudaError_t launch_xfmt_g(const float* x, int ldx, int K, int KP, int ldp, int Tp, int ncols, const float* norm_w,
                           float eps, const BatchParams* bp, void* planes, float* xs, cudaStream_t s) {
-    if (KP > ldp || KP < K || ncols < 1 || ncols > Tp) return cudaErrorInvalidValue;
-    k_xfmt_g<<<ncols, 1024, 0, s>>>(x, ldx, K, KP, ldp, Tp, norm_w, eps, bp, (__half*)planes, xs);
+    if (KP > ldp || KP < K || ncols < 1 || ncols > Tp || KP > 32 * 1024) return cudaErrorInvalidValue;
+    __half* pl = (__half*)planes;
+    if (KP <= 4 * 1024)
+        k_xfmt_g<4><<<ncols, 1024, 0, s>>>(x, ldx, K, KP, ldp, Tp, norm_w, eps, bp, pl, xs);
+    else if (KP <= 8 * 1024)
+        k_xfmt_g<8><<<ncols, 1024, 0, s>>>(x, ldx, K, KP, ldp, Tp, norm_w, eps, bp, pl, xs);
+    else if (KP <= 16 * 1024)
+        k_xfmt_g<16><<<ncols, 1024, 0, s>>>(x, ldx, K, KP, ldp, Tp, norm_w, eps, bp, pl, xs);
+    else
+        k_xfmt_g<32><<<ncols, 1024, 0, s>>>(x, ldx, K, KP, ldp, Tp, norm_w, eps, bp, pl, xs);
     return cudaGetLastError();
 }
 

@@ -443,8 +443,11 @@ cudaError_t launch_embed_b(const uint8_t* raw, int type, int cols, int vocab, co
 // in rounds of 4 (all K/V loads of a round in flight), keeps an online softmax
 // (max m, sum l, unnormalised o; lane = 4 dims), and the warps merge in shared
 // memory: out = o / l (src/math/ops.rs:15-25 applied to the merged sums).
+#ifndef TALOS_ATB_MINB
+#define TALOS_ATB_MINB 4
+#endif
 constexpr int ATB_WARPS = 8, ATB_ROUND = 4;
-__global__ void __launch_bounds__(ATB_WARPS * 32) k_attention_b(const float* q, int ldq, const float* kc,
+__global__ void __launch_bounds__(ATB_WARPS * 32, TALOS_ATB_MINB) k_attention_b(const float* q, int ldq, const float* kc,
                                                                 const float* vc, size_t seq_stride, int kv_dim,
                                                                 int n_head, int n_kv, int hd, float* out, int ldo,
                                                                 const BatchParams* bp) {

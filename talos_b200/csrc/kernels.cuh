@@ -150,7 +150,10 @@ size_t gemm_map_bytes();
 // weight through which the GEMM copies its lane records and scales.
 cudaError_t gemm_weight_maps(const PackedW& w, void* lrec_map, void* sc_map);
 // nt: token columns per tile (32, 64 or 128); grid: CTAs (one per SM at most).
-cudaError_t launch_gemm(const void* map, const GemmArgs& a, int type, int nt, int grid, cudaStream_t s);
+// pdl: programmatic dependent launch (the GEMM starts its weight copies while the
+// previous kernel of the stream finishes; it reads that kernel's output only after it).
+cudaError_t launch_gemm(const void* map, const GemmArgs& a, int type, int nt, int grid, cudaStream_t s,
+                        bool pdl = false);
 cudaError_t gemm_configure();
 
 // Tensor-parallel join after an EPI_B_PEER GEMM of `grid` CTAs (instance `inst`

@@ -1857,7 +1857,7 @@ static talos_status gm(talos_ctx* c, GmInput& fi, GemmArgs a, const float* in, c
     a.cnt = c->bcnt;
     const int units = a.nrt * a.S;  // one token tile: a step holds at most nt columns
     const int grid = std::min(units, sms);
-    e = launch_gemm(c->bmaps[ntc], a, type, nt, grid, c->stream);
+    e = launch_gemm(c->bmaps[ntc], a, type, nt, grid, c->stream, true);
     if (e != cudaSuccess) return set_err(TALOS_ERR_CUDA, "GEMM launch: %s", cudaGetErrorString(e));
     if (grid_out) *grid_out = grid;
     return TALOS_OK;
