@@ -746,17 +746,26 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             if (!last) continue;
             __threadfence();
             const float* base = a.ws + ((size_t)U.tile * a.S * NT) * GM_BM;
+            // 8 columns of up to 4 slices per round trip to L2 (32 loads in flight),
+            // added in slice order
 #pragma unroll 1
             for (int c = 0; c < NT; c += 8) {
                 float v[8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) v[j] = 0.f;
-                for (int s = 0; s < a.S; ++s) {
-                    float w[8];  // the slice's 8 columns, loaded together
+                for (int s0 = 0; s0 < a.S; s0 += 4) {
+                    float w[4][8];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) w[j] = __ldcg(base + ((size_t)s * NT + c + j) * GM_BM + r);
+                    for (int k = 0; k < 4; ++k)
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) v[j] += w[j];
+                        for (int j = 0; j < 8; ++j)
+                            w[k][j] = s0 + k < a.S ? __ldcg(base + ((size_t)(s0 + k) * NT + c + j) * GM_BM + r) : 0.f;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        if (s0 + k < a.S) {
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) v[j] += w[k][j];
+                        }
                 }
                 gm_epi<8>(a, sg, U.lt, r, t0 + c, ntok, v, exs + c, eps + c, esl + c);
             }

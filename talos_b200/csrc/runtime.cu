@@ -1816,15 +1816,16 @@ static GemmSeg gseg(const DevTensor* A, float* y, int ldy, int rows, int epi) {
 }
 
 // K slices per output tile: the split that fills the SMs' waves best (a slice
-// costs a partial tile's round trip through L2, so more slices must earn it).
-static int gm_split(int nrt, int R, int sms) {
+// costs a partial tile's round trip through L2, in proportion to the tile's nt
+// columns, so more slices must earn it).
+static int gm_split(int nrt, int R, int sms, int nt) {
     int best = 1;
     double bscore = -1.0;
     for (int S = 1; S <= std::min(R, 16); ++S) {
         const long units = (long)nrt * S;
         if (S > 1 && (units > (long)GM_MAX_WAVES * sms || nrt * 4 > GM_MAX_CNT)) break;
         const long waves = (units + sms - 1) / sms;
-        const double score = (double)units / (double)(waves * sms) - 0.02 * (S - 1);
+        const double score = (double)units / (double)(waves * sms) - 0.02 * (nt / 32) * (S - 1);
         if (score > bscore + 1e-9) {
             bscore = score;
             best = S;
@@ -1850,7 +1851,7 @@ static talos_status gm(talos_ctx* c, GmInput& fi, GemmArgs a, const float* in, c
     a.KP = KP;
     a.nrt = 0;
     for (int i = 0; i < a.nseg; ++i) a.nrt += a.seg[i].ntiles;
-    a.S = gm_split(a.nrt, KP / 128, sms);
+    a.S = gm_split(a.nrt, KP / 128, sms, nt);
     a.xs = c->bxs;
     a.bp = c->bp;
     a.ws = c->bws;

@@ -19,6 +19,12 @@ profiling; its weights still exceed the L2):
 builds the Mistral-7B shape (seed 1, Q4_0, Q6_K output) with L layers, feeds a
 16-token prompt and times K device-side greedy steps.
 
+Prefill on the same model (one batched tensor-core pass per 128 positions):
+
+    python -m talos_b200.kbench --prefill N [--layers L] [--steps K]
+
+times K talos_prefill calls of an N-token prompt at position 0 (CUDA events).
+
 Batched decode on the same model:
 
     python -m talos_b200.kbench --batch N [--layers L] [--steps K]
@@ -83,6 +89,7 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--step-kernel", default="auto", choices=["auto", "fused", "layered"])
     ap.add_argument("--batch", type=int, default=0)
+    ap.add_argument("--prefill", type=int, default=0)
     ap.add_argument("--llama70b", action="store_true")
     ap.add_argument("--model-dir", default="/dev/shm")
     ap.add_argument("--config5", action="store_true")
@@ -97,6 +104,8 @@ def main(argv=None):
         return llama70b_bench(a)
     if a.batch:
         return batch_bench(a)
+    if a.prefill:
+        return prefill_bench(a)
     if a.step:
         return step_bench(a)
 
@@ -204,6 +213,40 @@ def step_bench(a) -> int:
     wbytes = layers * (2 * E * E + 2 * shape.kv_dim * E + 3 * E * F) * 18 // 32 + V * E * 210 // 256
     out = {"kernel": "decode_step", "step_kernel": m.ctx.step_kernel(), "layers": layers,
            "ms_per_step": ms, "weight_bytes": wbytes, "gbs": wbytes / (ms * 1e-3) / 1e9, "model_gen_s": gen_s}
+    print(json.dumps(out), flush=True)
+    m.close()
+    return 0
+
+
+def prefill_bench(a) -> int:
+    import dataclasses
+
+    import torch
+
+    from talos_b200 import Model, build, gguf, synth
+
+    build.build()
+    torch.cuda.set_device(a.device)
+    layers = a.layers or 2
+    shape = dataclasses.replace(synth.MISTRAL_7B, n_layer=layers, ctx=max(256, a.prefill))
+    data = synth.llama_bytes(shape, 1, wtype=gguf.Q4_0, out_type=gguf.Q6_K)
+    m = Model.load_bytes(data, device=a.device, max_ctx=max(256, a.prefill))
+    del data
+    prompt = synth.token_ids(1, a.prefill, shape.vocab)
+    m.prefill(prompt, 0)  # warm-up (graph capture)
+    stream = torch.cuda.ExternalStream(m.ctx.stream(), device=torch.device("cuda", a.device))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(a.steps):
+        m.prefill(prompt, 0)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.steps
+    E, F, V = shape.n_embd, shape.n_ff, shape.vocab
+    params = layers * (2 * E * E + 2 * shape.kv_dim * E + 3 * E * F)
+    out = {"kernel": "prefill", "layers": layers, "tokens": a.prefill, "ms": ms, "tok_s": a.prefill / (ms * 1e-3),
+           "useful_tflops_layers": 2.0 * params * a.prefill / (ms * 1e-3) / 1e12}
     print(json.dumps(out), flush=True)
     m.close()
     return 0
