@@ -446,7 +446,10 @@ cudaError_t launch_embed_b(const uint8_t* raw, int type, int cols, int vocab, co
 #ifndef TALOS_ATB_MINB
 #define TALOS_ATB_MINB 4
 #endif
-constexpr int ATB_WARPS = 8, ATB_ROUND = 4;
+#ifndef TALOS_ATB_ROUND
+#define TALOS_ATB_ROUND 4
+#endif
+constexpr int ATB_WARPS = 8, ATB_ROUND = TALOS_ATB_ROUND;
 __global__ void __launch_bounds__(ATB_WARPS * 32, TALOS_ATB_MINB) k_attention_b(const float* q, int ldq, const float* kc,
                                                                 const float* vc, size_t seq_stride, int kv_dim,
                                                                 int n_head, int n_kv, int hd, float* out, int ldo,
