@@ -40,6 +40,17 @@ writes the 39.7 GB GGUF file to DIR (default /dev/shm; about 95 s), loads it,
 times a 32-token prefill, the per-token decode (device greedy loop, best of
 3 x 48 tokens) and 12 batched steps of 4 sequences, then deletes the file.
 
+Per-phase times of the per-token kernel, on 1, 2, 4 or 8 GPUs (tensor parallel):
+
+    python -m talos_b200.kbench --phases --tp N [--layers L]
+
+loads the 7B shape with L layers (default 4) on every rank, feeds a 16-token
+prompt, and reads the kernel's device-timer stamps (talos_profile_phases) of
+three steps: per phase kind the median over CTAs, layers and steps of the
+input staging, the compute, the epilogue tail up to the CTA's arrival, and the
+wait from the arrival to the next phase's start (the grid barrier; after the
+o-proj and down phases under tensor parallelism the cross-rank barrier).
+
 The 70B multi-prompt workload (32 sequences, each a 512-token uniform-random
 prompt then 128 greedy tokens) on 1, 2, 4 or 8 GPUs, one process per GPU:
 
@@ -93,6 +104,7 @@ def main(argv=None):
     ap.add_argument("--llama70b", action="store_true")
     ap.add_argument("--model-dir", default="/dev/shm")
     ap.add_argument("--config5", action="store_true")
+    ap.add_argument("--phases", action="store_true")
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--seqs", type=int, default=32)
     ap.add_argument("--prompt", type=int, default=512)
@@ -100,6 +112,8 @@ def main(argv=None):
     a = ap.parse_args(argv)
     if a.config5:
         return config5_bench(a)
+    if a.phases:
+        return phases_bench(a)
     if a.llama70b:
         return llama70b_bench(a)
     if a.batch:
@@ -370,6 +384,93 @@ def _c5_rank(rank, tp, path, a, q_id, q_out):
         import traceback
 
         q_out.put((rank, None, None, None, traceback.format_exc()))
+
+
+PHASE_KINDS = ("qkv", "attn", "oproj", "gateup", "down")
+
+
+def _ph_rank(rank, tp, data, layers, q_id, q_out):
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    try:
+        import torch
+
+        from talos_b200 import Model, nccl_unique_id, synth
+
+        torch.cuda.set_device(rank)
+        kw = {}
+        if tp > 1:
+            if rank == 0:
+                uid = nccl_unique_id()
+                for _ in range(tp - 1):
+                    q_id.put(uid)
+            else:
+                uid = q_id.get(timeout=600)
+            kw = dict(tp_size=tp, tp_rank=rank, nccl_id=uid)
+        m = Model.load_bytes(data, device=rank, **kw)
+        V = m.ctx.cfg.vocab_size
+        toks = synth.token_ids(1, 16, V)
+        for p, t in enumerate(toks):
+            m.forward_gpu(int(t), p)
+        runs = []
+        for i in range(5):
+            st = m.ctx.profile_phases(int(toks[i]), 16 + i)
+            if i >= 2:
+                runs.append(st.astype(np.int64))
+        q_out.put((rank, runs, None))
+        m.close()
+    except Exception:
+        import traceback
+
+        q_out.put((rank, None, traceback.format_exc()))
+
+
+def phases_bench(a) -> int:
+    import dataclasses
+    import multiprocessing as mp
+
+    from talos_b200 import build, gguf, synth
+
+    build.build()
+    layers = a.layers or 4
+    shape = dataclasses.replace(synth.MISTRAL_7B, n_layer=layers, ctx=64)
+    data = synth.llama_bytes(shape, 1, wtype=gguf.Q4_0, out_type=gguf.Q6_K)
+    ctx = mp.get_context("spawn")
+    q_id, q_out = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_ph_rank, args=(r, a.tp, data, layers, q_id, q_out)) for r in range(a.tp)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(a.tp):
+        r, runs, err = q_out.get(timeout=1800)
+        res[r] = (runs, err)
+    for p in procs:
+        p.join(timeout=120)
+    errs = {r: v[1] for r, v in res.items() if v[1]}
+    if errs:
+        print(json.dumps({"kernel": "phases", "tp": a.tp, "error": errs}))
+        return 1
+    out = {"kernel": "phases", "tp": a.tp, "layers": layers, "position": "16-18", "per_layer_us": {}}
+    runs = res[0][0]
+    parts = {k: {"staging": [], "compute": [], "tail": [], "wait": []} for k in PHASE_KINDS}
+    for st in runs:  # [phase][cta][4] ns: entered, staged, computed, arrived
+        nph = st.shape[0]
+        for p in range(min(nph - 1, 5 * layers)):
+            kind = PHASE_KINDS[p % 5]
+            e, s_, c, ar = (st[p, :, k] for k in range(4))
+            nxt = st[p + 1, :, 0]
+            ok = lambda x, y: (x > 0) & (y > 0)
+            for name, x, y in (("staging", e, s_), ("compute", s_, c), ("tail", c, ar), ("wait", ar, nxt)):
+                m = ok(x, y)
+                if m.any():
+                    parts[kind][name].append(float(np.median((y - x)[m])) / 1e3)
+    total = 0.0
+    for k in PHASE_KINDS:
+        d = {n: (round(float(np.median(v)), 2) if v else None) for n, v in parts[k].items()}
+        out["per_layer_us"][k] = d
+        total += sum(x for x in d.values() if x)
+    out["layer_us"] = round(total, 1)
+    print(json.dumps(out), flush=True)
+    return 0
 
 
 def config5_bench(a) -> int:
