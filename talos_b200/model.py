@@ -374,8 +374,16 @@ class Model:
         return self.ctx.prefill(tokens, pos0)
 
     def set_batch(self, max_seqs: int):
-        """Cache slots for up to 4 sequences decoded together (0 frees them)."""
+        """Cache slots for up to 64 sequences decoded together (0 frees them)."""
         self.ctx.set_batch(max_seqs)
+
+    def prefill_slot(self, slot: int, tokens, pos0: int = 0):
+        """Sequence ``slot``'s prompt into its cache slot; the logits after its last token."""
+        return self.ctx.prefill_slot(slot, tokens, pos0)
+
+    def generate_batch_greedy(self, tokens, positions, steps: int) -> np.ndarray:
+        """Greedy tokens of sequences 0 .. n-1 decoded together on the GPU: [steps, n]."""
+        return self.ctx.generate_batch_greedy(tokens, positions, steps)
 
     def forward_batch(self, tokens, positions) -> np.ndarray:
         """One step for sequences 0 .. n-1: token i at positions[i] in slot i;
