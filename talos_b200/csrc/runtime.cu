@@ -1729,8 +1729,7 @@ static talos_status batch_alloc_shared(talos_ctx* c) {
 
 // The batched steps' buffers, with cache slots for max_seqs sequences (0: the
 // activations only, for prefill and perplexity on the main cache).
-static talos_status batch_alloc(talos_ctx* c, int max_seqs) {
-    TRY(batch_free(c));
+static talos_status batch_alloc_body(talos_ctx* c, int max_seqs) {
     const size_t E = c->cfg.n_embd, F = c->cfg.n_ff, V = c->cfg.vocab_size, L = c->cfg.n_layer;
     const size_t KPmax = ((std::max(E, F) + 127) / 128) * 128;  // largest GEMM input, rounded to 128
     const int sms = sm_count_dev(c->device);
@@ -1780,6 +1779,19 @@ static talos_status batch_alloc(talos_ctx* c, int max_seqs) {
     c->bmax = max_seqs;
     CK(cudaStreamSynchronize(c->stream));
     return TALOS_OK;
+}
+
+// batch_alloc_body, or on any failure no batch area at all (a half-made one
+// would pass chunked_ready's check); the error message is the body's.
+static talos_status batch_alloc(talos_ctx* c, int max_seqs) {
+    TRY(batch_free(c));
+    const talos_status st = batch_alloc_body(c, max_seqs);
+    if (st != TALOS_OK) {
+        const std::string msg = g_last_error;
+        batch_free(c);
+        g_last_error = msg;
+    }
+    return st;
 }
 
 extern "C" talos_status talos_ctx_set_batch(talos_ctx* c, int max_seqs) {
